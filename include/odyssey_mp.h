@@ -1,0 +1,231 @@
+/*
+ * odyssey_mp.h -- C ABI of libodyssey_mp.so, the B200 (sm_100a) mixed-
+ * precision parameter-update path of Odyssey.
+ *
+ * Plain C types only (pointers, sizes, POD structs); no CUDA or PyTorch
+ * types appear in a signature.  Every entry point returns an int status
+ * (ODY_OK or a negative ODY_ERR_*); the message of the last failure is
+ * returned by ody_last_error().  Where the reference raises an Error the
+ * message text is the reference's.
+ *
+ * Each declaration names the reference interface (HomericIntelligence/
+ * Odyssey, Mojo; file:line inside that project) it replaces.  A pointer
+ * argument of the stateless single-op functions may be host or device
+ * memory (detected per call); context buffers live in device memory owned by
+ * the context.
+ */
+#ifndef ODYSSEY_MP_H
+#define ODYSSEY_MP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ODY_ABI_VERSION 1
+
+/* ---- status codes -------------------------------------------------------- */
+#define ODY_OK 0
+#define ODY_ERR_ARG (-1)
+#define ODY_ERR_SHAPE (-2)
+#define ODY_ERR_DTYPE (-3)
+#define ODY_ERR_CUDA (-4)
+#define ODY_ERR_NCCL (-5)
+#define ODY_ERR_COMM_TIMEOUT (-6)
+#define ODY_ERR_DEVICE_BOUNDS (-7)
+#define ODY_ERR_STATE (-8)
+
+/* ---- element dtypes of gradients (DType.float32/float16/bfloat16) -------- */
+#define ODY_F32 0
+#define ODY_F16 1
+#define ODY_BF16 2
+
+/* ---- optimizers (src/odyssey/training/optimizers/{sgd,adam,adamw}.mojo) -- */
+#define ODY_SGD 0
+#define ODY_ADAM 1
+#define ODY_ADAMW 2
+
+/* ---- re-quantisation targets of the updated master weights --------------- */
+#define ODY_Q_NONE 0
+#define ODY_Q_FP16 1           /* update_model_from_master, FP16 (mixed_precision.mojo:299-354) */
+#define ODY_Q_BF16 2           /* update_model_from_master, BF16 */
+#define ODY_Q_FP8_E4M3 3       /* AnyTensor.to_fp8() (any_tensor.mojo:1946) */
+#define ODY_Q_FP8_E5M2 4       /* AnyTensor.to_bf8() (any_tensor.mojo:2165) */
+#define ODY_Q_FP8_E4M3_TENSOR 5 /* e4m3(w / s), s = amax/448 (per-tensor scale; extension) */
+#define ODY_Q_MXFP4 6          /* AnyTensor.to_mxfp4() (any_tensor.mojo:2237-2302), 17-byte blocks */
+#define ODY_Q_NVFP4 7          /* AnyTensor.to_nvfp4() (any_tensor.mojo:2329-2401), 9-byte blocks */
+#define ODY_Q_NVFP4_TENSOR 8   /* to_nvfp4(w / s_t), s_t = amax/(448*6) (per-tensor scale; extension) */
+
+/* ---- context buffers ------------------------------------------------------ */
+#define ODY_BUF_MASTER 0 /* float32 master weights */
+#define ODY_BUF_STATE1 1 /* SGD velocity / Adam(W) first moment m (float32) */
+#define ODY_BUF_STATE2 2 /* Adam(W) second moment v (float32) */
+#define ODY_BUF_GRAD 3   /* scaled gradients, in the context's gradient dtype */
+
+/*
+ * Step configuration.  Field names follow the reference: optimizer hyper-
+ * parameters are Float64 exactly as sgd_step/adam_step/adamw_step take them
+ * (sgd.mojo:27-35, adam.mojo:42-53, adamw.mojo:44-55); the scaler fields
+ * are GradientScaler.__init__'s (mixed_precision.mojo:96-122) and the TOML
+ * keys [precision.gradient_scaler] / [precision.gradient_clipping]
+ * (configs/lenet5/emnist/fp16.toml).
+ */
+typedef struct ody_config {
+  int32_t optimizer;          /* ODY_SGD / ODY_ADAM / ODY_ADAMW */
+  int32_t device;             /* CUDA device ordinal */
+  double learning_rate;
+  double momentum;            /* SGD */
+  double beta1, beta2, epsilon; /* Adam / AdamW */
+  double weight_decay;
+  int32_t use_gradient_scaler;  /* PrecisionConfig.use_gradient_scaler */
+  float initial_scale;          /* default 65536 */
+  float growth_factor;          /* default 2.0 */
+  float backoff_factor;         /* default 0.5 */
+  int64_t growth_interval;      /* default 2000 */
+  float min_scale;              /* default 1.0 */
+  float max_scale;              /* default 65536 */
+  int32_t clip_enabled;         /* clip_gradients_by_global_norm */
+  float max_norm;
+  int32_t comm_timeout_ms;      /* multi-GPU: bound on every collective wait */
+  int32_t reserved[7];
+} ody_config;
+
+/* What one step did (PrecisionConfig.step bookkeeping,
+ * precision_config.mojo:455-473, plus the clip of gradient_clipping.mojo:313-368). */
+typedef struct ody_step_result {
+  int32_t found_inf;      /* any non-finite unscaled gradient (all ranks) */
+  int32_t skipped;        /* update skipped (== found_inf) */
+  int32_t clipped;        /* global norm exceeded max_norm */
+  int32_t reserved0;
+  int64_t nonfinite_count;
+  double sumsq;           /* sum of float32 squares of the unscaled gradients */
+  float grad_norm;        /* Float32(sqrt(sumsq)) (gradient_clipping.mojo:310) */
+  float clip_coef;        /* 1.0 when not clipped */
+  float scale_used;       /* loss scale this step's gradients were unscaled by */
+  float scale_next;       /* loss scale after step()/backoff() */
+  int64_t step_count;     /* PrecisionConfig._step_count */
+  int64_t overflow_count; /* PrecisionConfig._overflow_count */
+  int64_t scaler_num_steps;   /* GradientScaler._num_steps */
+  int64_t steps_since_growth; /* GradientScaler._steps_since_growth */
+} ody_step_result;
+
+typedef struct ody_ctx ody_ctx;
+
+/* ---- library ------------------------------------------------------------- */
+int ody_abi_version(void);
+/* Message of the last failure on this thread (ctx may be NULL). */
+const char* ody_last_error(const ody_ctx* ctx);
+/* Fills the reference defaults: GradientScaler() (mixed_precision.mojo:
+ * 96-122), AdamW betas/eps (adamw.mojo:44-55), clip disabled. */
+void ody_config_default(ody_config* cfg);
+/* Bytes of the quantised form of n elements (tensor_dtype_conv.mojo:281-366). */
+int64_t ody_quant_bytes(int32_t kind, int64_t n);
+
+/* ---- the fused step context (replaces PrecisionConfig + GradientScaler +
+ *      init_*_state + the per-tensor optimizer/requant call sequence of
+ *      examples/lenet_emnist/run_train.mojo:219-306 and
+ *      examples/mixed_precision_training.mojo:132-216) ----------------------- */
+int ody_ctx_create(ody_ctx** out, const ody_config* cfg);
+/* Registers one parameter tensor (in model order); *index_out receives its
+ * global index.  All tensors of a context share one gradient dtype.
+ * Replaces init_optimizer_state (dispatch.mojo:227-313): states start at 0. */
+int ody_ctx_add_tensor(ody_ctx* ctx, int64_t numel, int32_t grad_dtype, int32_t quant_kind,
+                       int32_t* index_out);
+/* Freezes the tensor list, assigns whole tensors to ranks (ZeRO-1 flat
+ * shard; see ody_plan_shards), allocates this rank's device arenas and, for
+ * world_size > 1, joins the NCCL communicator identified by the 128-byte
+ * nccl_unique_id (from ody_nccl_unique_id on rank 0). */
+int ody_ctx_finalize(ody_ctx* ctx, int32_t world_size, int32_t rank, const void* nccl_unique_id);
+/* 128-byte NCCL unique id for ody_ctx_finalize (call on one rank, share it). */
+int ody_nccl_unique_id(void* out128);
+/* Host-only: contiguous balanced assignment of whole tensors to ranks (by
+ * element count).  owner_out[i] = rank owning tensor i. */
+int ody_plan_shards(const int64_t* numels, int32_t ntensors, int32_t world_size, int32_t* owner_out);
+int ody_ctx_tensor_owner(const ody_ctx* ctx, int32_t index, int32_t* rank_out);
+int ody_ctx_num_tensors(const ody_ctx* ctx, int32_t* n_out);
+
+/* Copy one tensor's buffer in / out (host or device memory; bytes must be
+ * numel * element size).  Synchronous. */
+int ody_upload(ody_ctx* ctx, int32_t which, int32_t index, const void* src, size_t bytes);
+int ody_download(ody_ctx* ctx, int32_t which, int32_t index, void* dst, size_t bytes);
+/* As ody_upload, enqueued on the context stream without waiting; the source
+ * must stay valid (and, for overlap, be pinned) until the next synchronous
+ * call on the context. */
+int ody_upload_async(ody_ctx* ctx, int32_t which, int32_t index, const void* src, size_t bytes);
+/* Device address of one tensor inside a context arena (zero-copy producers). */
+int ody_ctx_device_ptr(ody_ctx* ctx, int32_t which, int32_t index, void** ptr_out);
+/* The context's CUDA stream as an opaque handle. */
+int ody_ctx_stream(ody_ctx* ctx, void** stream_out);
+
+/* One fused step: unscale -> finite check -> [skip + backoff] -> clip ->
+ * optimizer -> requant -> scaler step.  t is the optimizer timestep
+ * (>= 1 for Adam/AdamW, adam.mojo:117-118).  Synchronous; fills *out. */
+int ody_step(ody_ctx* ctx, int64_t t, ody_step_result* out);
+/* Enqueue a step without waiting; ody_step_wait returns its result. */
+int ody_step_async(ody_ctx* ctx, int64_t t);
+int ody_step_wait(ody_ctx* ctx, ody_step_result* out);
+
+/* Per-pass device timing (no reference counterpart; used for the roofline):
+ * when enabled, every step records CUDA events on the context stream around
+ * pass 1 (gradient statistics), the multi-GPU exchange, pass 2 (update) and
+ * pass 3 (per-tensor requant).  ody_ctx_pass_times waits for the stream and
+ * returns the accumulated milliseconds per pass (ms_out[4]) and the number
+ * of timed steps, then resets the accumulators. */
+int ody_ctx_set_timing(ody_ctx* ctx, int32_t enable);
+int ody_ctx_pass_times(ody_ctx* ctx, double* ms_out, int64_t* steps_out);
+
+/* Quantised weights of one tensor in the reference's byte layout, and its
+ * per-tensor scale (1.0 for kinds without one). */
+int ody_get_quant(ody_ctx* ctx, int32_t index, void* dst, size_t bytes, float* tensor_scale);
+/* GradientScaler state (mixed_precision.mojo:77-93). */
+int ody_get_scaler(ody_ctx* ctx, float* scale, int64_t* steps_since_growth, int64_t* num_steps,
+                   int64_t* step_count, int64_t* overflow_count);
+int ody_set_scaler(ody_ctx* ctx, float scale, int64_t steps_since_growth, int64_t num_steps,
+                   int64_t step_count, int64_t overflow_count);
+/* Checkpoint of this rank's master weights, states and scaler
+ * (training/checkpoint.mojo:70 CheckpointManager; the reference does not
+ * persist the scaler, test_precision_checkpoint.mojo:202-232).  buf NULL ->
+ * *bytes receives the size needed. */
+int ody_ctx_export(ody_ctx* ctx, void* buf, size_t* bytes);
+int ody_ctx_import(ody_ctx* ctx, const void* buf, size_t bytes);
+void ody_ctx_destroy(ody_ctx* ctx);
+
+/* ---- stateless single operations (host or device pointers) -------------- */
+/* GradientScaler.unscale_gradients (mixed_precision.mojo:154-182). */
+int ody_unscale(const void* grads, int32_t dtype, int64_t n, float scale, void* out);
+/* check_gradients_finite (mixed_precision.mojo:357-381); *finite = 1 if no NaN/Inf. */
+int ody_check_finite(const void* grads, int32_t dtype, int64_t n, int32_t* finite);
+/* convert_to_fp32_master (mixed_precision.mojo:240-296). */
+int ody_to_fp32(const void* x, int32_t dtype, int64_t n, float* out);
+/* clip_gradients_by_global_norm (gradient_clipping.mojo:313-368): float32
+ * gradients clipped in place; returns the pre-clip norm in *total_norm. */
+int ody_global_norm_clip(float* const* grads, const int64_t* numels, int32_t ntensors, float max_norm,
+                         float* total_norm);
+/* sgd_step (sgd.mojo:27-121); velocity/out_velocity may be NULL when momentum == 0. */
+int ody_sgd_step(const float* params, const float* grads, const float* velocity, int64_t n,
+                 double learning_rate, double momentum, double weight_decay, float* out_params,
+                 float* out_velocity);
+/* adam_step (adam.mojo:42-166). */
+int ody_adam_step(const float* params, const float* grads, const float* m, const float* v, int64_t n,
+                  int64_t t, double learning_rate, double beta1, double beta2, double epsilon,
+                  double weight_decay, float* out_params, float* out_m, float* out_v);
+/* adamw_step (adamw.mojo:44-175). */
+int ody_adamw_step(const float* params, const float* grads, const float* m, const float* v, int64_t n,
+                   int64_t t, double learning_rate, double beta1, double beta2, double epsilon,
+                   double weight_decay, float* out_params, float* out_m, float* out_v);
+/* AnyTensor.to_fp8/to_bf8/to_mxfp4/to_nvfp4 (+ per-tensor-scaled kinds,
+ * + FP16/BF16 casts): src is float32 (src_dtype ODY_F32) or bfloat16
+ * (ODY_BF16, upcast exactly first); out holds ody_quant_bytes(kind, n)
+ * bytes; *tensor_scale (may be NULL) receives the per-tensor scale. */
+int ody_quantize(int32_t kind, const void* src, int32_t src_dtype, int64_t n, void* out,
+                 float* tensor_scale);
+/* AnyTensor.from_fp8/from_bf8/from_mxfp4/from_nvfp4 (tensor_dtype_conv.mojo:
+ * 69-92,211-235,369-494): n float32 values out. */
+int ody_dequantize(int32_t kind, const void* q, int64_t n, float tensor_scale, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ODYSSEY_MP_H */

@@ -1,0 +1,1125 @@
+// ody_capi.cu -- host side of libodyssey_mp.so: the extern "C" ABI declared in
+// include/odyssey_mp.h, the step context (device arenas, chunk tables,
+// stream, NCCL communicator) and the stateless single-op entry points.
+#include <dlfcn.h>
+#include <math.h>
+#include <nccl.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <chrono>
+#include <string>
+#include <vector>
+
+#include "../../include/odyssey_mp.h"
+#include "ody_internal.h"
+
+using namespace ody;
+
+static thread_local std::string g_err;
+
+static int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define ODY_CUDA(call)                                                              \
+  do {                                                                              \
+    cudaError_t e_ = (call);                                                        \
+    if (e_ != cudaSuccess)                                                          \
+      return fail(ODY_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// NCCL, bound at run time (dlopen) so that a process which already loaded a
+// libnccl.so.2 (e.g. PyTorch's) shares it, and a single-GPU user needs none.
+// ---------------------------------------------------------------------------
+struct NcclApi {
+  void* h = nullptr;
+  ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*commInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*commAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*commGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  const char* (*getErrorString)(ncclResult_t) = nullptr;
+};
+
+static NcclApi* nccl_api(std::string& why) {
+  static NcclApi api;
+  static bool tried = false;
+  if (api.h) return &api;
+  if (tried) {
+    why = "libnccl.so.2 could not be loaded";
+    return nullptr;
+  }
+  tried = true;
+  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) {
+    why = std::string("dlopen libnccl.so.2: ") + dlerror();
+    return nullptr;
+  }
+  api.getUniqueId = (decltype(api.getUniqueId))dlsym(h, "ncclGetUniqueId");
+  api.commInitRankConfig = (decltype(api.commInitRankConfig))dlsym(h, "ncclCommInitRankConfig");
+  api.allGather = (decltype(api.allGather))dlsym(h, "ncclAllGather");
+  api.commDestroy = (decltype(api.commDestroy))dlsym(h, "ncclCommDestroy");
+  api.commAbort = (decltype(api.commAbort))dlsym(h, "ncclCommAbort");
+  api.commGetAsyncError = (decltype(api.commGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
+  api.getErrorString = (decltype(api.getErrorString))dlsym(h, "ncclGetErrorString");
+  if (!api.getUniqueId || !api.commInitRankConfig || !api.allGather || !api.commDestroy ||
+      !api.commAbort || !api.commGetAsyncError || !api.getErrorString) {
+    why = "libnccl.so.2 lacks a required symbol";
+    return nullptr;
+  }
+  api.h = h;
+  return &api;
+}
+
+// ---------------------------------------------------------------------------
+// The context.
+// ---------------------------------------------------------------------------
+struct TensorSpec {
+  int64_t numel;
+  int32_t gdt;
+  int32_t quant;
+};
+
+struct ody_ctx {
+  ody_config cfg;
+  std::vector<TensorSpec> specs;
+  bool finalized = false;
+  bool broken = false;
+  int world = 1, rank = 0;
+  int gdt = -1;
+  std::vector<int32_t> owner;      // global index -> rank
+  std::vector<int32_t> local_of;   // global index -> local index or -1
+  std::vector<TensorDesc> tdesc;   // local tensors
+  std::vector<Chunk> chunks_upd, chunks_rq;
+  int64_t n_total = 0, q_total = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t done = nullptr;
+  // device memory
+  float *master = nullptr, *s1 = nullptr, *s2 = nullptr;
+  void* grad = nullptr;
+  uint8_t* qout = nullptr;
+  float* qscale = nullptr;
+  uint32_t* amax = nullptr;
+  Chunk *d_chunks_upd = nullptr, *d_chunks_rq = nullptr;
+  TensorDesc* d_tdesc = nullptr;
+  StatsPartial* partials = nullptr;
+  unsigned* ticket = nullptr;
+  DevScaler* scaler = nullptr;
+  Decision* dec = nullptr;
+  double* local_stats = nullptr;
+  double* gathered = nullptr;
+  Decision* h_dec = nullptr;  // pinned
+  int grid_stats = 0, grid_upd = 0, grid_rq = 0;
+  bool pending = false;
+  ncclComm_t comm = nullptr;
+  std::string err;
+  // per-pass timing: a ring of event slots, 5 events per step
+  bool timing = false;
+  std::vector<cudaEvent_t> tev;
+  std::vector<int64_t> tpending;  // ring slots recorded but not yet read
+  int64_t tnext = 0, tsteps = 0;
+  double tms[4] = {0, 0, 0, 0};
+};
+
+static constexpr int kTimingRing = 64;
+
+static cudaError_t timing_collect(ody_ctx* c, int64_t slot) {
+  cudaEvent_t* e = &c->tev[(size_t)(slot % kTimingRing) * 5];
+  cudaError_t r = cudaEventSynchronize(e[4]);
+  if (r != cudaSuccess) return r;
+  for (int k = 0; k < 4; k++) {
+    float ms = 0.0f;
+    r = cudaEventElapsedTime(&ms, e[k], e[k + 1]);
+    if (r != cudaSuccess) return r;
+    c->tms[k] += ms;
+  }
+  c->tsteps += 1;
+  return cudaSuccess;
+}
+
+static int ctx_fail(ody_ctx* c, int code, const std::string& msg) {
+  g_err = msg;
+  if (c) c->err = msg;
+  return code;
+}
+
+static size_t dtype_size(int gdt) { return gdt == DT_F32 ? 4 : 2; }
+
+extern "C" int ody_abi_version(void) { return ODY_ABI_VERSION; }
+
+extern "C" const char* ody_last_error(const ody_ctx* ctx) {
+  if (ctx && !ctx->err.empty()) return ctx->err.c_str();
+  return g_err.c_str();
+}
+
+extern "C" void ody_config_default(ody_config* c) {
+  memset(c, 0, sizeof(*c));
+  c->optimizer = ODY_ADAMW;
+  c->device = 0;
+  c->learning_rate = 1e-3;
+  c->momentum = 0.0;
+  c->beta1 = 0.9;
+  c->beta2 = 0.999;
+  c->epsilon = 1e-8;
+  c->weight_decay = 0.0;
+  c->use_gradient_scaler = 1;
+  c->initial_scale = 65536.0f;
+  c->growth_factor = 2.0f;
+  c->backoff_factor = 0.5f;
+  c->growth_interval = 2000;
+  c->min_scale = 1.0f;
+  c->max_scale = 65536.0f;
+  c->clip_enabled = 0;
+  c->max_norm = 1.0f;
+  c->comm_timeout_ms = 60000;
+}
+
+extern "C" int64_t ody_quant_bytes(int32_t kind, int64_t n) {
+  if (n < 0) return -1;
+  switch (kind) {
+    case ODY_Q_NONE:
+      return 0;
+    case ODY_Q_FP16:
+    case ODY_Q_BF16:
+      return 2 * n;
+    case ODY_Q_FP8_E4M3:
+    case ODY_Q_FP8_E5M2:
+    case ODY_Q_FP8_E4M3_TENSOR:
+      return n;
+    case ODY_Q_MXFP4:
+      return ((n + 31) / 32) * 17;
+    case ODY_Q_NVFP4:
+    case ODY_Q_NVFP4_TENSOR:
+      return ((n + 15) / 16) * 9;
+    default:
+      return -1;
+  }
+}
+
+// bytes of a tensor's region in the quantised-output arena: whole tiles
+static int64_t quant_region(int kind, int64_t npad) {
+  const int64_t tiles = (npad + kTile - 1) / kTile;
+  int64_t b = 0;
+  switch (kind) {
+    case Q_FP16:
+    case Q_BF16:
+      b = 2 * npad;
+      break;
+    case Q_FP8_E4M3:
+    case Q_FP8_E5M2:
+    case Q_FP8_E4M3_TENSOR:
+      b = npad;
+      break;
+    case Q_MXFP4:
+      b = tiles * kMxTileBytes;
+      break;
+    case Q_NVFP4:
+    case Q_NVFP4_TENSOR:
+      b = tiles * kNvTileBytes;
+      break;
+    default:
+      b = 0;
+  }
+  return (b + 255) / 256 * 256;
+}
+
+extern "C" int ody_ctx_create(ody_ctx** out, const ody_config* cfg) {
+  if (!out || !cfg) return fail(ODY_ERR_ARG, "ody_ctx_create: null argument");
+  if (cfg->optimizer < ODY_SGD || cfg->optimizer > ODY_ADAMW)
+    return fail(ODY_ERR_ARG, "unknown optimizer " + std::to_string(cfg->optimizer));
+  if (cfg->clip_enabled && !(cfg->max_norm > 0.0f))
+    return fail(ODY_ERR_ARG, "max_norm must be positive, got: " + std::to_string(cfg->max_norm));
+  if (cfg->use_gradient_scaler && cfg->initial_scale == 0.0f)
+    return fail(ODY_ERR_ARG, "Cannot unscale with zero scale factor");
+  ody_ctx* c = new ody_ctx();
+  c->cfg = *cfg;
+  if (c->cfg.comm_timeout_ms <= 0) c->cfg.comm_timeout_ms = 60000;
+  *out = c;
+  return ODY_OK;
+}
+
+extern "C" int ody_ctx_add_tensor(ody_ctx* c, int64_t numel, int32_t gdt, int32_t quant, int32_t* idx) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context already finalized");
+  if (numel <= 0) return ctx_fail(c, ODY_ERR_SHAPE, "Cannot unscale empty gradient tensor");
+  if (gdt < DT_F32 || gdt > DT_BF16) return ctx_fail(c, ODY_ERR_DTYPE, "unsupported gradient dtype");
+  if (quant < ODY_Q_NONE || quant > ODY_Q_NVFP4_TENSOR)
+    return ctx_fail(c, ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(quant));
+  if (c->gdt >= 0 && c->gdt != gdt)
+    return ctx_fail(c, ODY_ERR_DTYPE, "all tensors of a context must share one gradient dtype");
+  c->gdt = gdt;
+  c->specs.push_back({numel, gdt, quant});
+  if (idx) *idx = (int32_t)c->specs.size() - 1;
+  return ODY_OK;
+}
+
+extern "C" int ody_plan_shards(const int64_t* numels, int32_t nt, int32_t world, int32_t* owner) {
+  if (!numels || !owner || nt < 0 || world < 1) return fail(ODY_ERR_ARG, "ody_plan_shards: bad argument");
+  // Contiguous groups of whole tensors; rank r takes tensors until the
+  // running total passes (r+1)/world of all elements (closest boundary).
+  double total = 0;
+  for (int i = 0; i < nt; i++) total += (double)numels[i];
+  double run = 0;
+  int r = 0;
+  for (int i = 0; i < nt; i++) {
+    // move to the next rank when this tensor's midpoint lies past the
+    // current rank's share of the running total
+    while (r < world - 1 && run + 0.5 * (double)numels[i] > total * (r + 1) / world) r++;
+    owner[i] = r;
+    run += (double)numels[i];
+  }
+  // every rank keeps at least its order; ranks may own nothing when there
+  // are fewer tensors than ranks
+  return ODY_OK;
+}
+
+extern "C" int ody_nccl_unique_id(void* out128) {
+  if (!out128) return fail(ODY_ERR_ARG, "null output");
+  std::string why;
+  NcclApi* api = nccl_api(why);
+  if (!api) return fail(ODY_ERR_NCCL, why);
+  ncclUniqueId id;
+  ncclResult_t r = api->getUniqueId(&id);
+  if (r != ncclSuccess) return fail(ODY_ERR_NCCL, std::string("ncclGetUniqueId: ") + api->getErrorString(r));
+  memcpy(out128, &id, sizeof(id));
+  return ODY_OK;
+}
+
+static int wait_nccl(ody_ctx* c, NcclApi* api, const char* what) {
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t r = api->commGetAsyncError(c->comm, &st);
+    if (r != ncclSuccess) return ctx_fail(c, ODY_ERR_NCCL, std::string(what) + ": " + api->getErrorString(r));
+    if (st == ncclSuccess) return ODY_OK;
+    if (st != ncclInProgress) {
+      api->commAbort(c->comm);
+      c->comm = nullptr;
+      c->broken = true;
+      return ctx_fail(c, ODY_ERR_NCCL, std::string(what) + ": " + api->getErrorString(st));
+    }
+    auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+    if (ms > c->cfg.comm_timeout_ms) {
+      api->commAbort(c->comm);
+      c->comm = nullptr;
+      c->broken = true;
+      return ctx_fail(c, ODY_ERR_COMM_TIMEOUT, std::string(what) + ": timed out after " +
+                                                   std::to_string(c->cfg.comm_timeout_ms) + " ms");
+    }
+  }
+}
+
+template <typename T>
+static cudaError_t dalloc(T** p, size_t bytes) {
+  return cudaMalloc((void**)p, bytes < 256 ? 256 : bytes);
+}
+
+extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const void* uid) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context already finalized");
+  if (c->specs.empty()) return ctx_fail(c, ODY_ERR_SHAPE, "no tensors registered");
+  if (world < 1 || rank < 0 || rank >= world) return ctx_fail(c, ODY_ERR_ARG, "bad world_size/rank");
+  if (world > 1 && !uid) return ctx_fail(c, ODY_ERR_ARG, "nccl_unique_id required when world_size > 1");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  c->world = world;
+  c->rank = rank;
+  const int nt = (int)c->specs.size();
+  c->owner.assign(nt, 0);
+  std::vector<int64_t> numels(nt);
+  for (int i = 0; i < nt; i++) numels[i] = c->specs[i].numel;
+  ody_plan_shards(numels.data(), nt, world, c->owner.data());
+  c->local_of.assign(nt, -1);
+  int64_t off = 0, qoff = 0;
+  for (int i = 0; i < nt; i++) {
+    if (c->owner[i] != rank) continue;
+    TensorDesc d;
+    memset(&d, 0, sizeof(d));
+    d.numel = c->specs[i].numel;
+    d.npad = (d.numel + kPad - 1) / kPad * kPad;
+    d.off = off;
+    d.qoff = qoff;
+    d.quant = c->specs[i].quant;
+    c->local_of[i] = (int32_t)c->tdesc.size();
+    const int li = (int)c->tdesc.size();
+    c->tdesc.push_back(d);
+    for (int64_t s = 0; s < d.npad; s += kChunk) {
+      Chunk ch;
+      ch.start = d.off + s;
+      ch.len = (int32_t)((d.npad - s) < kChunk ? (d.npad - s) : kChunk);
+      ch.tensor = li;
+      c->chunks_upd.push_back(ch);
+      if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR) c->chunks_rq.push_back(ch);
+    }
+    off += d.npad;
+    qoff += quant_region(d.quant, d.npad);
+  }
+  c->n_total = off;
+  c->q_total = qoff;
+  const int nl = (int)c->tdesc.size();
+  ODY_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  ODY_CUDA(cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming));
+  const size_t n = (size_t)(off > 0 ? off : kPad);
+  const bool need_s1 = c->cfg.optimizer != ODY_SGD || c->cfg.momentum > 0.0;
+  const bool need_s2 = c->cfg.optimizer != ODY_SGD;
+  ODY_CUDA(dalloc(&c->master, n * 4));
+  ODY_CUDA(cudaMemsetAsync(c->master, 0, n * 4, c->stream));
+  if (need_s1) {
+    ODY_CUDA(dalloc(&c->s1, n * 4));
+    ODY_CUDA(cudaMemsetAsync(c->s1, 0, n * 4, c->stream));
+  }
+  if (need_s2) {
+    ODY_CUDA(dalloc(&c->s2, n * 4));
+    ODY_CUDA(cudaMemsetAsync(c->s2, 0, n * 4, c->stream));
+  }
+  ODY_CUDA(dalloc(&c->grad, n * dtype_size(c->gdt)));
+  ODY_CUDA(cudaMemsetAsync(c->grad, 0, n * dtype_size(c->gdt), c->stream));
+  ODY_CUDA(dalloc(&c->qout, (size_t)qoff));
+  ODY_CUDA(cudaMemsetAsync(c->qout, 0, (size_t)(qoff > 0 ? qoff : 256), c->stream));
+  ODY_CUDA(dalloc(&c->qscale, sizeof(float) * (nl > 0 ? nl : 1)));
+  std::vector<float> ones(nl > 0 ? nl : 1, 1.0f);
+  ODY_CUDA(cudaMemcpyAsync(c->qscale, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice, c->stream));
+  ODY_CUDA(dalloc(&c->amax, sizeof(uint32_t) * (nl > 0 ? nl : 1)));
+  ODY_CUDA(cudaMemsetAsync(c->amax, 0, sizeof(uint32_t) * (nl > 0 ? nl : 1), c->stream));
+  ODY_CUDA(dalloc(&c->d_tdesc, sizeof(TensorDesc) * (nl > 0 ? nl : 1)));
+  if (nl) ODY_CUDA(cudaMemcpyAsync(c->d_tdesc, c->tdesc.data(), sizeof(TensorDesc) * nl, cudaMemcpyHostToDevice, c->stream));
+  ODY_CUDA(dalloc(&c->d_chunks_upd, sizeof(Chunk) * (c->chunks_upd.size() + 1)));
+  if (!c->chunks_upd.empty())
+    ODY_CUDA(cudaMemcpyAsync(c->d_chunks_upd, c->chunks_upd.data(), sizeof(Chunk) * c->chunks_upd.size(),
+                             cudaMemcpyHostToDevice, c->stream));
+  ODY_CUDA(dalloc(&c->d_chunks_rq, sizeof(Chunk) * (c->chunks_rq.size() + 1)));
+  if (!c->chunks_rq.empty())
+    ODY_CUDA(cudaMemcpyAsync(c->d_chunks_rq, c->chunks_rq.data(), sizeof(Chunk) * c->chunks_rq.size(),
+                             cudaMemcpyHostToDevice, c->stream));
+  c->grid_stats = stats_grid(c->cfg.device);
+  c->grid_upd = update_grid(c->gdt, c->cfg.optimizer, c->cfg.device);
+  c->grid_rq = requant_grid(c->cfg.device);
+  ODY_CUDA(dalloc(&c->partials, sizeof(StatsPartial) * c->grid_stats));
+  ODY_CUDA(dalloc(&c->ticket, sizeof(unsigned)));
+  ODY_CUDA(cudaMemsetAsync(c->ticket, 0, sizeof(unsigned), c->stream));
+  ODY_CUDA(dalloc(&c->scaler, sizeof(DevScaler)));
+  DevScaler hs;
+  memset(&hs, 0, sizeof(hs));
+  hs.scale = c->cfg.initial_scale;
+  ODY_CUDA(cudaMemcpyAsync(c->scaler, &hs, sizeof(hs), cudaMemcpyHostToDevice, c->stream));
+  ODY_CUDA(dalloc(&c->dec, sizeof(Decision)));
+  ODY_CUDA(cudaMemsetAsync(c->dec, 0, sizeof(Decision), c->stream));
+  ODY_CUDA(dalloc(&c->local_stats, sizeof(double) * 2));
+  ODY_CUDA(dalloc(&c->gathered, sizeof(double) * 2 * world));
+  ODY_CUDA(cudaMallocHost((void**)&c->h_dec, sizeof(Decision)));
+  upload_fp4_tables(c->cfg.device);
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  if (world > 1) {
+    std::string why;
+    NcclApi* api = nccl_api(why);
+    if (!api) return ctx_fail(c, ODY_ERR_NCCL, why);
+    ncclUniqueId id;
+    memcpy(&id, uid, sizeof(id));
+    ncclConfig_t conf = NCCL_CONFIG_INITIALIZER;
+    conf.blocking = 0;
+    ncclResult_t r = api->commInitRankConfig(&c->comm, world, id, rank, &conf);
+    if (r != ncclSuccess && r != ncclInProgress)
+      return ctx_fail(c, ODY_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + api->getErrorString(r));
+    int rc = wait_nccl(c, api, "ncclCommInitRankConfig");
+    if (rc != ODY_OK) return rc;
+  }
+  c->finalized = true;
+  return ODY_OK;
+}
+
+extern "C" int ody_ctx_tensor_owner(const ody_ctx* c, int32_t i, int32_t* r) {
+  if (!c || !r) return fail(ODY_ERR_ARG, "null argument");
+  if (!c->finalized) return fail(ODY_ERR_STATE, "context not finalized");
+  if (i < 0 || i >= (int)c->specs.size()) return fail(ODY_ERR_ARG, "tensor index out of range");
+  *r = c->owner[i];
+  return ODY_OK;
+}
+
+extern "C" int ody_ctx_num_tensors(const ody_ctx* c, int32_t* n) {
+  if (!c || !n) return fail(ODY_ERR_ARG, "null argument");
+  *n = (int32_t)c->specs.size();
+  return ODY_OK;
+}
+
+static int locate(ody_ctx* c, int32_t which, int32_t i, void** base, size_t* bytes) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  if (i < 0 || i >= (int)c->specs.size()) return ctx_fail(c, ODY_ERR_ARG, "tensor index out of range");
+  const int li = c->local_of[i];
+  if (li < 0)
+    return ctx_fail(c, ODY_ERR_ARG, "tensor " + std::to_string(i) + " is owned by rank " +
+                                        std::to_string(c->owner[i]));
+  const TensorDesc& d = c->tdesc[li];
+  switch (which) {
+    case ODY_BUF_MASTER:
+      *base = c->master + d.off;
+      *bytes = (size_t)d.numel * 4;
+      break;
+    case ODY_BUF_STATE1:
+      if (!c->s1) return ctx_fail(c, ODY_ERR_ARG, "optimizer has no first state buffer");
+      *base = c->s1 + d.off;
+      *bytes = (size_t)d.numel * 4;
+      break;
+    case ODY_BUF_STATE2:
+      if (!c->s2) return ctx_fail(c, ODY_ERR_ARG, "optimizer has no second state buffer");
+      *base = c->s2 + d.off;
+      *bytes = (size_t)d.numel * 4;
+      break;
+    case ODY_BUF_GRAD:
+      *base = (uint8_t*)c->grad + (size_t)d.off * dtype_size(c->gdt);
+      *bytes = (size_t)d.numel * dtype_size(c->gdt);
+      break;
+    default:
+      return ctx_fail(c, ODY_ERR_ARG, "unknown buffer " + std::to_string(which));
+  }
+  return ODY_OK;
+}
+
+static int copy_tensor(ody_ctx* c, int32_t which, int32_t i, void* dst_or_src, size_t bytes, bool up,
+                       bool sync) {
+  void* base;
+  size_t need;
+  int rc = locate(c, which, i, &base, &need);
+  if (rc) return rc;
+  if (bytes != need)
+    return ctx_fail(c, ODY_ERR_SHAPE, "size mismatch: expected " + std::to_string(need) + " bytes, got " +
+                                          std::to_string(bytes));
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  if (up)
+    ODY_CUDA(cudaMemcpyAsync(base, dst_or_src, bytes, cudaMemcpyDefault, c->stream));
+  else
+    ODY_CUDA(cudaMemcpyAsync(dst_or_src, base, bytes, cudaMemcpyDefault, c->stream));
+  if (sync) ODY_CUDA(cudaStreamSynchronize(c->stream));
+  return ODY_OK;
+}
+
+extern "C" int ody_upload(ody_ctx* c, int32_t which, int32_t i, const void* src, size_t bytes) {
+  return copy_tensor(c, which, i, const_cast<void*>(src), bytes, true, true);
+}
+extern "C" int ody_upload_async(ody_ctx* c, int32_t which, int32_t i, const void* src, size_t bytes) {
+  return copy_tensor(c, which, i, const_cast<void*>(src), bytes, true, false);
+}
+extern "C" int ody_download(ody_ctx* c, int32_t which, int32_t i, void* dst, size_t bytes) {
+  return copy_tensor(c, which, i, dst, bytes, false, true);
+}
+
+extern "C" int ody_ctx_device_ptr(ody_ctx* c, int32_t which, int32_t i, void** out) {
+  if (!out) return fail(ODY_ERR_ARG, "null output");
+  size_t b;
+  return locate(c, which, i, out, &b);
+}
+
+extern "C" int ody_ctx_stream(ody_ctx* c, void** out) {
+  if (!c || !out) return fail(ODY_ERR_ARG, "null argument");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  *out = (void*)c->stream;
+  return ODY_OK;
+}
+
+// Optimizer constants: Float64 hyper-parameters rounded once to float32
+// (full_like, tensor_creation.mojo:355-376); bias corrections
+// 1 - beta^t computed in Float64 (adam.mojo:142-152).
+static OptConsts make_consts(const ody_config& cfg, int64_t t) {
+  OptConsts o;
+  memset(&o, 0, sizeof(o));
+  o.lr = (float)cfg.learning_rate;
+  o.mu = (float)cfg.momentum;
+  o.wd = (float)cfg.weight_decay;
+  o.use_wd = cfg.weight_decay > 0.0;
+  o.use_mu = cfg.momentum > 0.0;
+  o.b1 = (float)cfg.beta1;
+  o.omb1 = (float)(1.0 - cfg.beta1);
+  o.b2 = (float)cfg.beta2;
+  o.omb2 = (float)(1.0 - cfg.beta2);
+  o.eps = (float)cfg.epsilon;
+  if (t > 0) {
+    o.bc1 = (float)(1.0 - pow(cfg.beta1, (double)t));
+    o.bc2 = (float)(1.0 - pow(cfg.beta2, (double)t));
+  }
+  return o;
+}
+
+static DecideParams make_decide(const ody_config& cfg) {
+  DecideParams d;
+  memset(&d, 0, sizeof(d));
+  d.use_scaler = cfg.use_gradient_scaler;
+  d.clip_enabled = cfg.clip_enabled;
+  d.max_norm = cfg.max_norm;
+  d.growth_factor = cfg.growth_factor;
+  d.backoff_factor = cfg.backoff_factor;
+  d.min_scale = cfg.min_scale;
+  d.max_scale = cfg.max_scale;
+  d.growth_interval = cfg.growth_interval;
+  return d;
+}
+
+extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  if (c->broken) return ctx_fail(c, ODY_ERR_STATE, "context unusable after a communicator failure");
+  if (c->cfg.optimizer != ODY_SGD && t <= 0)
+    return ctx_fail(c, ODY_ERR_ARG, "Timestep t must be positive (starts at 1)");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  const OptConsts oc = make_consts(c->cfg, t);
+  const DecideParams dp = make_decide(c->cfg);
+  const int nl = (int)c->tdesc.size();
+  cudaEvent_t* tev = nullptr;
+  if (c->timing) {
+    const int64_t slot = c->tnext++;
+    if (!c->tpending.empty() && c->tpending.front() + kTimingRing <= slot) {
+      ODY_CUDA(timing_collect(c, c->tpending.front()));
+      c->tpending.erase(c->tpending.begin());
+    }
+    c->tpending.push_back(slot);
+    tev = &c->tev[(size_t)(slot % kTimingRing) * 5];
+    ODY_CUDA(cudaEventRecord(tev[0], c->stream));
+  }
+  cudaError_t e = launch_stats(c->gdt, c->grad, c->n_total, c->cfg.use_gradient_scaler, c->scaler, c->partials,
+                               c->grid_stats, c->ticket, c->world > 1 ? 1 : 0, c->local_stats, dp, c->dec,
+                               c->amax, nl, c->stream);
+  if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("stats kernel: ") + cudaGetErrorString(e));
+  if (tev) ODY_CUDA(cudaEventRecord(tev[1], c->stream));
+  if (c->world > 1) {
+    std::string why;
+    NcclApi* api = nccl_api(why);
+    if (!api) return ctx_fail(c, ODY_ERR_NCCL, why);
+    ncclResult_t r = api->allGather(c->local_stats, c->gathered, 2, ncclFloat64, c->comm, c->stream);
+    if (r != ncclSuccess && r != ncclInProgress)
+      return ctx_fail(c, ODY_ERR_NCCL, std::string("ncclAllGather: ") + api->getErrorString(r));
+    int rc = wait_nccl(c, api, "ncclAllGather");
+    if (rc != ODY_OK) return rc;
+    e = launch_finalize(c->gathered, c->world, c->scaler, dp, c->dec, c->amax, nl, c->stream);
+    if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("finalize kernel: ") + cudaGetErrorString(e));
+  }
+  if (tev) ODY_CUDA(cudaEventRecord(tev[2], c->stream));
+  if (!c->chunks_upd.empty()) {
+    e = launch_update(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd,
+                      (int)c->chunks_upd.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout,
+                      c->amax, c->dec, c->grid_upd, c->stream);
+    if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("update kernel: ") + cudaGetErrorString(e));
+  }
+  if (tev) ODY_CUDA(cudaEventRecord(tev[3], c->stream));
+  if (!c->chunks_rq.empty()) {
+    e = launch_requant(c->d_chunks_rq, (int)c->chunks_rq.size(), c->d_tdesc, c->master, c->qout, c->amax,
+                       c->qscale, c->dec, c->grid_rq, c->stream);
+    if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("requant kernel: ") + cudaGetErrorString(e));
+  }
+  if (tev) ODY_CUDA(cudaEventRecord(tev[4], c->stream));
+  ODY_CUDA(cudaMemcpyAsync(c->h_dec, c->dec, sizeof(Decision), cudaMemcpyDeviceToHost, c->stream));
+  ODY_CUDA(cudaEventRecord(c->done, c->stream));
+  c->pending = true;
+  return ODY_OK;
+}
+
+static void fill_result(const Decision& d, ody_step_result* o) {
+  memset(o, 0, sizeof(*o));
+  o->found_inf = d.nonfinite > 0;
+  o->skipped = d.skip;
+  o->clipped = d.clipped;
+  o->nonfinite_count = d.nonfinite;
+  o->sumsq = d.sumsq;
+  o->grad_norm = d.norm;
+  o->clip_coef = d.coef;
+  o->scale_used = d.scale_used;
+  o->scale_next = d.scale_next;
+  o->step_count = d.step_count;
+  o->overflow_count = d.overflow_count;
+  o->scaler_num_steps = d.scaler_num_steps;
+  o->steps_since_growth = d.steps_since_growth;
+}
+
+extern "C" int ody_step_wait(ody_ctx* c, ody_step_result* out) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->pending) return ctx_fail(c, ODY_ERR_STATE, "no step in flight");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  if (c->world > 1) {
+    // bounded host-side wait: a peer that stopped answering aborts the
+    // communicator instead of hanging this rank
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+      cudaError_t q = cudaEventQuery(c->done);
+      if (q == cudaSuccess) break;
+      if (q != cudaErrorNotReady) return ctx_fail(c, ODY_ERR_CUDA, std::string("step: ") + cudaGetErrorString(q));
+      std::string why;
+      NcclApi* api = nccl_api(why);
+      ncclResult_t st = ncclSuccess;
+      if (api && c->comm) api->commGetAsyncError(c->comm, &st);
+      auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+      if ((st != ncclSuccess && st != ncclInProgress) || ms > c->cfg.comm_timeout_ms) {
+        if (api && c->comm) api->commAbort(c->comm);
+        c->comm = nullptr;
+        c->broken = true;
+        c->pending = false;
+        return ctx_fail(c, ODY_ERR_COMM_TIMEOUT, "step: communicator failed or timed out");
+      }
+    }
+  } else {
+    ODY_CUDA(cudaEventSynchronize(c->done));
+  }
+  c->pending = false;
+  if (out) fill_result(*c->h_dec, out);
+  return ODY_OK;
+}
+
+extern "C" int ody_step(ody_ctx* c, int64_t t, ody_step_result* out) {
+  int rc = ody_step_async(c, t);
+  if (rc) return rc;
+  return ody_step_wait(c, out);
+}
+
+extern "C" int ody_ctx_set_timing(ody_ctx* c, int32_t enable) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  if (enable && c->tev.empty()) {
+    c->tev.resize((size_t)kTimingRing * 5);
+    for (auto& e : c->tev) ODY_CUDA(cudaEventCreate(&e));
+  }
+  c->timing = enable != 0;
+  return ODY_OK;
+}
+
+extern "C" int ody_ctx_pass_times(ody_ctx* c, double* ms_out, int64_t* steps_out) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  for (int64_t slot : c->tpending) ODY_CUDA(timing_collect(c, slot));
+  c->tpending.clear();
+  if (ms_out)
+    for (int k = 0; k < 4; k++) ms_out[k] = c->tms[k];
+  if (steps_out) *steps_out = c->tsteps;
+  for (int k = 0; k < 4; k++) c->tms[k] = 0.0;
+  c->tsteps = 0;
+  return ODY_OK;
+}
+
+extern "C" int ody_get_quant(ody_ctx* c, int32_t i, void* dst, size_t bytes, float* ts) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  if (i < 0 || i >= (int)c->specs.size()) return ctx_fail(c, ODY_ERR_ARG, "tensor index out of range");
+  const int li = c->local_of[i];
+  if (li < 0) return ctx_fail(c, ODY_ERR_ARG, "tensor not owned by this rank");
+  const TensorDesc& d = c->tdesc[li];
+  const int64_t need = ody_quant_bytes(d.quant, d.numel);
+  if (d.quant == ODY_Q_NONE) return ctx_fail(c, ODY_ERR_ARG, "tensor has no quantised form");
+  if ((int64_t)bytes != need)
+    return ctx_fail(c, ODY_ERR_SHAPE, "size mismatch: expected " + std::to_string(need) + " bytes");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  if (dst) ODY_CUDA(cudaMemcpyAsync(dst, c->qout + d.qoff, bytes, cudaMemcpyDefault, c->stream));
+  float s = 1.0f;
+  ODY_CUDA(cudaMemcpyAsync(&s, c->qscale + li, 4, cudaMemcpyDeviceToHost, c->stream));
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  if (ts) *ts = s;
+  return ODY_OK;
+}
+
+extern "C" int ody_get_scaler(ody_ctx* c, float* scale, int64_t* since, int64_t* num, int64_t* steps,
+                              int64_t* overflows) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  DevScaler h;
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  ODY_CUDA(cudaMemcpyAsync(&h, c->scaler, sizeof(h), cudaMemcpyDeviceToHost, c->stream));
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  if (scale) *scale = h.scale;
+  if (since) *since = h.steps_since_growth;
+  if (num) *num = h.num_steps;
+  if (steps) *steps = h.step_count;
+  if (overflows) *overflows = h.overflow_count;
+  return ODY_OK;
+}
+
+extern "C" int ody_set_scaler(ody_ctx* c, float scale, int64_t since, int64_t num, int64_t steps,
+                              int64_t overflows) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  DevScaler h;
+  memset(&h, 0, sizeof(h));
+  h.scale = scale;
+  h.steps_since_growth = since;
+  h.num_steps = num;
+  h.step_count = steps;
+  h.overflow_count = overflows;
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  ODY_CUDA(cudaMemcpyAsync(c->scaler, &h, sizeof(h), cudaMemcpyHostToDevice, c->stream));
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  return ODY_OK;
+}
+
+// checkpoint layout: header, DevScaler, then per local tensor in index
+// order: master, state1 (if any), state2 (if any), all float32
+struct CkptHeader {
+  char magic[8];
+  int32_t version;
+  int32_t optimizer;
+  int32_t ntensors_local;
+  int32_t nstates;
+  int64_t total_elems;
+};
+
+extern "C" int ody_ctx_export(ody_ctx* c, void* buf, size_t* bytes) {
+  if (!c || !bytes) return fail(ODY_ERR_ARG, "null argument");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  const int nstates = (c->s1 ? 1 : 0) + (c->s2 ? 1 : 0);
+  int64_t elems = 0;
+  for (auto& d : c->tdesc) elems += d.numel;
+  const size_t need = sizeof(CkptHeader) + sizeof(DevScaler) + (size_t)elems * 4 * (1 + nstates);
+  if (!buf) {
+    *bytes = need;
+    return ODY_OK;
+  }
+  if (*bytes < need) return ctx_fail(c, ODY_ERR_SHAPE, "checkpoint buffer too small");
+  CkptHeader h;
+  memset(&h, 0, sizeof(h));
+  memcpy(h.magic, "ODYMP01", 8);
+  h.version = 1;
+  h.optimizer = c->cfg.optimizer;
+  h.ntensors_local = (int32_t)c->tdesc.size();
+  h.nstates = nstates;
+  h.total_elems = elems;
+  uint8_t* p = (uint8_t*)buf;
+  memcpy(p, &h, sizeof(h));
+  p += sizeof(h);
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  ODY_CUDA(cudaMemcpyAsync(p, c->scaler, sizeof(DevScaler), cudaMemcpyDeviceToHost, c->stream));
+  p += sizeof(DevScaler);
+  float* arenas[3] = {c->master, c->s1, c->s2};
+  for (auto& d : c->tdesc)
+    for (int k = 0; k < 3; k++) {
+      if (!arenas[k]) continue;
+      ODY_CUDA(cudaMemcpyAsync(p, arenas[k] + d.off, (size_t)d.numel * 4, cudaMemcpyDeviceToHost, c->stream));
+      p += (size_t)d.numel * 4;
+    }
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  *bytes = need;
+  return ODY_OK;
+}
+
+extern "C" int ody_ctx_import(ody_ctx* c, const void* buf, size_t bytes) {
+  if (!c || !buf) return fail(ODY_ERR_ARG, "null argument");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  size_t need = 0;
+  int rc = ody_ctx_export(c, nullptr, &need);
+  if (rc) return rc;
+  CkptHeader h;
+  if (bytes < sizeof(h)) return ctx_fail(c, ODY_ERR_SHAPE, "checkpoint truncated");
+  memcpy(&h, buf, sizeof(h));
+  if (memcmp(h.magic, "ODYMP01", 8) != 0 || h.version != 1)
+    return ctx_fail(c, ODY_ERR_ARG, "not an odyssey_mp checkpoint");
+  if (bytes != need || h.optimizer != c->cfg.optimizer || h.ntensors_local != (int32_t)c->tdesc.size())
+    return ctx_fail(c, ODY_ERR_SHAPE, "checkpoint does not match this context");
+  const uint8_t* p = (const uint8_t*)buf + sizeof(h);
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  ODY_CUDA(cudaMemcpyAsync(c->scaler, p, sizeof(DevScaler), cudaMemcpyHostToDevice, c->stream));
+  p += sizeof(DevScaler);
+  float* arenas[3] = {c->master, c->s1, c->s2};
+  for (auto& d : c->tdesc)
+    for (int k = 0; k < 3; k++) {
+      if (!arenas[k]) continue;
+      ODY_CUDA(cudaMemcpyAsync(arenas[k] + d.off, p, (size_t)d.numel * 4, cudaMemcpyHostToDevice, c->stream));
+      p += (size_t)d.numel * 4;
+    }
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  return ODY_OK;
+}
+
+extern "C" void ody_ctx_destroy(ody_ctx* c) {
+  if (!c) return;
+  if (c->finalized || c->stream) cudaSetDevice(c->cfg.device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->comm) {
+    std::string why;
+    NcclApi* api = nccl_api(why);
+    if (api) api->commDestroy(c->comm);
+  }
+  void* bufs[] = {c->master, c->s1, c->s2, c->grad, c->qout, c->qscale, c->amax, c->d_chunks_upd,
+                  c->d_chunks_rq, c->d_tdesc, c->partials, c->ticket, c->scaler, c->dec,
+                  c->local_stats, c->gathered};
+  for (void* b : bufs)
+    if (b) cudaFree(b);
+  for (auto& e : c->tev) cudaEventDestroy(e);
+  if (c->h_dec) cudaFreeHost(c->h_dec);
+  if (c->done) cudaEventDestroy(c->done);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+// ---------------------------------------------------------------------------
+// Stateless single operations.  Each pointer may be host or device memory;
+// host operands are staged through temporary device buffers on the calling
+// thread's default stream.
+// ---------------------------------------------------------------------------
+static bool is_device_ptr(const void* p) {
+  if (!p) return false;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+namespace {
+struct Staged {
+  void* user = nullptr;
+  void* dev = nullptr;
+  size_t bytes = 0;
+  bool owned = false;
+};
+
+struct Scope {
+  cudaStream_t st = cudaStreamPerThread;
+  std::vector<Staged> bufs;
+  ~Scope() {
+    for (auto& b : bufs)
+      if (b.owned && b.dev) cudaFreeAsync(b.dev, st);
+  }
+  // in: copy host data to device; out-only: allocate
+  cudaError_t stage(const void* user, size_t bytes, bool copy_in, void** dev) {
+    if (!user) {
+      *dev = nullptr;
+      return cudaSuccess;
+    }
+    if (is_device_ptr(user)) {
+      *dev = const_cast<void*>(user);
+      bufs.push_back({const_cast<void*>(user), *dev, bytes, false});
+      return cudaSuccess;
+    }
+    void* d = nullptr;
+    cudaError_t e = cudaMallocAsync(&d, bytes < 16 ? 16 : bytes, st);
+    if (e != cudaSuccess) return e;
+    if (copy_in) {
+      e = cudaMemcpyAsync(d, user, bytes, cudaMemcpyHostToDevice, st);
+      if (e != cudaSuccess) return e;
+    }
+    bufs.push_back({const_cast<void*>(user), d, bytes, true});
+    *dev = d;
+    return cudaSuccess;
+  }
+  cudaError_t copy_out(void* user) {
+    for (auto& b : bufs)
+      if (b.user == user && b.owned) return cudaMemcpyAsync(user, b.dev, b.bytes, cudaMemcpyDeviceToHost, st);
+    return cudaSuccess;
+  }
+};
+}  // namespace
+
+#define ODY_STAGE(S, ptr, bytes, in, dev)                                             \
+  do {                                                                                \
+    cudaError_t se_ = (S).stage((ptr), (bytes), (in), (void**)(dev));                 \
+    if (se_ != cudaSuccess)                                                           \
+      return fail(ODY_ERR_CUDA, std::string("staging a buffer: ") + cudaGetErrorString(se_)); \
+  } while (0)
+
+static int check_dtype(int dt) {
+  if (dt < DT_F32 || dt > DT_BF16) return fail(ODY_ERR_DTYPE, "unsupported dtype " + std::to_string(dt));
+  return ODY_OK;
+}
+
+static void current_device_tables() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  upload_fp4_tables(dev);
+}
+
+extern "C" int ody_unscale(const void* g, int32_t dt, int64_t n, float scale, void* out) {
+  if (check_dtype(dt)) return ODY_ERR_DTYPE;
+  if (n <= 0) return fail(ODY_ERR_SHAPE, "Cannot unscale empty gradient tensor");
+  if (scale == 0.0f) return fail(ODY_ERR_ARG, "Cannot unscale with zero scale factor");
+  if (!g || !out) return fail(ODY_ERR_ARG, "null pointer");
+  Scope S;
+  void *dg, *dout;
+  const size_t b = (size_t)n * dtype_size(dt);
+  ODY_STAGE(S, g, b, true, &dg);
+  ODY_STAGE(S, out, b, false, &dout);
+  ODY_CUDA(launch_unscale(dt, dg, n, scale, dout, S.st));
+  ODY_CUDA(S.copy_out(out));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  return ODY_OK;
+}
+
+extern "C" int ody_check_finite(const void* g, int32_t dt, int64_t n, int32_t* finite) {
+  if (check_dtype(dt)) return ODY_ERR_DTYPE;
+  if (!finite || (!g && n > 0) || n < 0) return fail(ODY_ERR_ARG, "bad argument");
+  if (n == 0) {
+    *finite = 1;
+    return ODY_OK;
+  }
+  Scope S;
+  void *dg, *dc;
+  ODY_STAGE(S, g, (size_t)n * dtype_size(dt), true, &dg);
+  unsigned long long hc = 0;
+  ODY_CUDA(cudaMallocAsync(&dc, 8, S.st));
+  S.bufs.push_back({nullptr, dc, 8, true});
+  ODY_CUDA(cudaMemsetAsync(dc, 0, 8, S.st));
+  ODY_CUDA(launch_count_nonfinite(dt, dg, n, (unsigned long long*)dc, S.st));
+  ODY_CUDA(cudaMemcpyAsync(&hc, dc, 8, cudaMemcpyDeviceToHost, S.st));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  *finite = hc == 0;
+  return ODY_OK;
+}
+
+extern "C" int ody_to_fp32(const void* x, int32_t dt, int64_t n, float* out) {
+  if (check_dtype(dt)) return ODY_ERR_DTYPE;
+  if (n <= 0) return fail(ODY_ERR_SHAPE, "Cannot convert empty parameter tensor");
+  if (!x || !out) return fail(ODY_ERR_ARG, "null pointer");
+  Scope S;
+  void *dx, *dout;
+  ODY_STAGE(S, x, (size_t)n * dtype_size(dt), true, &dx);
+  ODY_STAGE(S, out, (size_t)n * 4, false, &dout);
+  // upcast = dequantise of the FP16/BF16 kinds; float32 is a copy
+  if (dt == DT_F32)
+    ODY_CUDA(cudaMemcpyAsync(dout, dx, (size_t)n * 4, cudaMemcpyDeviceToDevice, S.st));
+  else
+    ODY_CUDA(launch_dequantize(dt == DT_F16 ? Q_FP16 : Q_BF16, (const uint8_t*)dx, n, nullptr, (float*)dout, S.st));
+  ODY_CUDA(S.copy_out(out));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  return ODY_OK;
+}
+
+extern "C" int ody_global_norm_clip(float* const* grads, const int64_t* numels, int32_t nt, float max_norm,
+                                    float* total_norm) {
+  if (!(max_norm > 0.0f)) return fail(ODY_ERR_ARG, "max_norm must be positive, got: " + std::to_string(max_norm));
+  if (nt < 0 || (nt > 0 && (!grads || !numels))) return fail(ODY_ERR_ARG, "bad argument");
+  Scope S;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int grid = stats_grid(dev);
+  void *part, *ticket, *tot, *norm, *coef;
+  ODY_CUDA(cudaMallocAsync(&part, sizeof(StatsPartial) * grid, S.st));
+  S.bufs.push_back({nullptr, part, 0, true});
+  ODY_CUDA(cudaMallocAsync(&ticket, 4, S.st));
+  S.bufs.push_back({nullptr, ticket, 0, true});
+  ODY_CUDA(cudaMallocAsync(&tot, 8, S.st));
+  S.bufs.push_back({nullptr, tot, 0, true});
+  ODY_CUDA(cudaMallocAsync(&norm, 8, S.st));
+  S.bufs.push_back({nullptr, norm, 0, true});
+  coef = (float*)norm + 1;
+  ODY_CUDA(cudaMemsetAsync(ticket, 0, 4, S.st));
+  ODY_CUDA(cudaMemsetAsync(tot, 0, 8, S.st));
+  std::vector<void*> dptr(nt);
+  for (int i = 0; i < nt; i++) {
+    if (numels[i] < 0 || (numels[i] > 0 && !grads[i])) return fail(ODY_ERR_ARG, "bad tensor");
+    ODY_STAGE(S, grads[i], (size_t)numels[i] * 4, true, &dptr[i]);
+    if (numels[i] > 0)
+      ODY_CUDA(launch_sumsq((const float*)dptr[i], numels[i], (StatsPartial*)part, grid, (unsigned*)ticket,
+                            (double*)tot, S.st));
+  }
+  ODY_CUDA(launch_clip_coef((const double*)tot, max_norm, (float*)norm, (float*)coef, S.st));
+  for (int i = 0; i < nt; i++)
+    if (numels[i] > 0) ODY_CUDA(launch_scale_inplace((float*)dptr[i], numels[i], (const float*)coef, S.st));
+  for (int i = 0; i < nt; i++) ODY_CUDA(S.copy_out(grads[i]));
+  float hn = 0.0f;
+  ODY_CUDA(cudaMemcpyAsync(&hn, norm, 4, cudaMemcpyDeviceToHost, S.st));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  if (total_norm) *total_norm = hn;
+  return ODY_OK;
+}
+
+static int opt_common(int opt, const float* p, const float* g, const float* s1, const float* s2, int64_t n,
+                      int64_t t, double lr, double mu, double b1, double b2, double eps, double wd, float* op,
+                      float* os1, float* os2) {
+  if (n <= 0) return fail(ODY_ERR_SHAPE, "Parameters and gradients must have the same shape");
+  if (!p || !g || !op) return fail(ODY_ERR_ARG, "null pointer");
+  if (opt == OPT_SGD) {
+    if (mu > 0.0 && !s1)
+      return fail(ODY_ERR_ARG, "Velocity buffer required when using momentum (use zeros_like(params))");
+  } else {
+    if (!s1 || !s2 || !os1 || !os2)
+      return fail(ODY_ERR_ARG, "Moment buffers (m and v) must be initialized (use zeros_like(params))");
+    if (t <= 0) return fail(ODY_ERR_ARG, "Timestep t must be positive (starts at 1)");
+  }
+  ody_config cfg;
+  ody_config_default(&cfg);
+  cfg.learning_rate = lr;
+  cfg.momentum = mu;
+  cfg.beta1 = b1;
+  cfg.beta2 = b2;
+  cfg.epsilon = eps;
+  cfg.weight_decay = wd;
+  const OptConsts oc = make_consts(cfg, t);
+  Scope S;
+  const size_t b = (size_t)n * 4;
+  void *dp, *dg, *ds1 = nullptr, *ds2 = nullptr, *dop, *dos1 = nullptr, *dos2 = nullptr;
+  ODY_STAGE(S, p, b, true, &dp);
+  ODY_STAGE(S, g, b, true, &dg);
+  if (s1) ODY_STAGE(S, s1, b, true, &ds1);
+  if (s2) ODY_STAGE(S, s2, b, true, &ds2);
+  ODY_STAGE(S, op, b, false, &dop);
+  if (os1) ODY_STAGE(S, os1, b, false, &dos1);
+  if (os2) ODY_STAGE(S, os2, b, false, &dos2);
+  // SGD without a velocity input but with an output: velocity stays zero
+  if (opt == OPT_SGD && !s1 && dos1) ODY_CUDA(cudaMemsetAsync(dos1, 0, b, S.st));
+  ODY_CUDA(launch_opt_step(opt, oc, (const float*)dp, (const float*)dg, (const float*)ds1, (const float*)ds2, n,
+                           (float*)dop, (opt == OPT_SGD && !s1) ? nullptr : (float*)dos1, (float*)dos2, S.st));
+  ODY_CUDA(S.copy_out(op));
+  if (os1) ODY_CUDA(S.copy_out(os1));
+  if (os2) ODY_CUDA(S.copy_out(os2));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  return ODY_OK;
+}
+
+extern "C" int ody_sgd_step(const float* p, const float* g, const float* vel, int64_t n, double lr, double mu,
+                            double wd, float* op, float* ov) {
+  return opt_common(OPT_SGD, p, g, vel, nullptr, n, 0, lr, mu, 0.9, 0.999, 1e-8, wd, op, ov, nullptr);
+}
+
+extern "C" int ody_adam_step(const float* p, const float* g, const float* m, const float* v, int64_t n, int64_t t,
+                             double lr, double b1, double b2, double eps, double wd, float* op, float* om,
+                             float* ov) {
+  return opt_common(OPT_ADAM, p, g, m, v, n, t, lr, 0.0, b1, b2, eps, wd, op, om, ov);
+}
+
+extern "C" int ody_adamw_step(const float* p, const float* g, const float* m, const float* v, int64_t n, int64_t t,
+                              double lr, double b1, double b2, double eps, double wd, float* op, float* om,
+                              float* ov) {
+  return opt_common(OPT_ADAMW, p, g, m, v, n, t, lr, 0.0, b1, b2, eps, wd, op, om, ov);
+}
+
+extern "C" int ody_quantize(int32_t kind, const void* src, int32_t sdt, int64_t n, void* out, float* ts) {
+  if (kind <= ODY_Q_NONE || kind > ODY_Q_NVFP4_TENSOR)
+    return fail(ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(kind));
+  if (sdt != DT_F32 && sdt != DT_BF16) return fail(ODY_ERR_DTYPE, "quantize source must be float32 or bfloat16");
+  if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot quantize an empty tensor");
+  if (!src || !out) return fail(ODY_ERR_ARG, "null pointer");
+  current_device_tables();
+  Scope S;
+  void *dx, *dout, *damax, *dts;
+  const int64_t qb = ody_quant_bytes(kind, n);
+  ODY_STAGE(S, src, (size_t)n * dtype_size(sdt), true, &dx);
+  ODY_STAGE(S, out, (size_t)qb, false, &dout);
+  ODY_CUDA(cudaMallocAsync(&damax, 8, S.st));
+  S.bufs.push_back({nullptr, damax, 0, true});
+  dts = (uint32_t*)damax + 1;
+  ODY_CUDA(cudaMemsetAsync(damax, 0, 8, S.st));
+  if (kind == ODY_Q_NVFP4_TENSOR || kind == ODY_Q_FP8_E4M3_TENSOR)
+    ODY_CUDA(launch_amax(sdt, dx, n, (uint32_t*)damax, S.st));
+  ODY_CUDA(launch_quantize(kind, sdt, dx, n, (uint8_t*)dout, (const uint32_t*)damax, (float*)dts, S.st));
+  ODY_CUDA(S.copy_out(out));
+  float hts = 1.0f;
+  ODY_CUDA(cudaMemcpyAsync(&hts, dts, 4, cudaMemcpyDeviceToHost, S.st));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  if (ts) *ts = hts;
+  return ODY_OK;
+}
+
+extern "C" int ody_dequantize(int32_t kind, const void* q, int64_t n, float ts, float* out) {
+  if (kind <= ODY_Q_NONE || kind > ODY_Q_NVFP4_TENSOR)
+    return fail(ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(kind));
+  if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot dequantize an empty tensor");
+  if (!q || !out) return fail(ODY_ERR_ARG, "null pointer");
+  Scope S;
+  void *dq, *dout, *dts;
+  ODY_STAGE(S, q, (size_t)ody_quant_bytes(kind, n), true, &dq);
+  ODY_STAGE(S, out, (size_t)n * 4, false, &dout);
+  ODY_CUDA(cudaMallocAsync(&dts, 4, S.st));
+  S.bufs.push_back({nullptr, dts, 0, true});
+  ODY_CUDA(cudaMemcpyAsync(dts, &ts, 4, cudaMemcpyHostToDevice, S.st));
+  ODY_CUDA(launch_dequantize(kind, (const uint8_t*)dq, n, (const float*)dts, (float*)dout, S.st));
+  ODY_CUDA(S.copy_out(out));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  return ODY_OK;
+}

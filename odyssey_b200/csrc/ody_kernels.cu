@@ -1,0 +1,1054 @@
+// ody_kernels.cu -- sm_100a kernels of the fused mixed-precision step.
+//
+// Pass structure of one step (all passes stream HBM; no tensor cores):
+//   pass 1  stats_kernel    grads -> unscale, isfinite count, sum of float32
+//                           squares in float64 (per-CTA partials, fixed-order
+//                           final sum in the last CTA -> deterministic), and
+//                           the GradScaler / clip decision in device memory.
+//   pass 2  update_kernel   chunk-table multi-tensor apply: unscale, clip,
+//                           SGD / Adam / AdamW on float32 master + states,
+//                           direct requant (FP16/BF16/FP8/MXFP4/NVFP4) and the
+//                           per-tensor amax of the new master for the
+//                           per-tensor-scaled kinds.
+//   pass 3  requant_kernel  FP8-E4M3 and NVFP4 with a per-tensor scale, which
+//                           need the whole tensor's amax first.
+// Standalone quantise / dequantise / single-op kernels live at the end.
+#include <math.h>
+#include <stdio.h>
+
+#include "ody_internal.h"
+
+namespace ody {
+
+// ---------------------------------------------------------------------------
+// FP4 threshold tables (see fp4_encode in ody_numerics.cuh).  Index: the
+// E8M0 byte (MXFP4) or the E4M3 byte (NVFP4) of the block scale.
+// ---------------------------------------------------------------------------
+__device__ Fp4Thr g_thr_mx[256];
+__device__ Fp4Thr g_thr_nv[128];
+
+static float host_bits(uint32_t b) {
+  float f;
+  memcpy(&f, &b, 4);
+  return f;
+}
+
+// least float x >= 0 with RN(x / s) >= T (IEEE float division on the host);
+// NaN when no float reaches T.
+static float host_threshold(float s, float T) {
+  auto reaches = [&](uint32_t xb) {
+    volatile float x = host_bits(xb);
+    volatile float q = x / s;
+    return q >= T;
+  };
+  uint32_t lo = 0, hi = 0x7f800000u;
+  if (!reaches(hi)) return host_bits(0x7fc00000u);
+  if (reaches(lo)) return 0.0f;
+  while (hi - lo > 1) {
+    uint32_t mid = lo + (hi - lo) / 2;
+    if (reaches(mid))
+      hi = mid;
+    else
+      lo = mid;
+  }
+  return host_bits(hi);
+}
+
+static void host_fill_thr(float s, Fp4Thr* t) {
+  const float T[7] = {host_bits(1u), 0.5f, 1.25f, 1.75f, 2.5f, 3.5f, 5.0f};
+  for (int k = 0; k < 7; k++) t->t[k] = host_threshold(s, T[k]);
+  t->t[7] = 0.0f;
+}
+
+static float host_e8m0_to_f32(int e) {
+  if (e == 0) return 0.0f;
+  if (e == 255) return host_bits(0x7f800000u);
+  return host_bits((uint32_t)e << 23);
+}
+
+static float host_e4m3_to_f32(int b) {
+  int e = (b >> 3) & 0xf, m = b & 7;
+  if (e == 0) return ldexpf((float)m, -9);
+  return ldexpf((float)(8 + m), e - 10);
+}
+
+static Fp4Thr h_thr_mx[256], h_thr_nv[128];
+static bool h_thr_ready = false;
+static bool d_thr_ready[64] = {false};
+
+void upload_fp4_tables(int device) {
+  if (!h_thr_ready) {
+    for (int e = 0; e < 256; e++) host_fill_thr(host_e8m0_to_f32(e), &h_thr_mx[e]);
+    for (int b = 0; b < 128; b++) host_fill_thr(b == 127 ? 0.0f : host_e4m3_to_f32(b), &h_thr_nv[b]);
+    h_thr_ready = true;
+  }
+  if (device >= 0 && device < 64 && !d_thr_ready[device]) {
+    cudaMemcpyToSymbol(g_thr_mx, h_thr_mx, sizeof(h_thr_mx));
+    cudaMemcpyToSymbol(g_thr_nv, h_thr_nv, sizeof(h_thr_nv));
+    d_thr_ready[device] = true;
+  }
+}
+
+__device__ __forceinline__ void load_thr_smem(Fp4Thr* s_mx, Fp4Thr* s_nv) {
+  float* dm = reinterpret_cast<float*>(s_mx);
+  float* dn = reinterpret_cast<float*>(s_nv);
+  const float* gm = reinterpret_cast<const float*>(g_thr_mx);
+  const float* gn = reinterpret_cast<const float*>(g_thr_nv);
+  for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) dm[i] = gm[i];
+  for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x) dn[i] = gn[i];
+}
+
+// ---------------------------------------------------------------------------
+// Gradient loading + unscale (GradientScaler.unscale_gradients,
+// src/odyssey/training/mixed_precision.mojo:154-182): g / full(F64(scale),
+// g.dtype) -- divisor rounded to the gradient dtype, quotient rounded to the
+// gradient dtype, then the exact upcast to float32 (convert_to_fp32_master).
+// ---------------------------------------------------------------------------
+template <int GDT>
+__device__ __forceinline__ float unscale_divisor(float scale) {
+  if (GDT == DT_F16) return f16_bits_to_f32(f32_to_f16_bits(scale));
+  if (GDT == DT_BF16) return bf16_bits_to_f32(f32_to_bf16_bits(scale));
+  return scale;
+}
+
+// Division by a power of two equals multiplication by its exact reciprocal
+// (both are the single correct rounding of the same real number).
+struct Divisor {
+  float d, r;
+  bool pow2;
+};
+__device__ __forceinline__ Divisor make_divisor(float d) {
+  Divisor v;
+  v.d = d;
+  uint32_t b = __float_as_uint(d);
+  uint32_t e = (b >> 23) & 0xff;
+  v.pow2 = ((b & 0x807fffffu) == 0) && e >= 1 && e <= 254;
+  v.r = v.pow2 ? __fdiv_rn(1.0f, d) : 0.0f;
+  return v;
+}
+__device__ __forceinline__ float divide(float x, const Divisor& v) {
+  return v.pow2 ? __fmul_rn(x, v.r) : __fdiv_rn(x, v.d);
+}
+
+template <int GDT>
+__device__ __forceinline__ void grad8(const void* g, int64_t e0, bool use_scaler, const Divisor& dv,
+                                      float out[8]) {
+  if (GDT == DT_F32) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(g) + e0);
+    float4 a = __ldcs(p), b = __ldcs(p + 1);
+    float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 8; k++) out[k] = use_scaler ? divide(x[k], dv) : x[k];
+  } else {
+    uint4 raw = __ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(g) + e0));
+    uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      uint16_t h = (uint16_t)(w[k >> 1] >> ((k & 1) * 16));
+      float x = GDT == DT_F16 ? f16_bits_to_f32(h) : bf16_bits_to_f32(h);
+      if (use_scaler) {
+        float q = divide(x, dv);
+        x = GDT == DT_F16 ? f16_bits_to_f32(f32_to_f16_bits(q)) : bf16_bits_to_f32(f32_to_bf16_bits(q));
+      }
+      out[k] = x;
+    }
+  }
+}
+
+__device__ __forceinline__ bool is_finite_f(float x) { return fabsf(x) < __uint_as_float(0x7f800000u); }
+
+// ---------------------------------------------------------------------------
+// The GradientScaler / PrecisionConfig.step decision (mixed_precision.mojo:
+// 184-221, precision_config.mojo:455-473) plus the global-norm clip
+// coefficient (gradient_clipping.mojo:273-368).
+// ---------------------------------------------------------------------------
+__device__ void decide(double sumsq, int64_t nonfinite, DevScaler* sc, const DecideParams& dp,
+                       Decision* out) {
+  Decision r;
+  memset(&r, 0, sizeof(r));
+  r.sumsq = sumsq;
+  r.nonfinite = nonfinite;
+  r.norm = __double2float_rn(__dsqrt_rn(sumsq));
+  r.scale_used = sc->scale;
+  r.coef = 1.0f;
+  sc->step_count += 1;
+  if (nonfinite > 0) {
+    r.skip = 1;
+    if (dp.use_scaler) {
+      float ns = __fmul_rn(sc->scale, dp.backoff_factor);
+      if (ns >= dp.min_scale) sc->scale = ns;
+      sc->steps_since_growth = 0;
+      sc->overflow_count += 1;
+    }
+  } else {
+    if (dp.clip_enabled && r.norm > dp.max_norm) {
+      r.clipped = 1;
+      r.coef = __double2float_rn(__ddiv_rn((double)dp.max_norm, __dadd_rn((double)r.norm, 1e-6)));
+    }
+    if (dp.use_scaler) {
+      sc->num_steps += 1;
+      sc->steps_since_growth += 1;
+      if (sc->steps_since_growth >= dp.growth_interval) {
+        float ns = __fmul_rn(sc->scale, dp.growth_factor);
+        sc->scale = ns > dp.max_scale ? dp.max_scale : ns;
+        sc->steps_since_growth = 0;
+      }
+    }
+  }
+  r.scale_next = sc->scale;
+  r.step_count = sc->step_count;
+  r.overflow_count = sc->overflow_count;
+  r.scaler_num_steps = sc->num_steps;
+  r.steps_since_growth = sc->steps_since_growth;
+  *out = r;
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum of (double, int64); result valid in thread 0.
+__device__ __forceinline__ void block_sum2(double& s, long long& c) {
+  __shared__ double sd[32];
+  __shared__ long long sc[32];
+  s = warp_sum(s);
+  c = warp_sum(c);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sd[w] = s;
+    sc[w] = c;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    s = l < nw ? sd[l] : 0.0;
+    c = l < nw ? sc[l] : 0;
+    s = warp_sum(s);
+    c = warp_sum(c);
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// Pass 1: gradient statistics and the step decision.
+// ---------------------------------------------------------------------------
+struct StatsArgs {
+  const void* grad;
+  int64_t n;  // multiple of 8
+  int use_scaler;
+  DevScaler* scaler;
+  StatsPartial* partials;
+  unsigned* ticket;
+  int world_mode;        // 0: decide here; 1: write local_stats for the allgather
+  double* local_stats;   // [2]: nonfinite (as double), sumsq
+  DecideParams dp;
+  Decision* dec;
+  uint32_t* amax_slots;  // zeroed for pass 2
+  int ntensors;
+};
+
+template <int GDT>
+__global__ void __launch_bounds__(kThreads) stats_kernel(StatsArgs a) {
+  const Divisor dv = make_divisor(unscale_divisor<GDT>(a.scaler->scale));
+  double acc = 0.0;
+  long long bad = 0;
+  const int64_t ngroups = a.n / 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  constexpr int U = 4;
+  for (; i + (U - 1) * stride < ngroups; i += U * stride) {
+    float v[U][8];
+#pragma unroll
+    for (int u = 0; u < U; u++) grad8<GDT>(a.grad, (i + u * stride) * 8, a.use_scaler, dv, v[u]);
+#pragma unroll
+    for (int u = 0; u < U; u++)
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        bad += !is_finite_f(v[u][k]);
+        acc += (double)__fmul_rn(v[u][k], v[u][k]);
+      }
+  }
+  for (; i < ngroups; i += stride) {
+    float v[8];
+    grad8<GDT>(a.grad, i * 8, a.use_scaler, dv, v);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      bad += !is_finite_f(v[k]);
+      acc += (double)__fmul_rn(v[k], v[k]);
+    }
+  }
+  block_sum2(acc, bad);
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    a.partials[blockIdx.x].sumsq = acc;
+    a.partials[blockIdx.x].nonfinite = bad;
+    __threadfence();
+    unsigned t = atomicAdd(a.ticket, 1u);
+    last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // fixed-order reduction of the per-CTA partials -> deterministic sum
+  double s = 0.0;
+  long long c = 0;
+  for (int j = threadIdx.x; j < (int)gridDim.x; j += blockDim.x) {
+    s += __ldcg(&a.partials[j].sumsq);
+    c += __ldcg(reinterpret_cast<const long long*>(&a.partials[j].nonfinite));
+  }
+  block_sum2(s, c);
+  for (int j = threadIdx.x; j < a.ntensors; j += blockDim.x) a.amax_slots[j] = 0u;
+  if (threadIdx.x == 0) {
+    *a.ticket = 0u;
+    if (a.world_mode == 0) {
+      decide(s, c, a.scaler, a.dp, a.dec);
+    } else {
+      a.local_stats[0] = (double)c;
+      a.local_stats[1] = s;
+    }
+  }
+}
+
+int stats_grid(int device) {
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  return sms * 8;
+}
+
+cudaError_t launch_stats(int gdt, const void* grad, int64_t n, int use_scaler, DevScaler* scaler,
+                         StatsPartial* partials, int grid, unsigned* ticket, int world_mode,
+                         double* local_stats, const DecideParams& dp, Decision* dec,
+                         uint32_t* amax_slots, int ntensors, cudaStream_t st) {
+  StatsArgs a{grad, n, use_scaler, scaler, partials, ticket, world_mode, local_stats, dp, dec,
+              amax_slots, ntensors};
+  if (gdt == DT_F32)
+    stats_kernel<DT_F32><<<grid, kThreads, 0, st>>>(a);
+  else if (gdt == DT_F16)
+    stats_kernel<DT_F16><<<grid, kThreads, 0, st>>>(a);
+  else
+    stats_kernel<DT_BF16><<<grid, kThreads, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// Multi-GPU: the per-rank {nonfinite, sumsq} pairs arrive in rank order from
+// an allgather; summing them in rank order gives every rank the identical
+// decision.
+__global__ void finalize_kernel(const double* gathered, int world, DevScaler* sc, DecideParams dp,
+                                Decision* dec, uint32_t* amax_slots, int ntensors) {
+  for (int j = threadIdx.x; j < ntensors; j += blockDim.x) amax_slots[j] = 0u;
+  if (threadIdx.x == 0) {
+    double c = 0.0, s = 0.0;
+    for (int r = 0; r < world; r++) {
+      c += gathered[2 * r];
+      s += gathered[2 * r + 1];
+    }
+    decide(s, (int64_t)c, sc, dp, dec);
+  }
+}
+
+cudaError_t launch_finalize(const double* gathered, int world, DevScaler* scaler,
+                            const DecideParams& dp, Decision* dec, uint32_t* amax_slots,
+                            int ntensors, cudaStream_t st) {
+  finalize_kernel<<<1, 256, 0, st>>>(gathered, world, scaler, dp, dec, amax_slots, ntensors);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Tile-level re-quantisation helpers shared by passes 2 and 3 and the
+// standalone quantiser.  Thread t of the CTA holds elements [8t, 8t+8) of a
+// 2048-element tile; MXFP4 blocks span 4 threads, NVFP4 blocks 2 threads.
+// Codes are staged in shared memory in the reference's AoS block layout
+// (tensor_dtype_conv.mojo:281-366: code bytes, element 2i in the high
+// nibble, then the scale byte) and written out as 16-byte stores.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void stage_mxfp4(const float v[8], uint8_t* stage, const Fp4Thr* thr) {
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
+  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+  const uint8_t e = e8m0_from_f32(block_scale_value(am));
+  const float* t = thr[e].t;
+  const int g = threadIdx.x, blk = g >> 2, j = g & 3;
+  uint8_t* dst = stage + blk * 17 + 4 * j;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+    dst[i] = (uint8_t)((fp4_encode(v[2 * i], t, false) << 4) | fp4_encode(v[2 * i + 1], t, false));
+  if (j == 3) stage[blk * 17 + 16] = e;
+}
+
+__device__ __forceinline__ void stage_nvfp4(const float v[8], uint8_t* stage, const Fp4Thr* thr) {
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
+  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+  const uint8_t e = e4m3_scale_from_f32(block_scale_value(am));
+  const float* t = thr[e].t;
+  const bool z = (e == 0);
+  const int g = threadIdx.x, blk = g >> 1, j = g & 1;
+  uint8_t* dst = stage + blk * 9 + 4 * j;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+    dst[i] = (uint8_t)((fp4_encode(v[2 * i], t, z) << 4) | fp4_encode(v[2 * i + 1], t, z));
+  if (j == 1) stage[blk * 9 + 8] = e;
+}
+
+// Copy `nbytes` staged bytes to global memory; 16-byte stores when the
+// destination is aligned and the whole range may be written, else bytes up to
+// `limit`.
+__device__ __forceinline__ void flush_stage(const uint8_t* stage, int nbytes, uint8_t* dst,
+                                            int64_t limit) {
+  if (limit >= nbytes && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
+    const uint4* s = reinterpret_cast<const uint4*>(stage);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int i = threadIdx.x; i < nbytes / 16; i += blockDim.x) d[i] = s[i];
+  } else {
+    const int m = (int)(limit < nbytes ? limit : nbytes);
+    for (int i = threadIdx.x; i < m; i += blockDim.x) dst[i] = stage[i];
+  }
+}
+
+__device__ __forceinline__ void store_elem8(int kind, const float v[8], uint8_t* dst) {
+  if (kind == Q_FP16 || kind == Q_BF16) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      uint32_t lo = kind == Q_FP16 ? f32_to_f16_bits(v[2 * i]) : f32_to_bf16_bits(v[2 * i]);
+      uint32_t hi = kind == Q_FP16 ? f32_to_f16_bits(v[2 * i + 1]) : f32_to_bf16_bits(v[2 * i + 1]);
+      w[i] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+    uint32_t w[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      uint32_t b = kind == Q_FP8_E5M2 ? f32_to_e5m2(v[i]) : f32_to_e4m3(v[i]);
+      w[i >> 2] |= b << ((i & 3) * 8);
+    }
+    *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+  }
+}
+
+// per-tensor scale from the amax slot (float bits; amax >= 0)
+__device__ __forceinline__ float tensor_scale_from_amax(int kind, uint32_t amax_bits) {
+  const float amax = __uint_as_float(amax_bits);
+  float s = __fdiv_rn(amax, kind == Q_NVFP4_TENSOR ? 2688.0f : 448.0f);
+  if (!(s > 0.0f) || s == __uint_as_float(0x7f800000u)) s = 1.0f;
+  return s;
+}
+
+__device__ __forceinline__ float block_amax_reduce(float v) {
+  __shared__ float sm[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    v = threadIdx.x < (blockDim.x >> 5) ? sm[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  }
+  __syncthreads();
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Pass 2: the fused optimizer update over the chunk table.
+// ---------------------------------------------------------------------------
+struct UpdateArgs {
+  OptConsts oc;
+  int use_scaler;
+  const Chunk* chunks;
+  int nchunks;
+  const TensorDesc* tensors;
+  float* master;
+  float* s1;
+  float* s2;
+  const void* grad;
+  uint8_t* qout;
+  uint32_t* amax_slots;
+  const Decision* dec;
+};
+
+template <int GDT, int OPT>
+__global__ void __launch_bounds__(kThreads, 4) update_kernel(UpdateArgs a) {
+  __shared__ Fp4Thr s_mx[256];
+  __shared__ Fp4Thr s_nv[128];
+  __shared__ __align__(16) uint8_t stage[kNvTileBytes];
+  const Decision* dec = a.dec;
+  if (dec->skip) return;
+  const Divisor dv = make_divisor(unscale_divisor<GDT>(dec->scale_used));
+  const bool clipped = dec->clipped != 0;
+  const float coef = dec->coef;
+  load_thr_smem(s_mx, s_nv);
+  __syncthreads();
+  const OptConsts oc = a.oc;
+
+  for (int c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
+    const Chunk ch = a.chunks[c];
+    const TensorDesc td = a.tensors[ch.tensor];
+    const int kind = td.quant;
+    const bool tensor_scaled = (kind == Q_FP8_E4M3_TENSOR || kind == Q_NVFP4_TENSOR);
+    float amax = 0.0f;
+    const int64_t end = ch.start + ch.len;
+    for (int64_t tb = ch.start; tb < end; tb += kTile) {
+      const int64_t e0 = tb + (int64_t)threadIdx.x * kVec;
+      const bool act = e0 < end;
+      float p[8], m[8], v[8], g[8];
+      if (act) {
+        const float4* pp = reinterpret_cast<const float4*>(a.master + e0);
+        float4 p0 = pp[0], p1 = pp[1];
+        p[0] = p0.x; p[1] = p0.y; p[2] = p0.z; p[3] = p0.w;
+        p[4] = p1.x; p[5] = p1.y; p[6] = p1.z; p[7] = p1.w;
+        if (OPT != OPT_SGD || oc.use_mu) {
+          const float4* mp = reinterpret_cast<const float4*>(a.s1 + e0);
+          float4 m0 = __ldcs(mp), m1 = __ldcs(mp + 1);
+          m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w;
+          m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
+        }
+        if (OPT != OPT_SGD) {
+          const float4* vp = reinterpret_cast<const float4*>(a.s2 + e0);
+          float4 v0 = __ldcs(vp), v1 = __ldcs(vp + 1);
+          v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
+          v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
+        }
+        grad8<GDT>(a.grad, e0, a.use_scaler, dv, g);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+          float gk = clipped ? __fmul_rn(g[k], coef) : g[k];
+          if (OPT == OPT_SGD)
+            sgd_elem(p[k], gk, m[k], oc);
+          else if (OPT == OPT_ADAM)
+            adam_elem<false>(p[k], gk, m[k], v[k], oc);
+          else
+            adam_elem<true>(p[k], gk, m[k], v[k], oc);
+        }
+        float4* pw = reinterpret_cast<float4*>(a.master + e0);
+        pw[0] = make_float4(p[0], p[1], p[2], p[3]);
+        pw[1] = make_float4(p[4], p[5], p[6], p[7]);
+        if (OPT != OPT_SGD || oc.use_mu) {
+          float4* mw = reinterpret_cast<float4*>(a.s1 + e0);
+          __stcs(mw, make_float4(m[0], m[1], m[2], m[3]));
+          __stcs(mw + 1, make_float4(m[4], m[5], m[6], m[7]));
+        }
+        if (OPT != OPT_SGD) {
+          float4* vw = reinterpret_cast<float4*>(a.s2 + e0);
+          __stcs(vw, make_float4(v[0], v[1], v[2], v[3]));
+          __stcs(vw + 1, make_float4(v[4], v[5], v[6], v[7]));
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) p[k] = 0.0f;
+      }
+      // ---- requant epilogue (uniform per chunk) ----
+      if (kind == Q_NONE) continue;
+      const int64_t te = e0 - td.off;  // element offset within the tensor
+      if (tensor_scaled) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) amax = amax_acc(amax, p[k]);
+      } else if (kind == Q_MXFP4 || kind == Q_NVFP4) {
+        const int64_t tile_in_tensor = (tb - td.off) / kTile;
+        if (kind == Q_MXFP4) {
+          stage_mxfp4(p, stage, s_mx);
+          __syncthreads();
+          flush_stage(stage, kMxTileBytes, a.qout + td.qoff + tile_in_tensor * kMxTileBytes, kMxTileBytes);
+        } else {
+          stage_nvfp4(p, stage, s_nv);
+          __syncthreads();
+          flush_stage(stage, kNvTileBytes, a.qout + td.qoff + tile_in_tensor * kNvTileBytes, kNvTileBytes);
+        }
+        __syncthreads();
+      } else if (act) {
+        const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
+        store_elem8(kind, p, a.qout + td.qoff + te * esz);
+      }
+    }
+    if (tensor_scaled) {
+      float bm = block_amax_reduce(amax);
+      if (threadIdx.x == 0) atomicMax(&a.amax_slots[ch.tensor], __float_as_uint(bm));
+    }
+  }
+}
+
+template <int GDT, int OPT>
+static int grid_for_update(int device) {
+  int sms = 148, per = 4;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, update_kernel<GDT, OPT>, kThreads, 0);
+  if (per < 1) per = 1;
+  return sms * per;
+}
+
+int update_grid(int gdt, int opt, int device) {
+#define ODY_G(G, O) \
+  if (gdt == G && opt == O) return grid_for_update<G, O>(device);
+  ODY_G(DT_F32, OPT_SGD) ODY_G(DT_F32, OPT_ADAM) ODY_G(DT_F32, OPT_ADAMW)
+  ODY_G(DT_F16, OPT_SGD) ODY_G(DT_F16, OPT_ADAM) ODY_G(DT_F16, OPT_ADAMW)
+  ODY_G(DT_BF16, OPT_SGD) ODY_G(DT_BF16, OPT_ADAM) ODY_G(DT_BF16, OPT_ADAMW)
+#undef ODY_G
+  return 148;
+}
+
+cudaError_t launch_update(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
+                          int nchunks, const TensorDesc* tensors, float* master, float* s1, float* s2,
+                          const void* grad, uint8_t* qout, uint32_t* amax_slots, const Decision* dec,
+                          int grid, cudaStream_t st) {
+  UpdateArgs a{oc, use_scaler, chunks, nchunks, tensors, master, s1, s2, grad, qout, amax_slots, dec};
+#define ODY_L(G, O)                                                    \
+  if (gdt == G && opt == O) {                                          \
+    update_kernel<G, O><<<grid, kThreads, 0, st>>>(a);                 \
+    return cudaGetLastError();                                         \
+  }
+  ODY_L(DT_F32, OPT_SGD) ODY_L(DT_F32, OPT_ADAM) ODY_L(DT_F32, OPT_ADAMW)
+  ODY_L(DT_F16, OPT_SGD) ODY_L(DT_F16, OPT_ADAM) ODY_L(DT_F16, OPT_ADAMW)
+  ODY_L(DT_BF16, OPT_SGD) ODY_L(DT_BF16, OPT_ADAM) ODY_L(DT_BF16, OPT_ADAMW)
+#undef ODY_L
+  return cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------------------
+// Pass 3: per-tensor-scaled requant of the new master weights.
+// ---------------------------------------------------------------------------
+struct RequantArgs {
+  const Chunk* chunks;
+  int nchunks;
+  const TensorDesc* tensors;
+  const float* master;
+  uint8_t* qout;
+  const uint32_t* amax_slots;
+  float* qscale;
+  const Decision* dec;
+};
+
+__global__ void __launch_bounds__(kThreads, 4) requant_kernel(RequantArgs a) {
+  __shared__ Fp4Thr s_mx[256];
+  __shared__ Fp4Thr s_nv[128];
+  __shared__ __align__(16) uint8_t stage[kNvTileBytes];
+  if (a.dec->skip) return;
+  load_thr_smem(s_mx, s_nv);
+  __syncthreads();
+  for (int c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
+    const Chunk ch = a.chunks[c];
+    const TensorDesc td = a.tensors[ch.tensor];
+    const int kind = td.quant;
+    const float s = tensor_scale_from_amax(kind, __ldcg(&a.amax_slots[ch.tensor]));
+    if (ch.start == td.off && threadIdx.x == 0) a.qscale[ch.tensor] = s;
+    const int64_t end = ch.start + ch.len;
+    for (int64_t tb = ch.start; tb < end; tb += kTile) {
+      const int64_t e0 = tb + (int64_t)threadIdx.x * kVec;
+      const bool act = e0 < end;
+      float x[8];
+      if (act) {
+        const float4* pp = reinterpret_cast<const float4*>(a.master + e0);
+        float4 p0 = __ldcs(pp), p1 = __ldcs(pp + 1);
+        x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
+        x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
+#pragma unroll
+        for (int k = 0; k < 8; k++) x[k] = __fdiv_rn(x[k], s);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++) x[k] = 0.0f;
+      }
+      if (kind == Q_NVFP4_TENSOR) {
+        const int64_t tile_in_tensor = (tb - td.off) / kTile;
+        stage_nvfp4(x, stage, s_nv);
+        __syncthreads();
+        flush_stage(stage, kNvTileBytes, a.qout + td.qoff + tile_in_tensor * kNvTileBytes, kNvTileBytes);
+        __syncthreads();
+      } else if (act) {
+        store_elem8(Q_FP8_E4M3, x, a.qout + td.qoff + (e0 - td.off));
+      }
+    }
+  }
+}
+
+int requant_grid(int device) {
+  int sms = 148, per = 4;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, requant_kernel, kThreads, 0);
+  if (per < 1) per = 1;
+  return sms * per;
+}
+
+cudaError_t launch_requant(const Chunk* chunks, int nchunks, const TensorDesc* tensors,
+                           const float* master, uint8_t* qout, const uint32_t* amax_slots,
+                           float* qscale, const Decision* dec, int grid, cudaStream_t st) {
+  if (nchunks == 0) return cudaSuccess;
+  RequantArgs a{chunks, nchunks, tensors, master, qout, amax_slots, qscale, dec};
+  requant_kernel<<<grid, kThreads, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Standalone quantise / dequantise of one tensor (AnyTensor.to_* / from_*,
+// src/odyssey/tensor/tensor_dtype_conv.mojo:13-494).  Source float32 or
+// bfloat16 (exact upcast first).  n is arbitrary; the last block is zero
+// padded as in the reference (tensor_dtype_conv.mojo:306-307).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void load_src8(int sdt, const void* x, int64_t n, int64_t e0, float v[8]) {
+  if (e0 + 8 <= n) {
+    if (sdt == DT_F32) {
+      const float* p = reinterpret_cast<const float*>(x) + e0;
+      if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+        float4 a = __ldcs(reinterpret_cast<const float4*>(p)), b = __ldcs(reinterpret_cast<const float4*>(p) + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        return;
+      }
+    } else {
+      const uint16_t* p = reinterpret_cast<const uint16_t*>(x) + e0;
+      if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+        uint4 r = __ldcs(reinterpret_cast<const uint4*>(p));
+        uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = bf16_bits_to_f32((uint16_t)(w[k >> 1] >> ((k & 1) * 16)));
+        return;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const int64_t i = e0 + k;
+    float val = 0.0f;
+    if (i < n)
+      val = sdt == DT_F32 ? reinterpret_cast<const float*>(x)[i]
+                          : bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(x)[i]);
+    v[k] = val;
+  }
+}
+
+__global__ void amax_kernel(int sdt, const void* x, int64_t n, uint32_t* out) {
+  float am = 0.0f;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 8;
+  for (int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; e0 < n; e0 += stride) {
+    float v[8];
+    load_src8(sdt, x, n, e0, v);
+#pragma unroll
+    for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
+  }
+  am = block_amax_reduce(am);
+  if (threadIdx.x == 0) atomicMax(out, __float_as_uint(am));
+}
+
+static int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+cudaError_t launch_amax(int sdt, const void* x, int64_t n, uint32_t* amax, cudaStream_t st) {
+  int64_t groups = (n + 7) / 8;
+  int64_t want = (groups + kThreads - 1) / kThreads;
+  int grid = (int)(want < (int64_t)sm_count() * 8 ? want : (int64_t)sm_count() * 8);
+  if (grid < 1) grid = 1;
+  amax_kernel<<<grid, kThreads, 0, st>>>(sdt, x, n, amax);
+  return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, int sdt, const void* x, int64_t n,
+                                                            uint8_t* out, int64_t out_bytes,
+                                                            const uint32_t* amax, float* tscale) {
+  __shared__ Fp4Thr s_mx[256];
+  __shared__ Fp4Thr s_nv[128];
+  __shared__ __align__(16) uint8_t stage[kNvTileBytes];
+  load_thr_smem(s_mx, s_nv);
+  __syncthreads();
+  const bool scaled = (kind == Q_NVFP4_TENSOR || kind == Q_FP8_E4M3_TENSOR);
+  const float s = scaled ? tensor_scale_from_amax(kind, *amax) : 1.0f;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && tscale) *tscale = s;
+  const int64_t ntiles = (n + kTile - 1) / kTile;
+  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int64_t e0 = t * kTile + (int64_t)threadIdx.x * kVec;
+    float v[8];
+    load_src8(sdt, x, n, e0, v);
+    if (scaled) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) v[k] = __fdiv_rn(v[k], s);
+    }
+    if (kind == Q_MXFP4 || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
+      const int tb = kind == Q_MXFP4 ? kMxTileBytes : kNvTileBytes;
+      if (kind == Q_MXFP4)
+        stage_mxfp4(v, stage, s_mx);
+      else
+        stage_nvfp4(v, stage, s_nv);
+      __syncthreads();
+      const int64_t off = t * tb;
+      flush_stage(stage, tb, out + off, out_bytes - off);
+      __syncthreads();
+    } else {
+      const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
+      const int qk = kind == Q_FP8_E4M3_TENSOR ? Q_FP8_E4M3 : kind;
+      uint8_t* dst = out + e0 * esz;
+      if (e0 + 8 <= n && (reinterpret_cast<uintptr_t>(dst) & (esz == 2 ? 15u : 7u)) == 0) {
+        store_elem8(qk, v, dst);
+      } else {
+        for (int k = 0; k < 8 && e0 + k < n; k++) {
+          if (esz == 2) {
+            uint16_t h = qk == Q_FP16 ? f32_to_f16_bits(v[k]) : f32_to_bf16_bits(v[k]);
+            reinterpret_cast<uint16_t*>(out)[e0 + k] = h;
+          } else {
+            out[e0 + k] = qk == Q_FP8_E5M2 ? f32_to_e5m2(v[k]) : f32_to_e4m3(v[k]);
+          }
+        }
+      }
+    }
+  }
+}
+
+static int64_t quant_bytes_dev(int kind, int64_t n) {
+  switch (kind) {
+    case Q_FP16:
+    case Q_BF16:
+      return 2 * n;
+    case Q_FP8_E4M3:
+    case Q_FP8_E5M2:
+    case Q_FP8_E4M3_TENSOR:
+      return n;
+    case Q_MXFP4:
+      return ((n + 31) / 32) * 17;
+    case Q_NVFP4:
+    case Q_NVFP4_TENSOR:
+      return ((n + 15) / 16) * 9;
+  }
+  return 0;
+}
+
+cudaError_t launch_quantize(int kind, int sdt, const void* x, int64_t n, uint8_t* out,
+                            const uint32_t* amax, float* tscale, cudaStream_t st) {
+  int64_t ntiles = (n + kTile - 1) / kTile;
+  int64_t cap = (int64_t)sm_count() * 6;
+  int grid = (int)(ntiles < cap ? ntiles : cap);
+  if (grid < 1) grid = 1;
+  quantize_kernel<<<grid, kThreads, 0, st>>>(kind, sdt, x, n, out, quant_bytes_dev(kind, n), amax,
+                                             tscale);
+  return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(kThreads) dequantize_kernel(int kind, const uint8_t* q, int64_t n,
+                                                              int64_t qbytes, const float* tscale,
+                                                              float* out) {
+  __shared__ __align__(16) uint8_t stage[kNvTileBytes];
+  const float ts = tscale ? *tscale : 1.0f;
+  const bool scaled = (kind == Q_NVFP4_TENSOR || kind == Q_FP8_E4M3_TENSOR);
+  const int64_t ntiles = (n + kTile - 1) / kTile;
+  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int64_t e0 = t * kTile + (int64_t)threadIdx.x * kVec;
+    float v[8];
+    if (kind == Q_MXFP4 || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
+      const int tb = kind == Q_MXFP4 ? kMxTileBytes : kNvTileBytes;
+      const int64_t off = t * tb;
+      const int64_t lim = qbytes - off < tb ? qbytes - off : tb;
+      for (int i = threadIdx.x; i < lim; i += blockDim.x) stage[i] = q[off + i];
+      __syncthreads();
+      if (kind == Q_MXFP4) {
+        const int blk = threadIdx.x >> 2, j = threadIdx.x & 3;
+        const float sf = (blk * 17 + 16 < lim) ? e8m0_to_f32(stage[blk * 17 + 16]) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint8_t b = (blk * 17 + 4 * j + i < lim) ? stage[blk * 17 + 4 * j + i] : 0;
+          v[2 * i] = fp4_decode(b >> 4, sf);
+          v[2 * i + 1] = fp4_decode(b & 15, sf);
+        }
+      } else {
+        const int blk = threadIdx.x >> 1, j = threadIdx.x & 1;
+        const float sf = (blk * 9 + 8 < lim) ? e4m3_to_f32(stage[blk * 9 + 8]) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint8_t b = (blk * 9 + 4 * j + i < lim) ? stage[blk * 9 + 4 * j + i] : 0;
+          v[2 * i] = fp4_decode(b >> 4, sf);
+          v[2 * i + 1] = fp4_decode(b & 15, sf);
+        }
+      }
+      __syncthreads();
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int64_t i = e0 + k;
+        float val = 0.0f;
+        if (i < n) {
+          if (kind == Q_FP16)
+            val = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(q)[i]);
+          else if (kind == Q_BF16)
+            val = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(q)[i]);
+          else if (kind == Q_FP8_E5M2)
+            val = e5m2_to_f32(q[i]);
+          else
+            val = e4m3_to_f32(q[i]);
+        }
+        v[k] = val;
+      }
+    }
+    if (scaled) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) v[k] = __fmul_rn(v[k], ts);
+    }
+    float* dst = out + e0;
+    if (e0 + 8 <= n && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+      __stcs(reinterpret_cast<float4*>(dst), make_float4(v[0], v[1], v[2], v[3]));
+      __stcs(reinterpret_cast<float4*>(dst) + 1, make_float4(v[4], v[5], v[6], v[7]));
+    } else {
+      for (int k = 0; k < 8 && e0 + k < n; k++) dst[k] = v[k];
+    }
+  }
+}
+
+cudaError_t launch_dequantize(int kind, const uint8_t* q, int64_t n, const float* tscale, float* out,
+                              cudaStream_t st) {
+  int64_t ntiles = (n + kTile - 1) / kTile;
+  int64_t cap = (int64_t)sm_count() * 6;
+  int grid = (int)(ntiles < cap ? ntiles : cap);
+  if (grid < 1) grid = 1;
+  dequantize_kernel<<<grid, kThreads, 0, st>>>(kind, q, n, quant_bytes_dev(kind, n), tscale, out);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Single-op kernels (the reference's separate API functions).
+// ---------------------------------------------------------------------------
+__global__ void unscale_kernel(int dt, const void* g, int64_t n, float scale, void* out) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    if (dt == DT_F32) {
+      reinterpret_cast<float*>(out)[i] = __fdiv_rn(reinterpret_cast<const float*>(g)[i], scale);
+    } else if (dt == DT_F16) {
+      const float d = unscale_divisor<DT_F16>(scale);
+      float x = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(g)[i]);
+      reinterpret_cast<uint16_t*>(out)[i] = f32_to_f16_bits(__fdiv_rn(x, d));
+    } else {
+      const float d = unscale_divisor<DT_BF16>(scale);
+      float x = bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(g)[i]);
+      reinterpret_cast<uint16_t*>(out)[i] = f32_to_bf16_bits(__fdiv_rn(x, d));
+    }
+  }
+}
+
+static int grid_for(int64_t n) {
+  int64_t want = (n + kThreads - 1) / kThreads;
+  int64_t cap = (int64_t)sm_count() * 8;
+  int g = (int)(want < cap ? want : cap);
+  return g < 1 ? 1 : g;
+}
+
+cudaError_t launch_unscale(int dt, const void* g, int64_t n, float scale, void* out, cudaStream_t st) {
+  unscale_kernel<<<grid_for(n), kThreads, 0, st>>>(dt, g, n, scale, out);
+  return cudaGetLastError();
+}
+
+__global__ void nonfinite_kernel(int dt, const void* g, int64_t n, unsigned long long* count) {
+  long long c = 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float x = dt == DT_F32 ? reinterpret_cast<const float*>(g)[i]
+              : dt == DT_F16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t*>(g)[i])
+                             : bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(g)[i]);
+    c += !is_finite_f(x);
+  }
+  c = warp_sum(c);
+  if ((threadIdx.x & 31) == 0 && c) atomicAdd(count, (unsigned long long)c);
+}
+
+cudaError_t launch_count_nonfinite(int dt, const void* g, int64_t n, unsigned long long* count,
+                                   cudaStream_t st) {
+  nonfinite_kernel<<<grid_for(n), kThreads, 0, st>>>(dt, g, n, count);
+  return cudaGetLastError();
+}
+
+// sum of float32 squares in float64, per-CTA partials + fixed-order final sum
+__global__ void sumsq_kernel(const float* g, int64_t n, StatsPartial* partials, unsigned* ticket,
+                             double* total) {
+  double acc = 0.0;
+  long long dummy = 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float x = g[i];
+    acc += (double)__fmul_rn(x, x);
+  }
+  block_sum2(acc, dummy);
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x].sumsq = acc;
+    __threadfence();
+    last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  double s = 0.0;
+  long long c = 0;
+  for (int j = threadIdx.x; j < (int)gridDim.x; j += blockDim.x) s += __ldcg(&partials[j].sumsq);
+  block_sum2(s, c);
+  if (threadIdx.x == 0) {
+    *total += s;  // accumulated over the tensors of one call, in call order
+    *ticket = 0u;
+  }
+}
+
+cudaError_t launch_sumsq(const float* g, int64_t n, StatsPartial* partials, int grid, unsigned* ticket,
+                         double* total, cudaStream_t st) {
+  sumsq_kernel<<<grid, kThreads, 0, st>>>(g, n, partials, ticket, total);
+  return cudaGetLastError();
+}
+
+// clip_gradients_by_global_norm (gradient_clipping.mojo:310-352)
+__global__ void clip_coef_kernel(const double* total, float max_norm, float* norm_out, float* coef_out) {
+  const float norm = __double2float_rn(__dsqrt_rn(*total));
+  *norm_out = norm;
+  *coef_out = norm > max_norm
+                  ? __double2float_rn(__ddiv_rn((double)max_norm, __dadd_rn((double)norm, 1e-6)))
+                  : 1.0f;
+}
+
+cudaError_t launch_clip_coef(const double* total, float max_norm, float* norm_out, float* coef_out,
+                             cudaStream_t st) {
+  clip_coef_kernel<<<1, 1, 0, st>>>(total, max_norm, norm_out, coef_out);
+  return cudaGetLastError();
+}
+
+__global__ void scale_kernel(float* g, int64_t n, const float* coef) {
+  const float c = *coef;
+  if (c == 1.0f) return;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    g[i] = __fmul_rn(g[i], c);
+}
+
+cudaError_t launch_scale_inplace(float* g, int64_t n, const float* coef, cudaStream_t st) {
+  scale_kernel<<<grid_for(n), kThreads, 0, st>>>(g, n, coef);
+  return cudaGetLastError();
+}
+
+template <int OPT>
+__global__ void opt_kernel(OptConsts oc, const float* p, const float* g, const float* s1, const float* s2,
+                           int64_t n, float* op, float* os1, float* os2) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float pp = p[i];
+    if (OPT == OPT_SGD) {
+      float vel = s1 ? s1[i] : 0.0f;
+      sgd_elem(pp, g[i], vel, oc);
+      if (os1) os1[i] = vel;
+    } else {
+      float m = s1[i], v = s2[i];
+      adam_elem<OPT == OPT_ADAMW>(pp, g[i], m, v, oc);
+      os1[i] = m;
+      os2[i] = v;
+    }
+    op[i] = pp;
+  }
+}
+
+cudaError_t launch_opt_step(int opt, const OptConsts& oc, const float* p, const float* g, const float* s1,
+                            const float* s2, int64_t n, float* op, float* os1, float* os2, cudaStream_t st) {
+  if (opt == OPT_SGD)
+    opt_kernel<OPT_SGD><<<grid_for(n), kThreads, 0, st>>>(oc, p, g, s1, s2, n, op, os1, os2);
+  else if (opt == OPT_ADAM)
+    opt_kernel<OPT_ADAM><<<grid_for(n), kThreads, 0, st>>>(oc, p, g, s1, s2, n, op, os1, os2);
+  else
+    opt_kernel<OPT_ADAMW><<<grid_for(n), kThreads, 0, st>>>(oc, p, g, s1, s2, n, op, os1, os2);
+  return cudaGetLastError();
+}
+
+}  // namespace ody

@@ -1,0 +1,105 @@
+"""Mirror of AnyTensor.to_/from_{fp8,bf8,mxfp4,nvfp4}
+(src/odyssey/tensor/any_tensor.mojo:1946-2427, tensor_dtype_conv.mojo:13-494)
+over libodyssey_mp.so.
+
+A quantised tensor is a flat uint8 buffer in the reference's layout (FP8:
+one byte per element; MXFP4: 17-byte blocks of 16 code bytes + 1 E8M0
+byte; NVFP4: 9-byte blocks of 8 code bytes + 1 E4M3 byte; element 2i in
+the high nibble) plus the original element count
+(AnyTensor._original_numel_quantized, any_tensor.mojo:140) and, for the
+per-tensor-scaled kinds, the float32 tensor scale.
+"""
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib as L
+
+
+@dataclass
+class QuantizedTensor:
+    data: object          # uint8 buffer (numpy array or torch tensor)
+    kind: int
+    original_numel: int
+    tensor_scale: float = 1.0
+
+
+def quantize(x, kind, dtype=None):
+    """x: float32 or bfloat16 (torch bfloat16, or numpy uint16 with dtype='bfloat16')."""
+    code = L.dtype_code(x, dtype)
+    if code == L.F16:
+        # the reference accepts float16 sources by an exact upcast
+        from .mixed_precision import convert_to_fp32_master
+        x, code = convert_to_fp32_master(x), L.F32
+    n = L.numel(x)
+    if n == 0:
+        raise L.OdysseyError("cannot quantize an empty tensor", L.ERR_SHAPE)
+    src = L.contiguous(x)
+    out = L.empty_like(src, "uint8", L.quant_bytes(kind, n))
+    ts = C.c_float(1.0)
+    L.check(L.lib().ody_quantize(kind, L.ptr(src), code, n, L.ptr(out), C.byref(ts)))
+    return QuantizedTensor(out, kind, n, ts.value)
+
+
+def dequantize(q):
+    """QuantizedTensor -> float32 values (1-D, original_numel long)."""
+    need = L.quant_bytes(q.kind, q.original_numel)
+    if L.numel(q.data) != need:
+        raise L.OdysseyError(f"quantised buffer has {L.numel(q.data)} bytes, expected {need}", L.ERR_SHAPE)
+    data = L.contiguous(q.data)
+    out = L.empty_like(data, "float32", q.original_numel)
+    L.check(L.lib().ody_dequantize(q.kind, L.ptr(data), q.original_numel, q.tensor_scale, L.ptr(out)))
+    return out
+
+
+def to_fp8(x, dtype=None):
+    return quantize(x, L.Q_FP8_E4M3, dtype)
+
+
+def to_bf8(x, dtype=None):
+    return quantize(x, L.Q_FP8_E5M2, dtype)
+
+
+def to_fp8_tensor_scaled(x, dtype=None):
+    return quantize(x, L.Q_FP8_E4M3_TENSOR, dtype)
+
+
+def to_mxfp4(x, dtype=None):
+    return quantize(x, L.Q_MXFP4, dtype)
+
+
+def to_nvfp4(x, dtype=None):
+    return quantize(x, L.Q_NVFP4, dtype)
+
+
+def to_nvfp4_tensor_scaled(x, dtype=None):
+    return quantize(x, L.Q_NVFP4_TENSOR, dtype)
+
+
+def _from(q, kind, block, what):
+    if isinstance(q, QuantizedTensor):
+        return dequantize(q)
+    nbytes = L.numel(q)
+    if block and nbytes % block:
+        raise L.OdysseyError(f"{what} tensor size must be multiple of {block} bytes", L.ERR_SHAPE)
+    n = nbytes // block * (32 if block == 17 else 16) if block else nbytes
+    return dequantize(QuantizedTensor(q, kind, n))
+
+
+def from_fp8(q):
+    return _from(q, L.Q_FP8_E4M3, 0, "FP8")
+
+
+def from_bf8(q):
+    return _from(q, L.Q_FP8_E5M2, 0, "BF8")
+
+
+def from_mxfp4(q):
+    """tensor_dtype_conv.mojo:369-430 (padded length when the original numel is unknown)."""
+    return _from(q, L.Q_MXFP4, 17, "MXFP4")
+
+
+def from_nvfp4(q):
+    """tensor_dtype_conv.mojo:433-494."""
+    return _from(q, L.Q_NVFP4, 9, "NVFP4")

@@ -1,0 +1,215 @@
+"""GPU parity of the fused step (MixedPrecisionStep -> ody_step) against the
+oracle's restatement of the reference call sequence: master weights and
+optimizer states within 2 float32 ulp (they come out bit-identical), quantised
+codes and scales bit-exact, skip/backoff decisions identical."""
+import numpy as np
+import pytest
+
+from odyssey_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+GDT = {"float32": 0, "float16": 1, "bfloat16": 2}
+OPT = {"sgd": 0, "adam": 1, "adamw": 2}
+QK = {"none": 0, "fp16": 1, "bf16": 2, "fp8": 3, "bf8": 4, "fp8_tensor": 5, "mxfp4": 6, "nvfp4": 7,
+      "nvfp4_tensor": 8}
+
+
+def ulp_diff(a, b):
+    ai = a.view(np.int32).astype(np.int64)
+    bi = b.view(np.int32).astype(np.int64)
+    ai = np.where(ai < 0, -(ai & 0x7FFFFFFF), ai)
+    bi = np.where(bi < 0, -(bi & 0x7FFFFFFF), bi)
+    return np.abs(ai - bi)
+
+
+def run_pair(oracle, wl, nsteps, numels=None, quants=None, seed=0, t0=1, check_every=1):
+    """Run the same workload through the GPU context and the oracle."""
+    from odyssey_b200 import MixedPrecisionStep
+    numels = numels or wl.numels
+    kw = wl.step_kwargs()
+    if quants is not None:
+        kw["quant"] = quants
+    qlist = kw["quant"] if isinstance(kw["quant"], list) else [kw["quant"]] * len(numels)
+    ctx = MixedPrecisionStep(numels, **kw)
+    specs = [{"numel": n, "grad_dtype": GDT[wl.grad_dtype], "quant": QK[q]} for n, q in zip(numels, qlist)]
+    hy = wl.hyper
+    sk = {k: kw[k] for k in ("initial_scale", "growth_factor", "backoff_factor", "growth_interval", "min_scale",
+                             "max_scale") if k in kw}
+    model = oracle.Model(specs, OPT[wl.optimizer], hy["learning_rate"], momentum=hy.get("momentum", 0.0),
+                         beta1=hy.get("beta1", 0.9), beta2=hy.get("beta2", 0.999), epsilon=hy.get("epsilon", 1e-8),
+                         weight_decay=hy.get("weight_decay", 0.0), clip_enabled=wl.clip is not None,
+                         max_norm=wl.clip or 1.0, scaler_kwargs=sk)
+    master = wl.master(seed, numels)
+    for i, m in enumerate(master):
+        ctx.set_master(i, m)
+        model.master[i][:] = m
+    t = t0
+    results = []
+    for s in range(nsteps):
+        grads = wl.grads(s, seed + 1, numels)
+        for i, g in enumerate(grads):
+            ctx.set_grad(i, g)
+        r = ctx.step(t)
+        ro = model.step(grads, t)
+        results.append((r, ro))
+        assert r["skipped"] == ro.skipped, s
+        assert r["nonfinite_count"] == ro.nonfinite, s
+        assert r["scale_used"] == ro.scale_used and r["scale_next"] == ro.scale_next, s
+        assert r["step_count"] == ro.step_count and r["overflow_count"] == ro.overflow_count
+        assert r["clipped"] == ro.clipped, s
+        assert abs(r["sumsq"] - ro.sumsq) <= 1e-12 * max(ro.sumsq, 1e-300), s
+        assert r["grad_norm"] == ro.norm and r["clip_coef"] == ro.coef, s
+        if not r["skipped"] and wl.optimizer != "sgd":
+            t += 1
+        if (s + 1) % check_every == 0 or s == nsteps - 1:
+            compare_state(ctx, model, numels, qlist, wl.optimizer)
+    return ctx, model, results
+
+
+def compare_state(ctx, model, numels, qlist, optimizer):
+    for i in range(len(numels)):
+        d = ulp_diff(ctx.master(i), model.master[i])
+        assert d.max() <= 2, (i, d.max())
+        if optimizer != "sgd" or model.cfg.momentum > 0:
+            assert ulp_diff(ctx.state(i, 0), model.s1[i]).max() <= 2, i
+        if optimizer != "sgd":
+            assert ulp_diff(ctx.state(i, 1), model.s2[i]).max() <= 2, i
+        if QK[qlist[i]] != 0:
+            q = ctx.get_quant(i)
+            nb = q.data.size
+            np.testing.assert_array_equal(q.data, model.qout[i][:nb], err_msg=f"tensor {i}")
+            assert np.float32(q.tensor_scale) == model.qscale[i][0]
+
+
+def test_lenet_sgd_fp16_100_steps(oracle):
+    """Config 1 at full size: 100 steps, seed 0, FP16 grads x 1024."""
+    ctx, model, res = run_pair(oracle, W.lenet(), 100, check_every=25)
+    ctx.close()
+
+
+def test_lenet_with_overflow_steps(oracle):
+    wl = W.lenet()
+    wl.inf_every = 3
+    ctx, model, res = run_pair(oracle, wl, 10)
+    assert sum(r["skipped"] for r, _ in res) == 3
+    ctx.close()
+
+
+def test_resnet18_adamw_fp8_tensor(oracle):
+    """Config 4 at full size (62 tensors), with the inf injection every 100th
+    step exercised by a shortened interval."""
+    wl = W.resnet18()
+    wl.inf_every = 4
+    ctx, model, res = run_pair(oracle, wl, 9, check_every=3)
+    assert [r["skipped"] for r, _ in res] == [0, 0, 0, 0, 1, 0, 0, 0, 1]
+    ctx.close()
+
+
+def test_flat_adamw_clip_nvfp4_tensor_small(oracle):
+    """Config 5's path (AdamW + global-norm clip + NVFP4 per-tensor scale) on
+    4 tensors of 512x512."""
+    wl = W.flat1b(ntensors=4, side=512)
+    ctx, model, res = run_pair(oracle, wl, 4)
+    assert all(r["clipped"] for r, _ in res)
+    ctx.close()
+
+
+@pytest.mark.parametrize("opt", ["sgd", "adam", "adamw"])
+@pytest.mark.parametrize("gdt", ["float32", "float16", "bfloat16"])
+def test_all_kinds_all_optimizers(oracle, opt, gdt):
+    """Every re-quantisation kind in one model, ragged tensor sizes."""
+    wl = W.Workload("mix", [(1,), (15,), (33,), (2049,), (5000,), (16384 + 64,), (40000,), (7,), (100,)],
+                    gdt, "none", opt,
+                    dict(learning_rate=1e-2, momentum=0.9, weight_decay=0.01) if opt == "sgd" else
+                    dict(learning_rate=1e-3, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.01),
+                    0.05, 1e-3, 256.0, clip=0.05)
+    quants = ["fp16", "bf16", "fp8", "bf8", "fp8_tensor", "mxfp4", "nvfp4", "nvfp4_tensor", "none"]
+    ctx, model, res = run_pair(oracle, wl, 3, quants=quants)
+    ctx.close()
+
+
+def test_no_scaler_no_clip(oracle):
+    wl = W.Workload("plain", [(3000,), (77,)], "float32", "mxfp4", "adam",
+                    dict(learning_rate=1e-3, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.0),
+                    0.05, 1e-3, 1.0)
+    from odyssey_b200 import MixedPrecisionStep
+    kw = wl.step_kwargs()
+    kw["use_gradient_scaler"] = False
+    ctx = MixedPrecisionStep(wl.numels, **kw)
+    specs = [{"numel": n, "grad_dtype": 0, "quant": 6} for n in wl.numels]
+    model = oracle.Model(specs, 1, 1e-3, use_scaler=False)
+    for i, m in enumerate(wl.master(0)):
+        ctx.set_master(i, m)
+        model.master[i][:] = m
+    for s in range(3):
+        g = wl.grads(s)
+        for i, x in enumerate(g):
+            ctx.set_grad(i, x)
+        r = ctx.step(s + 1)
+        ro = model.step(g, s + 1)
+        assert r["scale_used"] == ro.scale_used
+    compare_state(ctx, model, wl.numels, ["mxfp4"] * 2, "adam")
+    ctx.close()
+
+
+def test_checkpoint_resume_bit_identical(oracle):
+    """Export mid-run, continue, import, replay: identical to uninterrupted."""
+    from odyssey_b200 import MixedPrecisionStep
+    wl = W.flat1b(ntensors=3, side=256)
+    kw = wl.step_kwargs()
+    ctx = MixedPrecisionStep(wl.numels, **kw)
+    for i, m in enumerate(wl.master(0)):
+        ctx.set_master(i, m)
+
+    def run(steps, t0):
+        for s in steps:
+            for i, g in enumerate(wl.grads(s)):
+                ctx.set_grad(i, g)
+            ctx.step(t0 + s)
+
+    run(range(2), 1)
+    blob = ctx.export_state()
+    run(range(2, 5), 1)
+    final = [ctx.master(i) for i in range(3)]
+    codes = [ctx.get_quant(i).data for i in range(3)]
+    ctx.import_state(blob)
+    run(range(2, 5), 1)
+    for i in range(3):
+        np.testing.assert_array_equal(ctx.master(i), final[i])
+        np.testing.assert_array_equal(ctx.get_quant(i).data, codes[i])
+    ctx.close()
+
+
+def test_step_errors():
+    from odyssey_b200 import MixedPrecisionStep, OdysseyError
+    ctx = MixedPrecisionStep([100], grad_dtype="float32", optimizer="adamw")
+    with pytest.raises(OdysseyError, match="Timestep t must be positive"):
+        ctx.step(0)
+    with pytest.raises(OdysseyError, match="size mismatch"):
+        ctx.set_master(0, np.zeros(99, np.float32))
+    ctx.close()
+
+
+def test_async_pipeline_matches_sync(oracle):
+    """ody_step_async + ody_upload_async (pinned host) gives the same state as
+    synchronous steps."""
+    from odyssey_b200 import MixedPrecisionStep
+    wl = W.flat1b(ntensors=2, side=512)
+    a = MixedPrecisionStep(wl.numels, **wl.step_kwargs())
+    b = MixedPrecisionStep(wl.numels, **wl.step_kwargs())
+    for i, m in enumerate(wl.master(0)):
+        a.set_master(i, m)
+        b.set_master(i, m)
+    for s in range(3):
+        gs = wl.grads(s)
+        for i, g in enumerate(gs):
+            a.set_grad(i, g)
+            b.set_grad(i, g, sync=False)
+        a.step(s + 1)
+        b.step_async(s + 1)
+        b.wait()
+    for i in range(2):
+        np.testing.assert_array_equal(a.master(i), b.master(i))
+    a.close()
+    b.close()

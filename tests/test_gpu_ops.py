@@ -1,0 +1,135 @@
+"""GPU parity of the single-op entry points (unscale, finite check, global-
+norm clip, SGD / Adam / AdamW) against the oracle and the reference's golden
+vectors."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ody():
+    import odyssey_b200 as o
+    o.lib()
+    return o
+
+
+def _rand(n, seed, scale=1.0):
+    return (np.random.default_rng(seed).standard_normal(n) * scale).astype(np.float32)
+
+
+@pytest.mark.parametrize("name", ["sgd", "adam", "adamw"])
+def test_golden_vectors_f32(ody, golden, name):
+    """The reference's float64 golden vectors, through the float32 kernels:
+    within float32 rounding of the 1e-9 float64 answers."""
+    c = golden["optimizer_parity"][name]
+    f = lambda k: np.array(c[k], np.float32)  # noqa: E731
+    if name == "sgd":
+        p, v = ody.sgd_step(f("params"), f("grad"), f("velocity"), c["lr"], c["momentum"], c["weight_decay"])
+        np.testing.assert_allclose(v, c["new_velocity"], rtol=2e-6, atol=1e-8)
+    else:
+        fn = ody.adam_step if name == "adam" else ody.adamw_step
+        p, m, v = fn(f("params"), f("grad"), f("m"), f("v"), c["t"], c["lr"], c["beta1"], c["beta2"],
+                     c["epsilon"], c["weight_decay"])
+        np.testing.assert_allclose(m, c["new_m"], rtol=2e-6, atol=1e-9)
+        np.testing.assert_allclose(v, c["new_v"], rtol=2e-6, atol=1e-12)
+    np.testing.assert_allclose(p, c["new_params"], rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("n", [1, 7, 1000, 65537])
+@pytest.mark.parametrize("wd", [0.0, 0.01])
+def test_optimizers_bit_exact(ody, oracle, n, wd):
+    p, g, m = _rand(n, 1, 0.05), _rand(n, 2, 1e-3), _rand(n, 3, 1e-3)
+    v = np.abs(_rand(n, 4, 1e-6))
+    a = ody.sgd_step(p, g, m, 0.01, 0.9, wd)
+    b = oracle.sgd_step(p, g, m, 0.01, 0.9, wd)
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x.view(np.uint32), y.view(np.uint32))
+    for t in (1, 7, 1000):
+        a = ody.adam_step(p, g, m, v, t, 1e-3, 0.9, 0.999, 1e-8, wd)
+        b = oracle.adam_step(p, g, m, v, t, 1e-3, 0.9, 0.999, 1e-8, wd)
+        for x, y in zip(a, b):
+            np.testing.assert_array_equal(x.view(np.uint32), y.view(np.uint32))
+        a = ody.adamw_step(p, g, m, v, t, 1e-3, 0.9, 0.999, 1e-8, wd)
+        b = oracle.adamw_step(p, g, m, v, t, 1e-3, 0.9, 0.999, 1e-8, wd)
+        for x, y in zip(a, b):
+            np.testing.assert_array_equal(x.view(np.uint32), y.view(np.uint32))
+
+
+def test_optimizer_errors(ody):
+    z = np.zeros(4, np.float32)
+    with pytest.raises(ody.OdysseyError, match="Timestep t must be positive"):
+        ody.adamw_step(z, z, z, z, 0, 1e-3)
+    with pytest.raises(ody.OdysseyError, match="Velocity buffer required"):
+        ody.sgd_step(z, z, None, 0.1, momentum=0.9)
+    with pytest.raises(ody.OdysseyError, match="same shape"):
+        ody.sgd_step(z, np.zeros(5, np.float32), z, 0.1)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+def test_unscale_and_check(ody, oracle, dtype):
+    from odyssey_b200.workloads import f32_to_bf16_bits
+    x = _rand(10001, 9, 1024.0)
+    x[5] = np.float32(70000.0)
+    code = {"float32": 0, "float16": 1, "bfloat16": 2}[dtype]
+    g = x if dtype == "float32" else (x.astype(np.float16) if dtype == "float16" else f32_to_bf16_bits(x))
+    s = ody.GradientScaler(initial_scale=1024.0)
+    out = s.unscale_gradients(g, dtype=dtype if dtype == "bfloat16" else None)
+    want = oracle.unscale(g, 1024.0, dtype=code)
+    np.testing.assert_array_equal(np.asarray(out).view(np.uint8), want.view(np.uint8))
+    ok = ody.check_gradients_finite(g, dtype=dtype if dtype == "bfloat16" else None)
+    assert ok == (oracle.count_nonfinite(g, dtype=code) == 0)
+    # NaN / +-Inf detection (test_mixed_precision.mojo:209-286)
+    for bad in ("nan", "inf", "-inf"):
+        gb = g.copy()
+        gb[3] = {"float32": np.float32(bad), "float16": np.float16(bad),
+                 "bfloat16": f32_to_bf16_bits(np.float32([bad]))[0]}[dtype]
+        assert not ody.check_gradients_finite(gb, dtype=dtype if dtype == "bfloat16" else None)
+
+
+def test_unscale_fp16_scale_overflow(ody, oracle):
+    """full(F64(65536), float16) is +inf: g/inf = 0 and inf/inf = NaN, as the reference."""
+    g = np.float16([1.0, -2.0, np.inf, 0.0])
+    s = ody.GradientScaler()
+    out = s.unscale_gradients(g)
+    want = oracle.unscale(g, 65536.0)
+    np.testing.assert_array_equal(out.view(np.uint16)[:2], want.view(np.uint16)[:2])
+    assert np.isnan(out[2]) and np.isnan(want[2])
+
+
+def test_global_norm_clip_cases(ody, golden):
+    for case in golden["clip_cases"]["global_norm"]:
+        grads = [np.full(n, v, np.float32) for v, n in case["tensors"]]
+        norm = ody.clip_gradients_by_global_norm(grads, case["max_norm"])
+        assert abs(norm - case["expect_norm"]) <= case["atol"], case["name"]
+        if "expect_first" in case:
+            assert abs(grads[0][0] - case["expect_first"]) <= case["atol_value"], case["name"]
+        if "expect_new_norm" in case:
+            assert abs(ody.compute_gradient_norm_list(grads) - case["expect_new_norm"]) <= case["atol_new_norm"]
+    c = golden["clip_cases"]["by_norm"][0]
+    out = ody.clip_gradients_by_norm(np.float32(c["values"]), c["max_norm"])
+    np.testing.assert_allclose(out, c["expect"], atol=c["atol"])
+    with pytest.raises(ody.OdysseyError, match="max_norm must be positive"):
+        ody.clip_gradients_by_global_norm([np.zeros(3, np.float32)], 0.0)
+
+
+def test_global_norm_clip_vs_oracle(ody, oracle):
+    grads = [_rand(n, n, 3.0) for n in (1, 100, 70001, 1 << 20)]
+    a = [g.copy() for g in grads]
+    b = [g.copy() for g in grads]
+    na = ody.clip_gradients_by_global_norm(a, 1.0)
+    nb = oracle.global_norm_clip(b, 1.0)
+    assert na == nb
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x, y)
+
+
+def test_master_conversions(ody):
+    h = np.full(100, 0.5, np.float16)
+    m = ody.convert_to_fp32_master(h)
+    assert m.dtype == np.float32 and m[0] == 0.5
+    p = np.full(100, 1.0, np.float16)
+    ody.update_model_from_master(p, np.full(100, 2.0, np.float32))
+    assert p[0] == 2.0
+    with pytest.raises(ody.OdysseyError, match="sizes must match"):
+        ody.update_model_from_master(p, np.zeros(3, np.float32))

@@ -1,0 +1,190 @@
+"""GPU parity of the re-quantisation kernels against the oracle: bit-exact
+codes, block scales and per-tensor scales for every kind, on seeded inputs,
+ragged sizes and the special values the reference's tests use."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+KINDS = [1, 2, 3, 4, 5, 6, 7, 8]  # FP16 .. NVFP4_TENSOR
+
+
+@pytest.fixture(scope="module")
+def ody():
+    import odyssey_b200 as o
+    o.lib()
+    return o
+
+
+def _specials():
+    return np.float32([0.0, -0.0, np.nan, np.inf, -np.inf, 1e-45, -1e-45, 1e-38, 6.0, -6.0, 0.5, 1.25, 1.75, 2.5,
+                       3.5, 5.0, 448.0, 500.0, 65504.0, 1e30, -1e-7, 3e-8])
+
+
+def _mixed(n, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal(n).astype(np.float32)
+    x *= np.float32(10.0) ** rng.integers(-6, 3, n).astype(np.float32)
+    return x
+
+
+def _gpu_quant(ody, kind, x, src_dtype=0):
+    out = np.zeros(ody._lib.quant_bytes(kind, x.size), np.uint8)
+    ts = C.c_float(0)
+    ody._lib.check(ody.lib().ody_quantize(kind, x.ctypes.data, src_dtype, x.size, out.ctypes.data, C.byref(ts)))
+    return out, ts.value
+
+
+@pytest.mark.parametrize("kind", KINDS)
+@pytest.mark.parametrize("n", [1, 15, 16, 17, 31, 33, 2047, 2048, 2049, 100003])
+def test_quantize_bit_exact_ragged(ody, oracle, kind, n):
+    x = _mixed(n, n + kind)
+    if kind in (1, 2, 3, 4, 6, 7):  # finite specials for the plain kinds
+        sp = _specials()
+        k = min(n, sp.size)
+        x[:k] = sp[:k]
+    if kind in (5, 8):
+        x = np.nan_to_num(x, nan=0.0, posinf=7.0, neginf=-7.0)
+    got, ts = _gpu_quant(ody, kind, x)
+    want, wts = oracle.quantize(kind, x)
+    np.testing.assert_array_equal(got, want)
+    assert np.float32(ts) == np.float32(wts)
+
+
+@pytest.mark.parametrize("kind", [6, 7, 8])
+def test_quantize_bf16_source(ody, oracle, kind):
+    from odyssey_b200.workloads import bf16_bits_to_f32, f32_to_bf16_bits
+    h = f32_to_bf16_bits(_mixed(5000, 3) * np.float32(0.02))
+    got, ts = _gpu_quant(ody, kind, h, src_dtype=2)
+    want, wts = oracle.quantize(kind, bf16_bits_to_f32(h))
+    np.testing.assert_array_equal(got, want)
+    assert np.float32(ts) == np.float32(wts)
+
+
+def test_e4m3_cast_sweep(ody, oracle):
+    """Hardware cvt.rn.satfinite e4m3 (the NVFP4 block-scale byte) against the
+    oracle's software RNE on every 97th float32 bit pattern of [0, 480]."""
+    bits = np.arange(0, 0x43F00000, 97, dtype=np.uint32)
+    x = bits.view(np.float32)
+    x = np.concatenate([x, -x])
+    got, _ = _gpu_quant(ody, 3, x)
+    want, _ = oracle.quantize(3, x)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_e5m2_f16_bf16_cast_sweep(ody, oracle):
+    bits = np.arange(0x30000000, 0x47800000, 131, dtype=np.uint32)
+    x = np.concatenate([bits.view(np.float32), -bits.view(np.float32)])
+    for kind in (1, 2, 4):
+        got, _ = _gpu_quant(ody, kind, x)
+        want, _ = oracle.quantize(kind, x)
+        np.testing.assert_array_equal(got, want, err_msg=f"kind {kind}")
+
+
+@pytest.mark.parametrize("kind", [6, 7, 8])
+def test_fp4_threshold_tables_every_scale(ody, oracle, kind):
+    """For every block scale the table-driven encode equals the reference's
+    division ladder: blocks whose amax selects each E8M0/E4M3 scale, filled
+    with values straddling every threshold."""
+    B = 32 if kind == 6 else 16
+    rng = np.random.default_rng(7)
+    blocks = []
+    exps = range(-40, 40) if kind == 6 else np.linspace(-11, 9, 400)
+    for e in exps:
+        amax = np.float32(6.0 * 2.0 ** e)
+        vals = amax * rng.uniform(-1, 1, B).astype(np.float32)
+        t = np.float32([0.5, 1.25, 1.75, 2.5, 3.5, 5.0])
+        sc = amax / np.float32(6.0)
+        k = min(B - 1, 6)
+        vals[1:k + 1] = t[:k] * sc * np.float32(1 + 1e-7 * rng.standard_normal())
+        vals[0] = amax
+        blocks.append(vals)
+    x = np.concatenate(blocks).astype(np.float32)
+    got, ts = _gpu_quant(ody, kind, x)
+    want, wts = oracle.quantize(kind, x)
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_dequantize_bit_exact(ody, oracle, kind):
+    x = np.nan_to_num(_mixed(4099, kind), nan=0.0, posinf=1.0, neginf=-1.0)
+    q, ts = oracle.quantize(kind, x)
+    out = np.zeros(x.size, np.float32)
+    ody._lib.check(ody.lib().ody_dequantize(kind, q.ctypes.data, x.size, ts, out.ctypes.data))
+    want = oracle.dequantize(kind, q, x.size, ts)
+    np.testing.assert_array_equal(out.view(np.uint32), want.view(np.uint32))
+
+
+def test_every_code_byte_decodes(ody, oracle):
+    """Decode of all 256 byte values for each FP4 / FP8 kind."""
+    for kind in (3, 4, 6, 7):
+        if kind in (6, 7):
+            B = 17 if kind == 6 else 9
+            nb = 256
+            q = np.zeros(nb * B, np.uint8)
+            for b in range(nb):
+                q[b * B: b * B + B - 1] = b
+                q[b * B + B - 1] = (b * 37) % (256 if kind == 6 else 127)
+            n = nb * (32 if kind == 6 else 16)
+        else:
+            q = np.arange(256, dtype=np.uint8)
+            n = 256
+        out = np.zeros(n, np.float32)
+        ody._lib.check(ody.lib().ody_dequantize(kind, q.ctypes.data, n, 1.0, out.ctypes.data))
+        want = oracle.dequantize(kind, q, n, 1.0)
+        np.testing.assert_array_equal(np.isnan(out), np.isnan(want))
+        m = ~np.isnan(want)
+        np.testing.assert_array_equal(out[m].view(np.uint32), want[m].view(np.uint32))
+
+
+def test_python_mirror_api(ody, oracle):
+    x = _mixed(1000, 11)
+    q = ody.to_mxfp4(x)
+    want, _ = oracle.quantize(6, x)
+    np.testing.assert_array_equal(q.data, want)
+    np.testing.assert_array_equal(ody.from_mxfp4(q), oracle.dequantize(6, want, x.size))
+    with pytest.raises(ody.OdysseyError, match="multiple of 17"):
+        ody.from_mxfp4(np.zeros(18, np.uint8))
+    q = ody.to_nvfp4_tensor_scaled(x)
+    w, s = oracle.quantize(8, x)
+    np.testing.assert_array_equal(q.data, w)
+    assert q.tensor_scale == s
+
+
+def test_device_pointers_via_torch(ody, oracle):
+    torch = pytest.importorskip("torch")
+    x = _mixed(70000, 5)
+    xd = torch.from_numpy(x).cuda()
+    q = ody.to_nvfp4(xd)
+    assert q.data.is_cuda
+    want, _ = oracle.quantize(7, x)
+    np.testing.assert_array_equal(q.data.cpu().numpy(), want)
+    d = ody.from_nvfp4(q.data)
+    np.testing.assert_array_equal(d.cpu().numpy()[: x.size], oracle.dequantize(7, want, x.size))
+
+
+def test_config2_full_size_mxfp4(ody, oracle):
+    """Config 2 at full size (4096^2): bit-exact codes and round trip."""
+    from odyssey_b200.workloads import mxfp4_tensor
+    x = mxfp4_tensor(0)
+    got, _ = _gpu_quant(ody, 6, x)
+    want, _ = oracle.quantize(6, x)
+    np.testing.assert_array_equal(got, want)
+    out = np.zeros(x.size, np.float32)
+    ody._lib.check(ody.lib().ody_dequantize(6, got.ctypes.data, x.size, 1.0, out.ctypes.data))
+    np.testing.assert_array_equal(out, oracle.dequantize(6, want, x.size))
+
+
+def test_config3_full_size_nvfp4_bf16(ody, oracle):
+    """Config 3 at full size (8192^2 BF16) with the per-tensor scale and
+    without it (pure reference to_nvfp4)."""
+    from odyssey_b200.workloads import bf16_bits_to_f32, nvfp4_tensor_bf16
+    h = nvfp4_tensor_bf16(0)
+    xf = bf16_bits_to_f32(h)
+    for kind in (8, 7):
+        got, ts = _gpu_quant(ody, kind, h, src_dtype=2)
+        want, wts = oracle.quantize(kind, xf)
+        np.testing.assert_array_equal(got, want)
+        assert np.float32(ts) == np.float32(wts)

@@ -165,7 +165,8 @@ def run_reference(args, rank, world):
 
 
 def config_dict(world):
-    return {"workload": "flat1b_adamw_clip_bf16_nvfp4 (configs[4])", "params": TOTAL, "tensors": NT,
+    name = "flat1b_adamw_clip_bf16_nvfp4 (configs[4])" if NT == 64 else f"flat_{NT}x4096^2 (profiling case)"
+    return {"workload": name, "params": TOTAL, "tensors": NT,
             "tensor_shape": [SIDE, SIDE], "grad_dtype": "bf16", "master_dtype": "f32", "optimizer": "adamw",
             "clip_max_norm": 1.0, "quant": "nvfp4 + per-tensor f32 scale", "loss_scale": 4096.0,
             "parallelism": f"zero1 whole-tensor shards x{world}",
@@ -175,12 +176,16 @@ def config_dict(world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tensors", type=int, default=64,
+                    help="number of 4096x4096 tensors (64 = the 1B workload; fewer only for profiling)")
     args = ap.parse_args()
+    global NT, TOTAL
+    NT, TOTAL = args.tensors, args.tensors * PER
     world = env_int("WORLD_SIZE", 1)
     rank = env_int("RANK", 0)
     local = env_int("LOCAL_RANK", 0)
@@ -196,7 +201,7 @@ def main():
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    wl = flat1b()
+    wl = flat1b(ntensors=NT)
     kw = wl.step_kwargs()
     kw["device"] = local
     if world > 1:
@@ -233,6 +238,13 @@ def main():
     ctx.pass_times()
     barrier()
     with Clocks(local) as clk:
+        # keep the GPU loaded while the clock sampler starts (untimed steps)
+        w_end = time.perf_counter() + 0.6
+        while time.perf_counter() < w_end:
+            ctx.step(t)
+            t += 1
+        ctx.pass_times()
+        barrier()
         ev0.record(stream)
         for _ in range(args.steps):
             ctx.step_async(t)

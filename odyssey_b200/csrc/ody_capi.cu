@@ -361,7 +361,10 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   c->n_total = off;
   c->q_total = qoff;
   const int nl = (int)c->tdesc.size();
-  ODY_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  // a blocking stream: work on it is ordered after work the caller queued on
+  // the legacy default stream (e.g. PyTorch producing a device buffer that
+  // ody_upload then copies), and vice versa
+  ODY_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamDefault));
   ODY_CUDA(cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming));
   const size_t n = (size_t)(off > 0 ? off : kPad);
   const bool need_s1 = c->cfg.optimizer != ODY_SGD || c->cfg.momentum > 0.0;

@@ -130,29 +130,67 @@ __device__ __forceinline__ float divide(float x, const Divisor& v) {
   return v.pow2 ? __fmul_rn(x, v.r) : __fdiv_rn(x, v.d);
 }
 
+// Fast unscale for power-of-two divisors.  A bfloat16 (or float32) value
+// times an exact power of two is exact in float32 unless the product is
+// float32-subnormal, so only such tiny products need the rounding back to the
+// gradient dtype (float16 always rounds: its normal range is narrower).
 template <int GDT>
-__device__ __forceinline__ void grad8(const void* g, int64_t e0, bool use_scaler, const Divisor& dv,
-                                      float out[8]) {
+__device__ __forceinline__ float unscale_elem(float x, const Divisor& dv) {
+  if (GDT == DT_F32) return divide(x, dv);
+  if (GDT == DT_BF16 && dv.pow2) {
+    float q = __fmul_rn(x, dv.r);
+    if (fabsf(q) < 1.17549435e-38f) q = bf16_bits_to_f32(f32_to_bf16_bits(q));
+    return q;
+  }
+  const float q = divide(x, dv);
+  return GDT == DT_F16 ? f16_bits_to_f32(f32_to_f16_bits(q)) : bf16_bits_to_f32(f32_to_bf16_bits(q));
+}
+
+// raw gradient values of 8 consecutive elements, as float32 (exact upcast)
+template <int GDT>
+__device__ __forceinline__ void load_grad8_raw(const void* g, int64_t e0, float out[8]) {
   if (GDT == DT_F32) {
     const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(g) + e0);
     float4 a = __ldcs(p), b = __ldcs(p + 1);
-    float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int k = 0; k < 8; k++) out[k] = use_scaler ? divide(x[k], dv) : x[k];
+    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+    out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
   } else {
     uint4 raw = __ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(g) + e0));
     uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-      uint16_t h = (uint16_t)(w[k >> 1] >> ((k & 1) * 16));
-      float x = GDT == DT_F16 ? f16_bits_to_f32(h) : bf16_bits_to_f32(h);
-      if (use_scaler) {
-        float q = divide(x, dv);
-        x = GDT == DT_F16 ? f16_bits_to_f32(f32_to_f16_bits(q)) : bf16_bits_to_f32(f32_to_bf16_bits(q));
+    for (int k = 0; k < 4; k++) {
+      if (GDT == DT_BF16) {
+        out[2 * k] = __uint_as_float(w[k] << 16);
+        out[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+      } else {
+        out[2 * k] = f16_bits_to_f32((uint16_t)(w[k] & 0xffffu));
+        out[2 * k + 1] = f16_bits_to_f32((uint16_t)(w[k] >> 16));
       }
-      out[k] = x;
     }
   }
+}
+
+template <int GDT>
+__device__ __forceinline__ void grad8(const void* g, int64_t e0, bool use_scaler, const Divisor& dv,
+                                      float out[8]) {
+  load_grad8_raw<GDT>(g, e0, out);
+  if (use_scaler) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) out[k] = unscale_elem<GDT>(out[k], dv);
+  }
+}
+
+// Sum of the float32 squares of 8 consecutive elements, reduced in float32
+// as a SIMD reduce_add of width 8 (halves added pairwise), which is how the
+// reference's _norm_sq_simd_f32 (gradient_clipping.mojo:52-67) reduces each
+// vector before accumulating it in float64.
+__device__ __forceinline__ float sq8(const float v[8]) {
+  float q[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) q[k] = __fmul_rn(v[k], v[k]);
+  const float a0 = __fadd_rn(q[0], q[4]), a1 = __fadd_rn(q[1], q[5]);
+  const float a2 = __fadd_rn(q[2], q[6]), a3 = __fadd_rn(q[3], q[7]);
+  return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
 }
 
 __device__ __forceinline__ bool is_finite_f(float x) { return fabsf(x) < __uint_as_float(0x7f800000u); }
@@ -250,6 +288,25 @@ struct StatsArgs {
   int ntensors;
 };
 
+// nonfinite count of 8 values; only evaluated when their square sum is not
+// finite (a NaN/Inf element, or squares that overflow float32)
+__device__ __noinline__ int count_nonfinite8(const float v[8]) {
+  int c = 0;
+#pragma unroll
+  for (int k = 0; k < 8; k++) c += !is_finite_f(v[k]);
+  return c;
+}
+
+template <int GDT>
+__device__ __forceinline__ void stats8(const void* g, int64_t e0, bool use_scaler, const Divisor& dv,
+                                       double& acc, long long& bad) {
+  float v[8];
+  grad8<GDT>(g, e0, use_scaler, dv, v);
+  const float s = sq8(v);
+  if (!is_finite_f(s)) bad += count_nonfinite8(v);
+  acc += (double)s;
+}
+
 template <int GDT>
 __global__ void __launch_bounds__(kThreads) stats_kernel(StatsArgs a) {
   const Divisor dv = make_divisor(unscale_divisor<GDT>(a.scaler->scale));
@@ -260,26 +317,10 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(StatsArgs a) {
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   constexpr int U = 4;
   for (; i + (U - 1) * stride < ngroups; i += U * stride) {
-    float v[U][8];
 #pragma unroll
-    for (int u = 0; u < U; u++) grad8<GDT>(a.grad, (i + u * stride) * 8, a.use_scaler, dv, v[u]);
-#pragma unroll
-    for (int u = 0; u < U; u++)
-#pragma unroll
-      for (int k = 0; k < 8; k++) {
-        bad += !is_finite_f(v[u][k]);
-        acc += (double)__fmul_rn(v[u][k], v[u][k]);
-      }
+    for (int u = 0; u < U; u++) stats8<GDT>(a.grad, (i + u * stride) * 8, a.use_scaler, dv, acc, bad);
   }
-  for (; i < ngroups; i += stride) {
-    float v[8];
-    grad8<GDT>(a.grad, i * 8, a.use_scaler, dv, v);
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-      bad += !is_finite_f(v[k]);
-      acc += (double)__fmul_rn(v[k], v[k]);
-    }
-  }
+  for (; i < ngroups; i += stride) stats8<GDT>(a.grad, i * 8, a.use_scaler, dv, acc, bad);
   block_sum2(acc, bad);
   __shared__ bool last;
   if (threadIdx.x == 0) {
@@ -956,15 +997,19 @@ cudaError_t launch_count_nonfinite(int dt, const void* g, int64_t n, unsigned lo
   return cudaGetLastError();
 }
 
-// sum of float32 squares in float64, per-CTA partials + fixed-order final sum
+// sum of float32 squares in float64 (8-element float32 groups, as sq8),
+// per-CTA partials + fixed-order final sum
 __global__ void sumsq_kernel(const float* g, int64_t n, StatsPartial* partials, unsigned* ticket,
                              double* total) {
   double acc = 0.0;
   long long dummy = 0;
+  const int64_t ngroups = (n + 7) / 8;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const float x = g[i];
-    acc += (double)__fmul_rn(x, x);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ngroups; i += stride) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = (i * 8 + k < n) ? g[i * 8 + k] : 0.0f;
+    acc += (double)sq8(v);
   }
   block_sum2(acc, dummy);
   __shared__ bool last;

@@ -553,11 +553,24 @@ void ora_upcast(int dtype, const void* g, int64_t n, float* out) {
   for (int64_t i = 0; i < n; i++) out[i] = load_as_f32(dtype, g, i);
 }
 
-/* _norm_sq_simd_f32 (gradient_clipping.mojo:52-67): float32 squares,
- * accumulated in float64.  The reference groups lanes by the host's SIMD
- * width; here the float64 accumulation is sequential inside fixed 65536-
- * element blocks whose sums are then added in order, which is deterministic
- * for any thread count. */
+/* _norm_sq_simd_f32 (gradient_clipping.mojo:52-67): `vec * vec` in float32,
+ * `reduce_add()` of each SIMD vector in float32, accumulated in float64.
+ * The reference's vector width is the host's (8 lanes on AVX2, 16 on
+ * AVX-512); this restatement fixes it at 8 consecutive elements (tail
+ * zero-padded) with the halves-pairwise reduce_add order
+ * ((q0+q4)+(q2+q6)) + ((q1+q5)+(q3+q7)).  The float64 accumulation is
+ * sequential inside fixed 65536-element blocks whose sums are then added in
+ * order, which is deterministic for any thread count. */
+static inline float sq8(const float* g, int64_t i, int64_t n) {
+  float q[8];
+  for (int k = 0; k < 8; k++) {
+    float x = (i + k < n) ? g[i + k] : 0.0f;
+    q[k] = x * x;
+  }
+  float a0 = q[0] + q[4], a1 = q[1] + q[5], a2 = q[2] + q[6], a3 = q[3] + q[7];
+  return (a0 + a2) + (a1 + a3);
+}
+
 double ora_sumsq_f32(const float* g, int64_t n) {
   const int64_t B = 65536;
   int64_t nb = (n + B - 1) / B;
@@ -566,10 +579,7 @@ double ora_sumsq_f32(const float* g, int64_t n) {
   for (int64_t b = 0; b < nb; b++) {
     double acc = 0.0;
     int64_t e = (b + 1) * B < n ? (b + 1) * B : n;
-    for (int64_t i = b * B; i < e; i++) {
-      float sq = g[i] * g[i];
-      acc += (double)sq;
-    }
+    for (int64_t i = b * B; i < e; i += 8) acc += (double)sq8(g, i, n);
     part[b] = acc;
   }
   double t = 0.0;

@@ -1126,3 +1126,12 @@ extern "C" int ody_dequantize(int32_t kind, const void* q, int64_t n, float ts, 
   ODY_CUDA(cudaStreamSynchronize(S.st));
   return ODY_OK;
 }
+
+// Test hook (not part of include/odyssey_mp.h): the exact-division shortcut
+// used by the per-tensor-scaled requant against IEEE division, on device
+// arrays of n (x, s) pairs.
+extern "C" int odyx_selftest_divide(const float* x, const float* s, int64_t n, float* fast, float* ieee) {
+  ODY_CUDA(launch_selftest_divide(x, s, n, fast, ieee, cudaStreamPerThread));
+  ODY_CUDA(cudaStreamSynchronize(cudaStreamPerThread));
+  return ODY_OK;
+}

@@ -125,3 +125,8 @@ cudaError_t launch_opt_step(int opt, const OptConsts& oc, const float* p, const 
                             float* os2, cudaStream_t st);
 
 }  // namespace ody
+
+namespace ody {
+cudaError_t launch_selftest_divide(const float* x, const float* s, int64_t n, float* fast, float* ieee,
+                                   cudaStream_t st);
+}

@@ -146,17 +146,35 @@ __device__ __forceinline__ float unscale_elem(float x, const Divisor& dv) {
   return GDT == DT_F16 ? f16_bits_to_f32(f32_to_f16_bits(q)) : bf16_bits_to_f32(f32_to_bf16_bits(q));
 }
 
-// raw gradient values of 8 consecutive elements, as float32 (exact upcast)
+// raw gradient bits of 8 consecutive elements (one or two 16-byte loads)
+struct Raw8 {
+  uint4 a, b;
+};
+
 template <int GDT>
-__device__ __forceinline__ void load_grad8_raw(const void* g, int64_t e0, float out[8]) {
+__device__ __forceinline__ Raw8 ld_raw8(const void* g, int64_t e0) {
+  Raw8 r;
   if (GDT == DT_F32) {
-    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(g) + e0);
-    float4 a = __ldcs(p), b = __ldcs(p + 1);
-    out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
-    out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+    const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(g) + e0);
+    r.a = __ldcs(p);
+    r.b = __ldcs(p + 1);
   } else {
-    uint4 raw = __ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(g) + e0));
-    uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    r.a = __ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(g) + e0));
+    r.b = make_uint4(0, 0, 0, 0);
+  }
+  return r;
+}
+
+// exact upcast of the raw bits to float32
+template <int GDT>
+__device__ __forceinline__ void unpack8(const Raw8& r, float out[8]) {
+  if (GDT == DT_F32) {
+    out[0] = __uint_as_float(r.a.x); out[1] = __uint_as_float(r.a.y);
+    out[2] = __uint_as_float(r.a.z); out[3] = __uint_as_float(r.a.w);
+    out[4] = __uint_as_float(r.b.x); out[5] = __uint_as_float(r.b.y);
+    out[6] = __uint_as_float(r.b.z); out[7] = __uint_as_float(r.b.w);
+  } else {
+    const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       if (GDT == DT_BF16) {
@@ -171,13 +189,18 @@ __device__ __forceinline__ void load_grad8_raw(const void* g, int64_t e0, float 
 }
 
 template <int GDT>
-__device__ __forceinline__ void grad8(const void* g, int64_t e0, bool use_scaler, const Divisor& dv,
-                                      float out[8]) {
-  load_grad8_raw<GDT>(g, e0, out);
+__device__ __forceinline__ void unscale8(float v[8], bool use_scaler, const Divisor& dv) {
   if (use_scaler) {
 #pragma unroll
-    for (int k = 0; k < 8; k++) out[k] = unscale_elem<GDT>(out[k], dv);
+    for (int k = 0; k < 8; k++) v[k] = unscale_elem<GDT>(v[k], dv);
   }
+}
+
+template <int GDT>
+__device__ __forceinline__ void grad8(const void* g, int64_t e0, bool use_scaler, const Divisor& dv,
+                                      float out[8]) {
+  unpack8<GDT>(ld_raw8<GDT>(g, e0), out);
+  unscale8<GDT>(out, use_scaler, dv);
 }
 
 // Sum of the float32 squares of 8 consecutive elements, reduced in float32
@@ -288,43 +311,44 @@ struct StatsArgs {
   int ntensors;
 };
 
-// nonfinite count of 8 values; only evaluated when their square sum is not
-// finite (a NaN/Inf element, or squares that overflow float32)
-__device__ __noinline__ int count_nonfinite8(const float v[8]) {
-  int c = 0;
-#pragma unroll
-  for (int k = 0; k < 8; k++) c += !is_finite_f(v[k]);
-  return c;
-}
-
 template <int GDT>
-__device__ __forceinline__ void stats8(const void* g, int64_t e0, bool use_scaler, const Divisor& dv,
-                                       double& acc, long long& bad) {
+__device__ __forceinline__ void stats_raw8(const Raw8& r, bool use_scaler, const Divisor& dv, double& acc,
+                                           long long& bad) {
   float v[8];
-  grad8<GDT>(g, e0, use_scaler, dv, v);
+  unpack8<GDT>(r, v);
+  unscale8<GDT>(v, use_scaler, dv);
   const float s = sq8(v);
-  if (!is_finite_f(s)) bad += count_nonfinite8(v);
+  // a non-finite square sum means a NaN/Inf element or squares that overflow
+  // float32; only then are the elements counted one by one
+  if (!is_finite_f(s)) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) bad += !is_finite_f(v[k]);
+  }
   acc += (double)s;
 }
 
 template <int GDT>
-__global__ void __launch_bounds__(kThreads) stats_kernel(StatsArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) stats_kernel(StatsArgs a) {
   const Divisor dv = make_divisor(unscale_divisor<GDT>(a.scaler->scale));
-  double acc = 0.0;
+  constexpr int U = 4;
+  double acc[U] = {0.0, 0.0, 0.0, 0.0};
   long long bad = 0;
   const int64_t ngroups = a.n / 8;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  constexpr int U = 4;
   for (; i + (U - 1) * stride < ngroups; i += U * stride) {
+    Raw8 r[U];
 #pragma unroll
-    for (int u = 0; u < U; u++) stats8<GDT>(a.grad, (i + u * stride) * 8, a.use_scaler, dv, acc, bad);
+    for (int u = 0; u < U; u++) r[u] = ld_raw8<GDT>(a.grad, (i + u * stride) * 8);
+#pragma unroll
+    for (int u = 0; u < U; u++) stats_raw8<GDT>(r[u], a.use_scaler, dv, acc[u], bad);
   }
-  for (; i < ngroups; i += stride) stats8<GDT>(a.grad, i * 8, a.use_scaler, dv, acc, bad);
-  block_sum2(acc, bad);
+  for (; i < ngroups; i += stride) stats_raw8<GDT>(ld_raw8<GDT>(a.grad, i * 8), a.use_scaler, dv, acc[0], bad);
+  double acc_all = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  block_sum2(acc_all, bad);
   __shared__ bool last;
   if (threadIdx.x == 0) {
-    a.partials[blockIdx.x].sumsq = acc;
+    a.partials[blockIdx.x].sumsq = acc_all;
     a.partials[blockIdx.x].nonfinite = bad;
     __threadfence();
     unsigned t = atomicAdd(a.ticket, 1u);
@@ -356,7 +380,7 @@ __global__ void __launch_bounds__(kThreads) stats_kernel(StatsArgs a) {
 int stats_grid(int device) {
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  return sms * 8;
+  return sms * 4;
 }
 
 cudaError_t launch_stats(int gdt, const void* grad, int64_t n, int use_scaler, DevScaler* scaler,
@@ -398,58 +422,94 @@ cudaError_t launch_finalize(const double* gathered, int world, DevScaler* scaler
 }
 
 // ---------------------------------------------------------------------------
-// Tile-level re-quantisation helpers shared by passes 2 and 3 and the
-// standalone quantiser.  Thread t of the CTA holds elements [8t, 8t+8) of a
-// 2048-element tile; MXFP4 blocks span 4 threads, NVFP4 blocks 2 threads.
-// Codes are staged in shared memory in the reference's AoS block layout
-// (tensor_dtype_conv.mojo:281-366: code bytes, element 2i in the high
-// nibble, then the scale byte) and written out as 16-byte stores.
+// Re-quantisation helpers shared by passes 2 and 3 and the standalone
+// quantiser.  Lane l of a warp holds elements [8l, 8l+8) of the warp's 256-
+// element slice of a 2048-element tile; MXFP4 blocks span 4 lanes, NVFP4
+// blocks 2 lanes.  Each warp stages its slice's codes in its own piece of
+// shared memory in the reference's AoS block layout
+// (tensor_dtype_conv.mojo:281-366: code bytes with element 2i in the high
+// nibble, then the scale byte) and writes it out with 16-byte (NVFP4, 144 B
+// per warp) or 8-byte (MXFP4, 136 B per warp) stores; no CTA-wide barrier.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void stage_mxfp4(const float v[8], uint8_t* stage, const Fp4Thr* thr) {
+constexpr int kWarpStage = 160;  // bytes of shared memory per warp
+constexpr int kNvWarpBytes = 144;
+constexpr int kMxWarpBytes = 136;
+
+// 1 for a block whose codes need the reference's special cases (a NaN or
+// +-Inf element, a zero NVFP4 scale, an infinite MXFP4 scale); x*0 is NaN
+// exactly for non-finite x.
+__device__ __forceinline__ bool any_nonfinite8(const float v[8]) {
+  float z = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; k++) z = __fmaf_rn(v[k], 0.0f, z);
+  return z != z;
+}
+
+// the threshold ladder without special cases (finite x, positive finite scale)
+__device__ __forceinline__ uint32_t fp4_encode_plain(float x, const float* t) {
+  const float a = fabsf(x);
+  const uint32_t mag = 2u * (a >= t[1]) + (a >= t[2]) + (a >= t[3]) + (a >= t[4]) + (a >= t[5]) + (a >= t[6]);
+  return ((uint32_t)((x < 0.0f) && (a >= t[0])) << 3) | mag;
+}
+
+template <bool MX>
+__device__ __forceinline__ void stage_fp4(const float v[8], uint8_t* ws, const Fp4Thr* thr) {
   float am = 0.0f;
 #pragma unroll
   for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
   am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-  const uint8_t e = e8m0_from_f32(block_scale_value(am));
+  if (MX) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+  const uint8_t e = MX ? e8m0_from_f32(block_scale_value(am)) : e4m3_scale_from_f32(block_scale_value(am));
   const float* t = thr[e].t;
-  const int g = threadIdx.x, blk = g >> 2, j = g & 3;
-  uint8_t* dst = stage + blk * 17 + 4 * j;
+  const bool z = !MX && e == 0;
+  const bool special = z || (MX && e == 255) || any_nonfinite8(v);
+  const int lane = threadIdx.x & 31;
+  const int blk = MX ? (lane >> 2) : (lane >> 1), j = MX ? (lane & 3) : (lane & 1);
+  const int bb = MX ? 17 : 9;
+  uint8_t* dst = ws + blk * bb + 4 * j;
+  if (!special) {
 #pragma unroll
-  for (int i = 0; i < 4; i++)
-    dst[i] = (uint8_t)((fp4_encode(v[2 * i], t, false) << 4) | fp4_encode(v[2 * i + 1], t, false));
-  if (j == 3) stage[blk * 17 + 16] = e;
-}
-
-__device__ __forceinline__ void stage_nvfp4(const float v[8], uint8_t* stage, const Fp4Thr* thr) {
-  float am = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
-  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-  const uint8_t e = e4m3_scale_from_f32(block_scale_value(am));
-  const float* t = thr[e].t;
-  const bool z = (e == 0);
-  const int g = threadIdx.x, blk = g >> 1, j = g & 1;
-  uint8_t* dst = stage + blk * 9 + 4 * j;
-#pragma unroll
-  for (int i = 0; i < 4; i++)
-    dst[i] = (uint8_t)((fp4_encode(v[2 * i], t, z) << 4) | fp4_encode(v[2 * i + 1], t, z));
-  if (j == 1) stage[blk * 9 + 8] = e;
-}
-
-// Copy `nbytes` staged bytes to global memory; 16-byte stores when the
-// destination is aligned and the whole range may be written, else bytes up to
-// `limit`.
-__device__ __forceinline__ void flush_stage(const uint8_t* stage, int nbytes, uint8_t* dst,
-                                            int64_t limit) {
-  if (limit >= nbytes && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0)) {
-    const uint4* s = reinterpret_cast<const uint4*>(stage);
-    uint4* d = reinterpret_cast<uint4*>(dst);
-    for (int i = threadIdx.x; i < nbytes / 16; i += blockDim.x) d[i] = s[i];
+    for (int i = 0; i < 4; i++)
+      dst[i] = (uint8_t)((fp4_encode_plain(v[2 * i], t) << 4) | fp4_encode_plain(v[2 * i + 1], t));
   } else {
-    const int m = (int)(limit < nbytes ? limit : nbytes);
-    for (int i = threadIdx.x; i < m; i += blockDim.x) dst[i] = stage[i];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      dst[i] = (uint8_t)((fp4_encode(v[2 * i], t, z) << 4) | fp4_encode(v[2 * i + 1], t, z));
   }
+  if (j == (MX ? 3 : 1)) ws[blk * bb + bb - 1] = e;
+}
+
+// write a warp's staged bytes: whole 16-byte (NVFP4) / 8-byte (MXFP4) stores
+// when the destination is aligned and the whole slice may be written, else
+// bytes up to `limit`
+template <bool MX>
+__device__ __forceinline__ void flush_warp(const uint8_t* ws, uint8_t* dst, int64_t limit) {
+  const int lane = threadIdx.x & 31;
+  const int nbytes = MX ? kMxWarpBytes : kNvWarpBytes;
+  const uintptr_t al = MX ? 7u : 15u;
+  if (limit >= nbytes && ((reinterpret_cast<uintptr_t>(dst) & al) == 0)) {
+    if (MX) {
+      if (lane < nbytes / 8) reinterpret_cast<uint2*>(dst)[lane] = reinterpret_cast<const uint2*>(ws)[lane];
+    } else {
+      if (lane < nbytes / 16) reinterpret_cast<uint4*>(dst)[lane] = reinterpret_cast<const uint4*>(ws)[lane];
+    }
+  } else {
+    const int m = (int)(limit < nbytes ? (limit > 0 ? limit : 0) : nbytes);
+    for (int i = lane; i < m; i += 32) dst[i] = ws[i];
+  }
+}
+
+// Exact division x / s with s's reciprocal r = RN(1/s) precomputed: the
+// product estimate is corrected once with the exactly computed remainder
+// (Markstein's correction: q0 = x*r is within one ulp, x - q0*s is exact by
+// FMA, and q0 + rem*r rounded once is the correctly rounded quotient when r
+// is the correctly rounded reciprocal).  Zero, non-finite and extreme
+// magnitudes take the IEEE division.
+__device__ __forceinline__ float div_by(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float q = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
+  const float aq = fabsf(q0);
+  return (aq >= 0x1p-125f && aq <= 0x1p+125f) ? q : __fdiv_rn(x, s);
 }
 
 __device__ __forceinline__ void store_elem8(int kind, const float v[8], uint8_t* dst) {
@@ -518,7 +578,7 @@ template <int GDT, int OPT>
 __global__ void __launch_bounds__(kThreads, 4) update_kernel(UpdateArgs a) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
-  __shared__ __align__(16) uint8_t stage[kNvTileBytes];
+  __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
   const Decision* dec = a.dec;
   if (dec->skip) return;
   const Divisor dv = make_divisor(unscale_divisor<GDT>(dec->scale_used));
@@ -591,17 +651,22 @@ __global__ void __launch_bounds__(kThreads, 4) update_kernel(UpdateArgs a) {
 #pragma unroll
         for (int k = 0; k < 8; k++) amax = amax_acc(amax, p[k]);
       } else if (kind == Q_MXFP4 || kind == Q_NVFP4) {
-        const int64_t tile_in_tensor = (tb - td.off) / kTile;
-        if (kind == Q_MXFP4) {
-          stage_mxfp4(p, stage, s_mx);
-          __syncthreads();
-          flush_stage(stage, kMxTileBytes, a.qout + td.qoff + tile_in_tensor * kMxTileBytes, kMxTileBytes);
-        } else {
-          stage_nvfp4(p, stage, s_nv);
-          __syncthreads();
-          flush_stage(stage, kNvTileBytes, a.qout + td.qoff + tile_in_tensor * kNvTileBytes, kNvTileBytes);
+        // warp-uniform: the warp's first element is inside the chunk
+        if (tb + (int64_t)(threadIdx.x & ~31) * kVec < end) {
+          const int64_t tile_in_tensor = (tb - td.off) / kTile;
+          uint8_t* ws = stage + (threadIdx.x >> 5) * kWarpStage;
+          const int w = threadIdx.x >> 5;
+          if (kind == Q_MXFP4) {
+            stage_fp4<true>(p, ws, s_mx);
+            __syncwarp();
+            flush_warp<true>(ws, a.qout + td.qoff + tile_in_tensor * kMxTileBytes + w * kMxWarpBytes, kMxWarpBytes);
+          } else {
+            stage_fp4<false>(p, ws, s_nv);
+            __syncwarp();
+            flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
+          }
+          __syncwarp();
         }
-        __syncthreads();
       } else if (act) {
         const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
         store_elem8(kind, p, a.qout + td.qoff + te * esz);
@@ -667,7 +732,7 @@ struct RequantArgs {
 __global__ void __launch_bounds__(kThreads, 4) requant_kernel(RequantArgs a) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
-  __shared__ __align__(16) uint8_t stage[kNvTileBytes];
+  __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
   if (a.dec->skip) return;
   load_thr_smem(s_mx, s_nv);
   __syncthreads();
@@ -676,6 +741,7 @@ __global__ void __launch_bounds__(kThreads, 4) requant_kernel(RequantArgs a) {
     const TensorDesc td = a.tensors[ch.tensor];
     const int kind = td.quant;
     const float s = tensor_scale_from_amax(kind, __ldcg(&a.amax_slots[ch.tensor]));
+    const float r = __frcp_rn(s);
     if (ch.start == td.off && threadIdx.x == 0) a.qscale[ch.tensor] = s;
     const int64_t end = ch.start + ch.len;
     for (int64_t tb = ch.start; tb < end; tb += kTile) {
@@ -688,17 +754,21 @@ __global__ void __launch_bounds__(kThreads, 4) requant_kernel(RequantArgs a) {
         x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
         x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
 #pragma unroll
-        for (int k = 0; k < 8; k++) x[k] = __fdiv_rn(x[k], s);
+        for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
       } else {
 #pragma unroll
         for (int k = 0; k < 8; k++) x[k] = 0.0f;
       }
       if (kind == Q_NVFP4_TENSOR) {
-        const int64_t tile_in_tensor = (tb - td.off) / kTile;
-        stage_nvfp4(x, stage, s_nv);
-        __syncthreads();
-        flush_stage(stage, kNvTileBytes, a.qout + td.qoff + tile_in_tensor * kNvTileBytes, kNvTileBytes);
-        __syncthreads();
+        if (tb + (int64_t)(threadIdx.x & ~31) * kVec < end) {
+          const int64_t tile_in_tensor = (tb - td.off) / kTile;
+          const int w = threadIdx.x >> 5;
+          uint8_t* ws = stage + w * kWarpStage;
+          stage_fp4<false>(x, ws, s_nv);
+          __syncwarp();
+          flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
+          __syncwarp();
+        }
       } else if (act) {
         store_elem8(Q_FP8_E4M3, x, a.qout + td.qoff + (e0 - td.off));
       }
@@ -794,11 +864,12 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, int sdt, c
                                                             const uint32_t* amax, float* tscale) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
-  __shared__ __align__(16) uint8_t stage[kNvTileBytes];
+  __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
   load_thr_smem(s_mx, s_nv);
   __syncthreads();
   const bool scaled = (kind == Q_NVFP4_TENSOR || kind == Q_FP8_E4M3_TENSOR);
   const float s = scaled ? tensor_scale_from_amax(kind, *amax) : 1.0f;
+  const float r = __frcp_rn(s);
   if (blockIdx.x == 0 && threadIdx.x == 0 && tscale) *tscale = s;
   const int64_t ntiles = (n + kTile - 1) / kTile;
   for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -807,18 +878,23 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, int sdt, c
     load_src8(sdt, x, n, e0, v);
     if (scaled) {
 #pragma unroll
-      for (int k = 0; k < 8; k++) v[k] = __fdiv_rn(v[k], s);
+      for (int k = 0; k < 8; k++) v[k] = div_by(v[k], s, r);
     }
     if (kind == Q_MXFP4 || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
-      const int tb = kind == Q_MXFP4 ? kMxTileBytes : kNvTileBytes;
-      if (kind == Q_MXFP4)
-        stage_mxfp4(v, stage, s_mx);
-      else
-        stage_nvfp4(v, stage, s_nv);
-      __syncthreads();
-      const int64_t off = t * tb;
-      flush_stage(stage, tb, out + off, out_bytes - off);
-      __syncthreads();
+      const int w = threadIdx.x >> 5;
+      uint8_t* ws = stage + w * kWarpStage;
+      if (kind == Q_MXFP4) {
+        stage_fp4<true>(v, ws, s_mx);
+        __syncwarp();
+        const int64_t off = t * kMxTileBytes + w * kMxWarpBytes;
+        flush_warp<true>(ws, out + off, out_bytes - off);
+      } else {
+        stage_fp4<false>(v, ws, s_nv);
+        __syncwarp();
+        const int64_t off = t * kNvTileBytes + w * kNvWarpBytes;
+        flush_warp<false>(ws, out + off, out_bytes - off);
+      }
+      __syncwarp();
     } else {
       const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
       const int qk = kind == Q_FP8_E4M3_TENSOR ? Q_FP8_E4M3 : kind;
@@ -1096,4 +1172,21 @@ cudaError_t launch_opt_step(int opt, const OptConsts& oc, const float* p, const 
   return cudaGetLastError();
 }
 
+}  // namespace ody
+
+namespace ody {
+// Test hook: div_by against the IEEE division for arbitrary (x, s) pairs.
+__global__ void selftest_divide_kernel(const float* x, const float* s, int64_t n, float* fast, float* ieee) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    fast[i] = div_by(x[i], s[i], __frcp_rn(s[i]));
+    ieee[i] = __fdiv_rn(x[i], s[i]);
+  }
+}
+
+cudaError_t launch_selftest_divide(const float* x, const float* s, int64_t n, float* fast, float* ieee,
+                                   cudaStream_t st) {
+  selftest_divide_kernel<<<grid_for(n), kThreads, 0, st>>>(x, s, n, fast, ieee);
+  return cudaGetLastError();
+}
 }  // namespace ody

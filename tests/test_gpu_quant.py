@@ -188,3 +188,23 @@ def test_config3_full_size_nvfp4_bf16(ody, oracle):
         want, wts = oracle.quantize(kind, xf)
         np.testing.assert_array_equal(got, want)
         assert np.float32(ts) == np.float32(wts)
+
+
+def test_exact_division_shortcut(ody):
+    """The requant's reciprocal + one-remainder-correction division equals
+    IEEE division bit for bit, over random scales spanning the float32 range
+    and the per-tensor scales of real weights."""
+    import ctypes as C
+    torch = pytest.importorskip("torch")
+    g = torch.Generator(device="cuda").manual_seed(0)
+    n = 1 << 24
+    for lo, hi in ((-30.0, 30.0), (-120.0, 120.0), (-14.0, -6.0)):
+        x = (torch.randn(n, device="cuda", generator=g) * torch.exp2(torch.empty(n, device="cuda").uniform_(
+            lo, hi, generator=g))).float()
+        s = torch.exp2(torch.empty(n, device="cuda").uniform_(lo, hi, generator=g)).float()
+        s = s * (1 + torch.rand(n, device="cuda", generator=g))
+        fast, ieee = torch.empty_like(x), torch.empty_like(x)
+        f = ody.lib().odyx_selftest_divide
+        f.argtypes = [C.c_void_p] * 3 + [C.c_int64] + [C.c_void_p] * 2
+        assert f(x.data_ptr(), s.data_ptr(), n, fast.data_ptr(), ieee.data_ptr()) == 0
+        assert torch.equal(fast.view(torch.int32), ieee.view(torch.int32))

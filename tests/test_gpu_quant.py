@@ -205,6 +205,6 @@ def test_exact_division_shortcut(ody):
         s = s * (1 + torch.rand(n, device="cuda", generator=g))
         fast, ieee = torch.empty_like(x), torch.empty_like(x)
         f = ody.lib().odyx_selftest_divide
-        f.argtypes = [C.c_void_p] * 3 + [C.c_int64] + [C.c_void_p] * 2
+        f.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
         assert f(x.data_ptr(), s.data_ptr(), n, fast.data_ptr(), ieee.data_ptr()) == 0
         assert torch.equal(fast.view(torch.int32), ieee.view(torch.int32))

@@ -203,6 +203,22 @@ int ody_to_fp32(const void* x, int32_t dtype, int64_t n, float* out);
  * gradients clipped in place; returns the pre-clip norm in *total_norm. */
 int ody_global_norm_clip(float* const* grads, const int64_t* numels, int32_t ntensors, float max_norm,
                          float* total_norm);
+/* As ody_global_norm_clip, for callers that cannot allocate GPU memory (a
+ * fixed memory budget inside another framework's pool, work placed between
+ * graph captures, real-time code where an allocation's implicit
+ * synchronisation is not allowed).  No counterpart in the reference.
+ * Allocates nothing: its pointer table, per-block partial sums and results
+ * live in one file-scope __device__ array of about 32 KB, which every GPU
+ * that loads this library holds until the process exits.  grads must be
+ * device pointers (clipped in place); at most 1024 tensors per call, more
+ * is rejected with ODY_ERR_SHAPE.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  All calls on a device
+ * share the array, which keeps the last call's contents (each call clears
+ * what must start at zero); calls that overlap on the GPU race.  Runs on
+ * the calling thread's default stream and returns after it completes. */
+int ody_global_norm_clip_noalloc(float* const* grads, const int64_t* numels, int32_t ntensors,
+                                 float max_norm, float* total_norm);
 /* sgd_step (sgd.mojo:27-121); velocity/out_velocity may be NULL when momentum == 0. */
 int ody_sgd_step(const float* params, const float* grads, const float* velocity, int64_t n,
                  double learning_rate, double momentum, double weight_decay, float* out_params,

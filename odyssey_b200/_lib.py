@@ -92,6 +92,7 @@ _SIGS = {
     "ody_check_finite": (C.c_int, [_p, _i32, _i64, _p]),
     "ody_to_fp32": (C.c_int, [_p, _i32, _i64, _p]),
     "ody_global_norm_clip": (C.c_int, [_p, _p, _i32, C.c_float, _p]),
+    "ody_global_norm_clip_noalloc": (C.c_int, [_p, _p, _i32, C.c_float, _p]),
     "ody_sgd_step": (C.c_int, [_p, _p, _p, _i64, C.c_double, C.c_double, C.c_double, _p, _p]),
     "ody_adam_step": (C.c_int, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p]),
     "ody_adamw_step": (C.c_int, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p]),

@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libodyssey_mp.so")
-SOURCES = ["ody_kernels.cu", "ody_capi.cu"]
+SOURCES = ["ody_kernels.cu", "ody_capi.cu", "ody_noalloc.cu"]
 HEADERS = ["ody_internal.h", "ody_numerics.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

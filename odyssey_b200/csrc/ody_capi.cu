@@ -1135,3 +1135,5 @@ extern "C" int odyx_selftest_divide(const float* x, const float* s, int64_t n, f
   ODY_CUDA(cudaStreamSynchronize(cudaStreamPerThread));
   return ODY_OK;
 }
+
+void ody::record_error(const std::string& msg) { g_err = msg; }

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <string>
+
 #include "ody_numerics.cuh"
 
 namespace ody {
@@ -129,4 +131,9 @@ cudaError_t launch_opt_step(int opt, const OptConsts& oc, const float* p, const 
 namespace ody {
 cudaError_t launch_selftest_divide(const float* x, const float* s, int64_t n, float* fast, float* ieee,
                                    cudaStream_t st);
+}
+
+namespace ody {
+// sets the message ody_last_error(NULL) returns on this thread
+void record_error(const std::string& msg);
 }

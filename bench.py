@@ -35,7 +35,7 @@ NT, SIDE = 64, 4096
 PER = SIDE * SIDE
 TOTAL = NT * PER
 ALG_BYTES_STEP = 26.5625        # grads 2 + master/m/v r+w 24 + NVFP4 codes 0.5625 (B/param)
-ALG_BYTES_UPDATE = 26.0         # pass 2: grads 2 + master/m/v r+w 24
+ALG_BYTES_UPDATE = 26.5625      # apply kernel: grads 2 + master/m/v r+w 24 + NVFP4 codes 0.5625
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -308,7 +308,7 @@ def main():
             "hbm_gbs_per_gpu": step_gbs_gpu, "hbm_frac_per_gpu": step_gbs_gpu / peak,
             "alg_bytes_per_param": ALG_BYTES_STEP,
             "passes_ms_per_step": {k: v / max(nsteps, 1) for k, v in passes.items()},
-            "roofline": {"kernel": "update_kernel (pass 2)", "bound": "hbm", "achieved": upd_gbs, "peak": peak,
+            "roofline": {"kernel": "apply_kernel (update + per-tensor requant)", "bound": "hbm", "achieved": upd_gbs, "peak": peak,
                          "unit": "GB/s", "frac": upd_gbs / peak, "peak_source": peak_kind,
                          "alg_bytes_per_launch": ALG_BYTES_UPDATE * nloc, "traffic": None},
             "e2e": {"value": TOTAL / (e2e_ms * 1e-3), "unit": "params/s", "ms_per_step": e2e_ms,

@@ -95,7 +95,8 @@ struct ody_ctx {
   std::vector<int32_t> owner;      // global index -> rank
   std::vector<int32_t> local_of;   // global index -> local index or -1
   std::vector<TensorDesc> tdesc;   // local tensors
-  std::vector<Chunk> chunks_upd, chunks_rq;
+  std::vector<Chunk> chunks_upd;
+  std::vector<uint32_t> jobs;  // apply-kernel job list (bit 31: requant job)
   int64_t n_total = 0, q_total = 0;
   cudaStream_t stream = nullptr;
   cudaEvent_t done = nullptr;
@@ -105,7 +106,9 @@ struct ody_ctx {
   uint8_t* qout = nullptr;
   float* qscale = nullptr;
   uint32_t* amax = nullptr;
-  Chunk *d_chunks_upd = nullptr, *d_chunks_rq = nullptr;
+  Chunk* d_chunks_upd = nullptr;
+  uint32_t* d_jobs = nullptr;
+  uint32_t* sync = nullptr;  // job ticket + per-tensor done counts
   TensorDesc* d_tdesc = nullptr;
   StatsPartial* partials = nullptr;
   unsigned* ticket = nullptr;
@@ -114,7 +117,7 @@ struct ody_ctx {
   double* local_stats = nullptr;
   double* gathered = nullptr;
   Decision* h_dec = nullptr;  // pinned
-  int grid_stats = 0, grid_upd = 0, grid_rq = 0;
+  int grid_stats = 0, grid_apply = 0;
   bool pending = false;
   ncclComm_t comm = nullptr;
   std::string err;
@@ -319,6 +322,31 @@ static cudaError_t dalloc(T** p, size_t bytes) {
   return cudaMalloc((void**)p, bytes < 256 ? 256 : bytes);
 }
 
+// Job list of the apply kernel: every update chunk in arena order; the
+// requant chunks of a per-tensor-scaled tensor become eligible a grid-width
+// of jobs after that tensor's last update job and are interleaved, up to two
+// per update job, with the following tensors' update jobs; what is left
+// runs at the end.
+static void build_jobs(ody_ctx* c) {
+  c->jobs.clear();
+  std::vector<std::pair<size_t, uint32_t>> pending;  // (eligible position, chunk)
+  size_t head = 0;
+  const size_t W = (size_t)(c->grid_apply > 0 ? c->grid_apply : 1);
+  size_t ci = 0;
+  for (size_t li = 0; li < c->tdesc.size(); li++) {
+    const TensorDesc& d = c->tdesc[li];
+    const size_t first = ci;
+    for (int k = 0; k < d.nchunks; k++, ci++) {
+      c->jobs.push_back((uint32_t)ci);
+      for (int r = 0; r < 2 && head < pending.size() && pending[head].first <= c->jobs.size(); r++)
+        c->jobs.push_back(0x80000000u | pending[head++].second);
+    }
+    if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR)
+      for (size_t k = first; k < ci; k++) pending.push_back({c->jobs.size() + W, (uint32_t)k});
+  }
+  while (head < pending.size()) c->jobs.push_back(0x80000000u | pending[head++].second);
+}
+
 extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const void* uid) {
   if (!c) return fail(ODY_ERR_ARG, "null context");
   if (c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context already finalized");
@@ -353,7 +381,7 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
       ch.len = (int32_t)((d.npad - s) < kChunk ? (d.npad - s) : kChunk);
       ch.tensor = li;
       c->chunks_upd.push_back(ch);
-      if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR) c->chunks_rq.push_back(ch);
+      c->tdesc[li].nchunks++;
     }
     off += d.npad;
     qoff += quant_region(d.quant, d.npad);
@@ -394,13 +422,15 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   if (!c->chunks_upd.empty())
     ODY_CUDA(cudaMemcpyAsync(c->d_chunks_upd, c->chunks_upd.data(), sizeof(Chunk) * c->chunks_upd.size(),
                              cudaMemcpyHostToDevice, c->stream));
-  ODY_CUDA(dalloc(&c->d_chunks_rq, sizeof(Chunk) * (c->chunks_rq.size() + 1)));
-  if (!c->chunks_rq.empty())
-    ODY_CUDA(cudaMemcpyAsync(c->d_chunks_rq, c->chunks_rq.data(), sizeof(Chunk) * c->chunks_rq.size(),
-                             cudaMemcpyHostToDevice, c->stream));
+  c->grid_apply = apply_grid(c->gdt, c->cfg.optimizer, c->cfg.device);
+  build_jobs(c);
+  ODY_CUDA(dalloc(&c->d_jobs, sizeof(uint32_t) * (c->jobs.size() + 1)));
+  if (!c->jobs.empty())
+    ODY_CUDA(cudaMemcpyAsync(c->d_jobs, c->jobs.data(), sizeof(uint32_t) * c->jobs.size(), cudaMemcpyHostToDevice,
+                             c->stream));
+  ODY_CUDA(dalloc(&c->sync, sizeof(uint32_t) * (nl + 1)));
+  ODY_CUDA(cudaMemsetAsync(c->sync, 0, sizeof(uint32_t) * (nl + 1), c->stream));
   c->grid_stats = stats_grid(c->cfg.device);
-  c->grid_upd = update_grid(c->gdt, c->cfg.optimizer, c->cfg.device);
-  c->grid_rq = requant_grid(c->cfg.device);
   ODY_CUDA(dalloc(&c->partials, sizeof(StatsPartial) * c->grid_stats));
   ODY_CUDA(dalloc(&c->ticket, sizeof(unsigned)));
   ODY_CUDA(cudaMemsetAsync(c->ticket, 0, sizeof(unsigned), c->stream));
@@ -583,7 +613,7 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   }
   cudaError_t e = launch_stats(c->gdt, c->grad, c->n_total, c->cfg.use_gradient_scaler, c->scaler, c->partials,
                                c->grid_stats, c->ticket, c->world > 1 ? 1 : 0, c->local_stats, dp, c->dec,
-                               c->amax, nl, c->stream);
+                               c->amax, c->sync, nl, c->stream);
   if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("stats kernel: ") + cudaGetErrorString(e));
   if (tev) ODY_CUDA(cudaEventRecord(tev[1], c->stream));
   if (c->world > 1) {
@@ -599,18 +629,13 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
     if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("finalize kernel: ") + cudaGetErrorString(e));
   }
   if (tev) ODY_CUDA(cudaEventRecord(tev[2], c->stream));
-  if (!c->chunks_upd.empty()) {
-    e = launch_update(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd,
-                      (int)c->chunks_upd.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout,
-                      c->amax, c->dec, c->grid_upd, c->stream);
-    if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("update kernel: ") + cudaGetErrorString(e));
+  if (!c->jobs.empty()) {
+    e = launch_apply(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd, c->d_jobs,
+                     (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout, c->amax, c->qscale,
+                     c->sync, c->dec, c->grid_apply, c->stream);
+    if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("apply kernel: ") + cudaGetErrorString(e));
   }
   if (tev) ODY_CUDA(cudaEventRecord(tev[3], c->stream));
-  if (!c->chunks_rq.empty()) {
-    e = launch_requant(c->d_chunks_rq, (int)c->chunks_rq.size(), c->d_tdesc, c->master, c->qout, c->amax,
-                       c->qscale, c->dec, c->grid_rq, c->stream);
-    if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("requant kernel: ") + cudaGetErrorString(e));
-  }
   if (tev) ODY_CUDA(cudaEventRecord(tev[4], c->stream));
   ODY_CUDA(cudaMemcpyAsync(c->h_dec, c->dec, sizeof(Decision), cudaMemcpyDeviceToHost, c->stream));
   ODY_CUDA(cudaEventRecord(c->done, c->stream));
@@ -665,6 +690,9 @@ extern "C" int ody_step_wait(ody_ctx* c, ody_step_result* out) {
   }
   c->pending = false;
   if (out) fill_result(*c->h_dec, out);
+  if (c->h_dec->err)
+    return ctx_fail(c, ODY_ERR_DEVICE_BOUNDS,
+                    "apply kernel: a requant job waited past its time limit for its tensor's update");
   return ODY_OK;
 }
 
@@ -839,7 +867,7 @@ extern "C" void ody_ctx_destroy(ody_ctx* c) {
     if (api) api->commDestroy(c->comm);
   }
   void* bufs[] = {c->master, c->s1, c->s2, c->grad, c->qout, c->qscale, c->amax, c->d_chunks_upd,
-                  c->d_chunks_rq, c->d_tdesc, c->partials, c->ticket, c->scaler, c->dec,
+                  c->d_jobs, c->sync, c->d_tdesc, c->partials, c->ticket, c->scaler, c->dec,
                   c->local_stats, c->gathered};
   for (void* b : bufs)
     if (b) cudaFree(b);

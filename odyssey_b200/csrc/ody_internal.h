@@ -29,7 +29,7 @@ struct TensorDesc {
   int64_t npad;    // numel rounded up to kPad
   int64_t qoff;    // byte offset in the quantised-output arena (multiple of 256)
   int32_t quant;   // ody::Q_*
-  int32_t pad;
+  int32_t nchunks; // update chunks of this tensor
 };
 
 // One entry of the chunk table: a kTile-aligned slice of one tensor.
@@ -73,7 +73,7 @@ struct Decision {
   float scale_used;
   float scale_next;
   float unscale_div;  // the divisor, the scale rounded to the gradient dtype
-  int32_t pad;
+  int32_t err;        // set by the apply kernel when a bounded wait ran out
   double sumsq;
   int64_t nonfinite;
   int64_t step_count;
@@ -92,19 +92,15 @@ void upload_fp4_tables(int device);  // once per device
 cudaError_t launch_stats(int gdt, const void* grad, int64_t n, int use_scaler, DevScaler* scaler,
                          StatsPartial* partials, int grid, unsigned* ticket, int world_mode,
                          double* local_stats, const DecideParams& dp, Decision* dec,
-                         uint32_t* amax_slots, int ntensors, cudaStream_t st);
+                         uint32_t* amax_slots, uint32_t* sync, int ntensors, cudaStream_t st);
 cudaError_t launch_finalize(const double* gathered, int world, DevScaler* scaler,
                             const DecideParams& dp, Decision* dec, uint32_t* amax_slots,
                             int ntensors, cudaStream_t st);
-cudaError_t launch_update(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
-                          int nchunks, const TensorDesc* tensors, float* master, float* s1, float* s2,
-                          const void* grad, uint8_t* qout, uint32_t* amax_slots, const Decision* dec,
-                          int grid, cudaStream_t st);
-cudaError_t launch_requant(const Chunk* chunks, int nchunks, const TensorDesc* tensors,
-                           const float* master, uint8_t* qout, const uint32_t* amax_slots,
-                           float* qscale, const Decision* dec, int grid, cudaStream_t st);
-int update_grid(int gdt, int opt, int device);
-int requant_grid(int device);
+cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
+                         const uint32_t* jobs, int njobs, const TensorDesc* tensors, float* master, float* s1,
+                         float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
+                         uint32_t* sync, Decision* dec, int grid, cudaStream_t st);
+int apply_grid(int gdt, int opt, int device);
 int stats_grid(int device);
 
 // stateless whole-tensor operations (device pointers)

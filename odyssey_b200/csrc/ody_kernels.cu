@@ -308,6 +308,7 @@ struct StatsArgs {
   DecideParams dp;
   Decision* dec;
   uint32_t* amax_slots;  // zeroed for pass 2
+  uint32_t* sync;        // job ticket + per-tensor done counts, zeroed for pass 2
   int ntensors;
 };
 
@@ -366,6 +367,7 @@ __global__ void __launch_bounds__(kThreads, 4) stats_kernel(StatsArgs a) {
   }
   block_sum2(s, c);
   for (int j = threadIdx.x; j < a.ntensors; j += blockDim.x) a.amax_slots[j] = 0u;
+  for (int j = threadIdx.x; j < a.ntensors + 1; j += blockDim.x) a.sync[j] = 0u;
   if (threadIdx.x == 0) {
     *a.ticket = 0u;
     if (a.world_mode == 0) {
@@ -386,9 +388,9 @@ int stats_grid(int device) {
 cudaError_t launch_stats(int gdt, const void* grad, int64_t n, int use_scaler, DevScaler* scaler,
                          StatsPartial* partials, int grid, unsigned* ticket, int world_mode,
                          double* local_stats, const DecideParams& dp, Decision* dec,
-                         uint32_t* amax_slots, int ntensors, cudaStream_t st) {
+                         uint32_t* amax_slots, uint32_t* sync, int ntensors, cudaStream_t st) {
   StatsArgs a{grad, n, use_scaler, scaler, partials, ticket, world_mode, local_stats, dp, dec,
-              amax_slots, ntensors};
+              amax_slots, sync, ntensors};
   if (gdt == DT_F32)
     stats_kernel<DT_F32><<<grid, kThreads, 0, st>>>(a);
   else if (gdt == DT_F16)
@@ -503,13 +505,15 @@ __device__ __forceinline__ void flush_warp(const uint8_t* ws, uint8_t* dst, int6
 // product estimate is corrected once with the exactly computed remainder
 // (Markstein's correction: q0 = x*r is within one ulp, x - q0*s is exact by
 // FMA, and q0 + rem*r rounded once is the correctly rounded quotient when r
-// is the correctly rounded reciprocal).  Zero, non-finite and extreme
-// magnitudes take the IEEE division.
+// is the correctly rounded reciprocal, provided nothing under- or overflows:
+// the remainder is a multiple of about ulp(x) * 2^-24, exact only while |x|
+// stays above 2^-100).  Zero, non-finite and extreme magnitudes take the
+// IEEE division.
 __device__ __forceinline__ float div_by(float x, float s, float r) {
   const float q0 = __fmul_rn(x, r);
   const float q = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
-  const float aq = fabsf(q0);
-  return (aq >= 0x1p-125f && aq <= 0x1p+125f) ? q : __fdiv_rn(x, s);
+  const float aq = fabsf(q0), ax = fabsf(x);
+  return (aq >= 0x1p-125f && aq <= 0x1p+125f && ax >= 0x1p-100f && ax <= 0x1p+125f) ? q : __fdiv_rn(x, s);
 }
 
 __device__ __forceinline__ void store_elem8(int kind, const float v[8], uint8_t* dst) {
@@ -557,13 +561,25 @@ __device__ __forceinline__ float block_amax_reduce(float v) {
 }
 
 // ---------------------------------------------------------------------------
-// Pass 2: the fused optimizer update over the chunk table.
+// Passes 2+3: the apply kernel.  A persistent grid pulls jobs from a job
+// list with an atomic ticket.  An update job runs the optimizer over one
+// chunk (unscale, clip, SGD/Adam/AdamW, direct requant, per-tensor amax) and
+// then counts itself done for its tensor; a requant job re-quantises one
+// chunk of a per-tensor-scaled tensor once every update job of that tensor is
+// done (the scale needs the whole tensor's amax).  The host orders the list
+// so a tensor's requant jobs come a grid-width after its last update job,
+// interleaved with the next tensor's update jobs: the ALU-heavy requant work
+// overlaps the memory-bound update work instead of running as its own pass.
+// A job only ever waits for jobs fetched before it, which are held by
+// running CTAs, so the wait always ends; it is still bounded by
+// %globaltimer and reports through Decision::err instead of hanging.
 // ---------------------------------------------------------------------------
-struct UpdateArgs {
+struct ApplyArgs {
   OptConsts oc;
   int use_scaler;
-  const Chunk* chunks;
-  int nchunks;
+  const Chunk* chunks;  // update chunk table (requant jobs index it too)
+  const uint32_t* jobs; // bit 31: requant job; low bits: chunk index
+  int njobs;
   const TensorDesc* tensors;
   float* master;
   float* s1;
@@ -571,126 +587,222 @@ struct UpdateArgs {
   const void* grad;
   uint8_t* qout;
   uint32_t* amax_slots;
-  const Decision* dec;
+  float* qscale;
+  uint32_t* sync;  // [0] job ticket, [1..] update jobs done per tensor
+  Decision* dec;
 };
 
+constexpr uint32_t kRequantJob = 0x80000000u;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 template <int GDT, int OPT>
-__global__ void __launch_bounds__(kThreads, 4) update_kernel(UpdateArgs a) {
+__device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch, const Divisor& dv, bool clipped,
+                                             float coef, const Fp4Thr* s_mx, const Fp4Thr* s_nv, uint8_t* stage) {
+  const OptConsts& oc = a.oc;
+  const TensorDesc td = a.tensors[ch.tensor];
+  const int kind = td.quant;
+  const bool tensor_scaled = (kind == Q_FP8_E4M3_TENSOR || kind == Q_NVFP4_TENSOR);
+  float amax = 0.0f;
+  const int64_t end = ch.start + ch.len;
+  for (int64_t tb = ch.start; tb < end; tb += kTile) {
+    const int64_t e0 = tb + (int64_t)threadIdx.x * kVec;
+    const bool act = e0 < end;
+    float p[8], m[8], v[8], g[8];
+    if (act) {
+      const float4* pp = reinterpret_cast<const float4*>(a.master + e0);
+      float4 p0 = __ldcs(pp), p1 = __ldcs(pp + 1);
+      p[0] = p0.x; p[1] = p0.y; p[2] = p0.z; p[3] = p0.w;
+      p[4] = p1.x; p[5] = p1.y; p[6] = p1.z; p[7] = p1.w;
+      if (OPT != OPT_SGD || oc.use_mu) {
+        const float4* mp = reinterpret_cast<const float4*>(a.s1 + e0);
+        float4 m0 = __ldcs(mp), m1 = __ldcs(mp + 1);
+        m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w;
+        m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
+      }
+      if (OPT != OPT_SGD) {
+        const float4* vp = reinterpret_cast<const float4*>(a.s2 + e0);
+        float4 v0 = __ldcs(vp), v1 = __ldcs(vp + 1);
+        v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
+        v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
+      }
+      grad8<GDT>(a.grad, e0, a.use_scaler, dv, g);
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        float gk = clipped ? __fmul_rn(g[k], coef) : g[k];
+        if (OPT == OPT_SGD)
+          sgd_elem(p[k], gk, m[k], oc);
+        else if (OPT == OPT_ADAM)
+          adam_elem<false>(p[k], gk, m[k], v[k], oc);
+        else
+          adam_elem<true>(p[k], gk, m[k], v[k], oc);
+      }
+      float4* pw = reinterpret_cast<float4*>(a.master + e0);
+      pw[0] = make_float4(p[0], p[1], p[2], p[3]);
+      pw[1] = make_float4(p[4], p[5], p[6], p[7]);
+      if (OPT != OPT_SGD || oc.use_mu) {
+        float4* mw = reinterpret_cast<float4*>(a.s1 + e0);
+        __stcs(mw, make_float4(m[0], m[1], m[2], m[3]));
+        __stcs(mw + 1, make_float4(m[4], m[5], m[6], m[7]));
+      }
+      if (OPT != OPT_SGD) {
+        float4* vw = reinterpret_cast<float4*>(a.s2 + e0);
+        __stcs(vw, make_float4(v[0], v[1], v[2], v[3]));
+        __stcs(vw + 1, make_float4(v[4], v[5], v[6], v[7]));
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; k++) p[k] = 0.0f;
+    }
+    // ---- requant epilogue (uniform per chunk) ----
+    if (kind == Q_NONE) continue;
+    if (tensor_scaled) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) amax = amax_acc(amax, p[k]);
+    } else if (kind == Q_MXFP4 || kind == Q_NVFP4) {
+      // warp-uniform: the warp's first element is inside the chunk
+      if (tb + (int64_t)(threadIdx.x & ~31) * kVec < end) {
+        const int64_t tile_in_tensor = (tb - td.off) / kTile;
+        const int w = threadIdx.x >> 5;
+        uint8_t* ws = stage + w * kWarpStage;
+        if (kind == Q_MXFP4) {
+          stage_fp4<true>(p, ws, s_mx);
+          __syncwarp();
+          flush_warp<true>(ws, a.qout + td.qoff + tile_in_tensor * kMxTileBytes + w * kMxWarpBytes, kMxWarpBytes);
+        } else {
+          stage_fp4<false>(p, ws, s_nv);
+          __syncwarp();
+          flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
+        }
+        __syncwarp();
+      }
+    } else if (act) {
+      const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
+      store_elem8(kind, p, a.qout + td.qoff + (e0 - td.off) * esz);
+    }
+  }
+  if (tensor_scaled) {
+    const float bm = block_amax_reduce(amax);
+    if (threadIdx.x == 0) atomicMax(&a.amax_slots[ch.tensor], __float_as_uint(bm));
+    // publish: every thread's stores of this chunk, then the done count
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) atomicAdd(&a.sync[1 + ch.tensor], 1u);
+  }
+}
+
+__device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& ch, const Fp4Thr* s_nv,
+                                              uint8_t* stage) {
+  const TensorDesc td = a.tensors[ch.tensor];
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const uint32_t* done = &a.sync[1 + ch.tensor];
+    int ok = 1;
+    if (ld_acquire(done) < (uint32_t)td.nchunks) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (ld_acquire(done) < (uint32_t)td.nchunks) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          ok = 0;
+          atomicOr(&a.dec->err, 1);
+          break;
+        }
+        __nanosleep(256);
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const int kind = td.quant;
+  const float s = tensor_scale_from_amax(kind, __ldcg(&a.amax_slots[ch.tensor]));
+  const float r = __frcp_rn(s);
+  if (ch.start == td.off && threadIdx.x == 0) a.qscale[ch.tensor] = s;
+  const int64_t end = ch.start + ch.len;
+  for (int64_t tb = ch.start; tb < end; tb += kTile) {
+    const int64_t e0 = tb + (int64_t)threadIdx.x * kVec;
+    const bool act = e0 < end;
+    float x[8];
+    if (act) {
+      const float4* pp = reinterpret_cast<const float4*>(a.master + e0);
+      float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
+      x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
+      x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
+#pragma unroll
+      for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; k++) x[k] = 0.0f;
+    }
+    if (kind == Q_NVFP4_TENSOR) {
+      if (tb + (int64_t)(threadIdx.x & ~31) * kVec < end) {
+        const int64_t tile_in_tensor = (tb - td.off) / kTile;
+        const int w = threadIdx.x >> 5;
+        uint8_t* ws = stage + w * kWarpStage;
+        stage_fp4<false>(x, ws, s_nv);
+        __syncwarp();
+        flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
+        __syncwarp();
+      }
+    } else if (act) {
+      store_elem8(Q_FP8_E4M3, x, a.qout + td.qoff + (e0 - td.off));
+    }
+  }
+}
+
+template <int GDT, int OPT>
+__global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
+  __shared__ uint32_t s_next;
   const Decision* dec = a.dec;
   if (dec->skip) return;
   const Divisor dv = make_divisor(unscale_divisor<GDT>(dec->scale_used));
   const bool clipped = dec->clipped != 0;
   const float coef = dec->coef;
   load_thr_smem(s_mx, s_nv);
+  if (threadIdx.x == 0) s_next = atomicAdd(&a.sync[0], 1u);
   __syncthreads();
-  const OptConsts oc = a.oc;
-
-  for (int c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
-    const Chunk ch = a.chunks[c];
-    const TensorDesc td = a.tensors[ch.tensor];
-    const int kind = td.quant;
-    const bool tensor_scaled = (kind == Q_FP8_E4M3_TENSOR || kind == Q_NVFP4_TENSOR);
-    float amax = 0.0f;
-    const int64_t end = ch.start + ch.len;
-    for (int64_t tb = ch.start; tb < end; tb += kTile) {
-      const int64_t e0 = tb + (int64_t)threadIdx.x * kVec;
-      const bool act = e0 < end;
-      float p[8], m[8], v[8], g[8];
-      if (act) {
-        const float4* pp = reinterpret_cast<const float4*>(a.master + e0);
-        float4 p0 = pp[0], p1 = pp[1];
-        p[0] = p0.x; p[1] = p0.y; p[2] = p0.z; p[3] = p0.w;
-        p[4] = p1.x; p[5] = p1.y; p[6] = p1.z; p[7] = p1.w;
-        if (OPT != OPT_SGD || oc.use_mu) {
-          const float4* mp = reinterpret_cast<const float4*>(a.s1 + e0);
-          float4 m0 = __ldcs(mp), m1 = __ldcs(mp + 1);
-          m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w;
-          m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
-        }
-        if (OPT != OPT_SGD) {
-          const float4* vp = reinterpret_cast<const float4*>(a.s2 + e0);
-          float4 v0 = __ldcs(vp), v1 = __ldcs(vp + 1);
-          v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
-          v[4] = v1.x; v[5] = v1.y; v[6] = v1.z; v[7] = v1.w;
-        }
-        grad8<GDT>(a.grad, e0, a.use_scaler, dv, g);
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-          float gk = clipped ? __fmul_rn(g[k], coef) : g[k];
-          if (OPT == OPT_SGD)
-            sgd_elem(p[k], gk, m[k], oc);
-          else if (OPT == OPT_ADAM)
-            adam_elem<false>(p[k], gk, m[k], v[k], oc);
-          else
-            adam_elem<true>(p[k], gk, m[k], v[k], oc);
-        }
-        float4* pw = reinterpret_cast<float4*>(a.master + e0);
-        pw[0] = make_float4(p[0], p[1], p[2], p[3]);
-        pw[1] = make_float4(p[4], p[5], p[6], p[7]);
-        if (OPT != OPT_SGD || oc.use_mu) {
-          float4* mw = reinterpret_cast<float4*>(a.s1 + e0);
-          __stcs(mw, make_float4(m[0], m[1], m[2], m[3]));
-          __stcs(mw + 1, make_float4(m[4], m[5], m[6], m[7]));
-        }
-        if (OPT != OPT_SGD) {
-          float4* vw = reinterpret_cast<float4*>(a.s2 + e0);
-          __stcs(vw, make_float4(v[0], v[1], v[2], v[3]));
-          __stcs(vw + 1, make_float4(v[4], v[5], v[6], v[7]));
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; k++) p[k] = 0.0f;
-      }
-      // ---- requant epilogue (uniform per chunk) ----
-      if (kind == Q_NONE) continue;
-      const int64_t te = e0 - td.off;  // element offset within the tensor
-      if (tensor_scaled) {
-#pragma unroll
-        for (int k = 0; k < 8; k++) amax = amax_acc(amax, p[k]);
-      } else if (kind == Q_MXFP4 || kind == Q_NVFP4) {
-        // warp-uniform: the warp's first element is inside the chunk
-        if (tb + (int64_t)(threadIdx.x & ~31) * kVec < end) {
-          const int64_t tile_in_tensor = (tb - td.off) / kTile;
-          uint8_t* ws = stage + (threadIdx.x >> 5) * kWarpStage;
-          const int w = threadIdx.x >> 5;
-          if (kind == Q_MXFP4) {
-            stage_fp4<true>(p, ws, s_mx);
-            __syncwarp();
-            flush_warp<true>(ws, a.qout + td.qoff + tile_in_tensor * kMxTileBytes + w * kMxWarpBytes, kMxWarpBytes);
-          } else {
-            stage_fp4<false>(p, ws, s_nv);
-            __syncwarp();
-            flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
-          }
-          __syncwarp();
-        }
-      } else if (act) {
-        const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
-        store_elem8(kind, p, a.qout + td.qoff + te * esz);
-      }
-    }
-    if (tensor_scaled) {
-      float bm = block_amax_reduce(amax);
-      if (threadIdx.x == 0) atomicMax(&a.amax_slots[ch.tensor], __float_as_uint(bm));
-    }
+  uint32_t j = s_next;
+  while (j < (uint32_t)a.njobs) {
+    uint32_t nxt = 0;
+    if (threadIdx.x == 0) nxt = atomicAdd(&a.sync[0], 1u);  // next job, fetched early
+    const uint32_t job = a.jobs[j];
+    const Chunk ch = a.chunks[job & ~kRequantJob];
+    if (job & kRequantJob)
+      requant_chunk(a, ch, s_nv, stage);
+    else
+      update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, stage);
+    __syncthreads();
+    if (threadIdx.x == 0) s_next = nxt;
+    __syncthreads();
+    j = s_next;
   }
 }
 
 template <int GDT, int OPT>
-static int grid_for_update(int device) {
+static int grid_for_apply(int device) {
   int sms = 148, per = 4;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, update_kernel<GDT, OPT>, kThreads, 0);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, apply_kernel<GDT, OPT>, kThreads, 0);
   if (per < 1) per = 1;
   return sms * per;
 }
 
-int update_grid(int gdt, int opt, int device) {
+int apply_grid(int gdt, int opt, int device) {
 #define ODY_G(G, O) \
-  if (gdt == G && opt == O) return grid_for_update<G, O>(device);
+  if (gdt == G && opt == O) return grid_for_apply<G, O>(device);
   ODY_G(DT_F32, OPT_SGD) ODY_G(DT_F32, OPT_ADAM) ODY_G(DT_F32, OPT_ADAMW)
   ODY_G(DT_F16, OPT_SGD) ODY_G(DT_F16, OPT_ADAM) ODY_G(DT_F16, OPT_ADAMW)
   ODY_G(DT_BF16, OPT_SGD) ODY_G(DT_BF16, OPT_ADAM) ODY_G(DT_BF16, OPT_ADAMW)
@@ -698,14 +810,15 @@ int update_grid(int gdt, int opt, int device) {
   return 148;
 }
 
-cudaError_t launch_update(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
-                          int nchunks, const TensorDesc* tensors, float* master, float* s1, float* s2,
-                          const void* grad, uint8_t* qout, uint32_t* amax_slots, const Decision* dec,
-                          int grid, cudaStream_t st) {
-  UpdateArgs a{oc, use_scaler, chunks, nchunks, tensors, master, s1, s2, grad, qout, amax_slots, dec};
+cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
+                         const uint32_t* jobs, int njobs, const TensorDesc* tensors, float* master, float* s1,
+                         float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
+                         uint32_t* sync, Decision* dec, int grid, cudaStream_t st) {
+  ApplyArgs a{oc, use_scaler, chunks, jobs, njobs, tensors, master, s1, s2, grad, qout, amax_slots, qscale, sync,
+              dec};
 #define ODY_L(G, O)                                                    \
   if (gdt == G && opt == O) {                                          \
-    update_kernel<G, O><<<grid, kThreads, 0, st>>>(a);                 \
+    apply_kernel<G, O><<<grid, kThreads, 0, st>>>(a);                  \
     return cudaGetLastError();                                         \
   }
   ODY_L(DT_F32, OPT_SGD) ODY_L(DT_F32, OPT_ADAM) ODY_L(DT_F32, OPT_ADAMW)
@@ -713,84 +826,6 @@ cudaError_t launch_update(int gdt, int opt, const OptConsts& oc, int use_scaler,
   ODY_L(DT_BF16, OPT_SGD) ODY_L(DT_BF16, OPT_ADAM) ODY_L(DT_BF16, OPT_ADAMW)
 #undef ODY_L
   return cudaErrorInvalidValue;
-}
-
-// ---------------------------------------------------------------------------
-// Pass 3: per-tensor-scaled requant of the new master weights.
-// ---------------------------------------------------------------------------
-struct RequantArgs {
-  const Chunk* chunks;
-  int nchunks;
-  const TensorDesc* tensors;
-  const float* master;
-  uint8_t* qout;
-  const uint32_t* amax_slots;
-  float* qscale;
-  const Decision* dec;
-};
-
-__global__ void __launch_bounds__(kThreads, 4) requant_kernel(RequantArgs a) {
-  __shared__ Fp4Thr s_mx[256];
-  __shared__ Fp4Thr s_nv[128];
-  __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
-  if (a.dec->skip) return;
-  load_thr_smem(s_mx, s_nv);
-  __syncthreads();
-  for (int c = blockIdx.x; c < a.nchunks; c += gridDim.x) {
-    const Chunk ch = a.chunks[c];
-    const TensorDesc td = a.tensors[ch.tensor];
-    const int kind = td.quant;
-    const float s = tensor_scale_from_amax(kind, __ldcg(&a.amax_slots[ch.tensor]));
-    const float r = __frcp_rn(s);
-    if (ch.start == td.off && threadIdx.x == 0) a.qscale[ch.tensor] = s;
-    const int64_t end = ch.start + ch.len;
-    for (int64_t tb = ch.start; tb < end; tb += kTile) {
-      const int64_t e0 = tb + (int64_t)threadIdx.x * kVec;
-      const bool act = e0 < end;
-      float x[8];
-      if (act) {
-        const float4* pp = reinterpret_cast<const float4*>(a.master + e0);
-        float4 p0 = __ldcs(pp), p1 = __ldcs(pp + 1);
-        x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
-        x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
-#pragma unroll
-        for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; k++) x[k] = 0.0f;
-      }
-      if (kind == Q_NVFP4_TENSOR) {
-        if (tb + (int64_t)(threadIdx.x & ~31) * kVec < end) {
-          const int64_t tile_in_tensor = (tb - td.off) / kTile;
-          const int w = threadIdx.x >> 5;
-          uint8_t* ws = stage + w * kWarpStage;
-          stage_fp4<false>(x, ws, s_nv);
-          __syncwarp();
-          flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
-          __syncwarp();
-        }
-      } else if (act) {
-        store_elem8(Q_FP8_E4M3, x, a.qout + td.qoff + (e0 - td.off));
-      }
-    }
-  }
-}
-
-int requant_grid(int device) {
-  int sms = 148, per = 4;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, requant_kernel, kThreads, 0);
-  if (per < 1) per = 1;
-  return sms * per;
-}
-
-cudaError_t launch_requant(const Chunk* chunks, int nchunks, const TensorDesc* tensors,
-                           const float* master, uint8_t* qout, const uint32_t* amax_slots,
-                           float* qscale, const Decision* dec, int grid, cudaStream_t st) {
-  if (nchunks == 0) return cudaSuccess;
-  RequantArgs a{chunks, nchunks, tensors, master, qout, amax_slots, qscale, dec};
-  requant_kernel<<<grid, kThreads, 0, st>>>(a);
-  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------

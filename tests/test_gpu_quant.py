@@ -207,4 +207,8 @@ def test_exact_division_shortcut(ody):
         f = ody.lib().odyx_selftest_divide
         f.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]
         assert f(x.data_ptr(), s.data_ptr(), n, fast.data_ptr(), ieee.data_ptr()) == 0
-        assert torch.equal(fast.view(torch.int32), ieee.view(torch.int32))
+        bad = (fast.view(torch.int32) != ieee.view(torch.int32)).nonzero().flatten()
+        if bad.numel():
+            i = bad[:5].tolist()
+            pytest.fail(f"{bad.numel()} mismatches, e.g. x={x[i].tolist()} s={s[i].tolist()} "
+                        f"fast={fast[i].tolist()} ieee={ieee[i].tolist()}")

@@ -109,6 +109,7 @@ struct ody_ctx {
   Chunk* d_chunks_upd = nullptr;
   uint32_t* d_jobs = nullptr;
   uint32_t* sync = nullptr;  // job ticket + per-tensor done counts
+  Fp4Thr* comp_thr = nullptr;  // per tensor: composite NVFP4 thresholds
   TensorDesc* d_tdesc = nullptr;
   StatsPartial* partials = nullptr;
   unsigned* ticket = nullptr;
@@ -429,6 +430,7 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
     ODY_CUDA(cudaMemcpyAsync(c->d_jobs, c->jobs.data(), sizeof(uint32_t) * c->jobs.size(), cudaMemcpyHostToDevice,
                              c->stream));
   ODY_CUDA(dalloc(&c->sync, sizeof(uint32_t) * (nl + 1)));
+  ODY_CUDA(dalloc(&c->comp_thr, sizeof(Fp4Thr) * 128 * (nl > 0 ? nl : 1)));
   ODY_CUDA(cudaMemsetAsync(c->sync, 0, sizeof(uint32_t) * (nl + 1), c->stream));
   c->grid_stats = stats_grid(c->cfg.device);
   ODY_CUDA(dalloc(&c->partials, sizeof(StatsPartial) * c->grid_stats));
@@ -572,6 +574,8 @@ static OptConsts make_consts(const ody_config& cfg, int64_t t) {
   if (t > 0) {
     o.bc1 = (float)(1.0 - pow(cfg.beta1, (double)t));
     o.bc2 = (float)(1.0 - pow(cfg.beta2, (double)t));
+    o.rbc1 = 1.0f / o.bc1;  // IEEE float division: the correctly rounded reciprocal
+    o.rbc2 = 1.0f / o.bc2;
   }
   return o;
 }
@@ -632,7 +636,7 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   if (!c->jobs.empty()) {
     e = launch_apply(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd, c->d_jobs,
                      (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout, c->amax, c->qscale,
-                     c->sync, c->dec, c->grid_apply, c->stream);
+                     c->sync, c->comp_thr, c->dec, c->grid_apply, c->stream);
     if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("apply kernel: ") + cudaGetErrorString(e));
   }
   if (tev) ODY_CUDA(cudaEventRecord(tev[3], c->stream));
@@ -867,7 +871,7 @@ extern "C" void ody_ctx_destroy(ody_ctx* c) {
     if (api) api->commDestroy(c->comm);
   }
   void* bufs[] = {c->master, c->s1, c->s2, c->grad, c->qout, c->qscale, c->amax, c->d_chunks_upd,
-                  c->d_jobs, c->sync, c->d_tdesc, c->partials, c->ticket, c->scaler, c->dec,
+                  c->d_jobs, c->sync, c->comp_thr, c->d_tdesc, c->partials, c->ticket, c->scaler, c->dec,
                   c->local_stats, c->gathered};
   for (void* b : bufs)
     if (b) cudaFree(b);

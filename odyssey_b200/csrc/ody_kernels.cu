@@ -448,10 +448,23 @@ __device__ __forceinline__ bool any_nonfinite8(const float v[8]) {
 }
 
 // the threshold ladder without special cases (finite x, positive finite scale)
+// compare producing an all-ones (true) or zero (false) mask
+__device__ __forceinline__ uint32_t ge_mask(float a, float b) {
+  uint32_t d;
+  asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(d) : "f"(a), "f"(b));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t fp4_encode_plain(float x, const float* t) {
   const float a = fabsf(x);
-  const uint32_t mag = 2u * (a >= t[1]) + (a >= t[2]) + (a >= t[3]) + (a >= t[4]) + (a >= t[5]) + (a >= t[6]);
-  return ((uint32_t)((x < 0.0f) && (a >= t[0])) << 3) | mag;
+  // each true compare contributes -1; the first threshold counts twice
+  // (magnitudes 0, 2, 3, .., 7: the 0.5 code is never produced)
+  const uint32_t m1 = ge_mask(a, t[1]);
+  const uint32_t neg = (m1 + m1 + ge_mask(a, t[2])) + (ge_mask(a, t[3]) + ge_mask(a, t[4])) +
+                       (ge_mask(a, t[5]) + ge_mask(a, t[6]));
+  const uint32_t mag = 0u - neg;
+  const uint32_t sgn = ge_mask(-x, t[0]) & 8u;  // x < 0 with RN(|x|/s) != 0
+  return sgn | mag;
 }
 
 template <bool MX>
@@ -481,6 +494,41 @@ __device__ __forceinline__ void stage_fp4(const float v[8], uint8_t* ws, const F
   if (j == (MX ? 3 : 1)) ws[blk * bb + bb - 1] = e;
 }
 
+// NVFP4 with a per-tensor scale s (r = RN(1/s)): the reference encode of
+// x' = RN(x / s).  The block amax of x' is RN(amax(|x|) / s) (division is
+// monotone), and the codes come from the tensor's composite thresholds on x
+// itself; blocks that need the special cases divide and take the general
+// encode.
+__device__ __forceinline__ void stage_nvfp4_scaled(const float v[8], float s, float r, uint8_t* ws,
+                                                   const Fp4Thr* thr, const Fp4Thr* comp) {
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
+  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+  const float amq = div_by(am, s, r);
+  const uint8_t e = e4m3_scale_from_f32(block_scale_value(amq));
+  const bool z = e == 0;
+  const bool special = z || any_nonfinite8(v);
+  const int lane = threadIdx.x & 31;
+  const int blk = lane >> 1, j = lane & 1;
+  uint8_t* dst = ws + blk * 9 + 4 * j;
+  if (!special) {
+    const float* t = comp[e].t;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      dst[i] = (uint8_t)((fp4_encode_plain(v[2 * i], t) << 4) | fp4_encode_plain(v[2 * i + 1], t));
+  } else {
+    const float* t = thr[e].t;
+    float q[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) q[k] = div_by(v[k], s, r);
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      dst[i] = (uint8_t)((fp4_encode(q[2 * i], t, z) << 4) | fp4_encode(q[2 * i + 1], t, z));
+  }
+  if (j == 1) ws[blk * 9 + 8] = e;
+}
+
 // write a warp's staged bytes: whole 16-byte (NVFP4) / 8-byte (MXFP4) stores
 // when the destination is aligned and the whole slice may be written, else
 // bytes up to `limit`
@@ -501,20 +549,6 @@ __device__ __forceinline__ void flush_warp(const uint8_t* ws, uint8_t* dst, int6
   }
 }
 
-// Exact division x / s with s's reciprocal r = RN(1/s) precomputed: the
-// product estimate is corrected once with the exactly computed remainder
-// (Markstein's correction: q0 = x*r is within one ulp, x - q0*s is exact by
-// FMA, and q0 + rem*r rounded once is the correctly rounded quotient when r
-// is the correctly rounded reciprocal, provided nothing under- or overflows:
-// the remainder is a multiple of about ulp(x) * 2^-24, exact only while |x|
-// stays above 2^-100).  Zero, non-finite and extreme magnitudes take the
-// IEEE division.
-__device__ __forceinline__ float div_by(float x, float s, float r) {
-  const float q0 = __fmul_rn(x, r);
-  const float q = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
-  const float aq = fabsf(q0), ax = fabsf(x);
-  return (aq >= 0x1p-125f && aq <= 0x1p+125f && ax >= 0x1p-100f && ax <= 0x1p+125f) ? q : __fdiv_rn(x, s);
-}
 
 __device__ __forceinline__ void store_elem8(int kind, const float v[8], uint8_t* dst) {
   if (kind == Q_FP16 || kind == Q_BF16) {
@@ -589,8 +623,11 @@ struct ApplyArgs {
   uint32_t* amax_slots;
   float* qscale;
   uint32_t* sync;  // [0] job ticket, [1..] update jobs done per tensor
+  Fp4Thr* comp_thr;  // per tensor: 128 composite NVFP4 threshold rows
   Decision* dec;
 };
+
+__device__ __forceinline__ void finish_tensor(const ApplyArgs& a, int tensor, const TensorDesc& td);
 
 constexpr uint32_t kRequantJob = 0x80000000u;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
@@ -698,20 +735,67 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
     // publish: every thread's stores of this chunk, then the done count
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) atomicAdd(&a.sync[1 + ch.tensor], 1u);
+    __shared__ int s_last;
+    if (threadIdx.x == 0)
+      s_last = atomicAdd(&a.sync[1 + ch.tensor], 1u) == (uint32_t)td.nchunks - 1u;
+    __syncthreads();
+    if (s_last) finish_tensor(a, ch.tensor, td);
   }
 }
 
+// Run by the CTA that completed a tensor's last update chunk: the tensor's
+// amax is final, so its per-tensor scale is fixed.  For NVFP4 it also builds
+// the tensor's composite threshold table: for every E4M3 block scale sf and
+// ladder value T, the least float x with RN(RN(x / s_t) / sf) >= T (both
+// divisions IEEE, as the encode defines them; the composite is monotone in
+// x).  Requant jobs then encode x directly with compares.  The done count
+// goes to nchunks + 1 when this is published.
+__device__ __forceinline__ void finish_tensor(const ApplyArgs& a, int tensor, const TensorDesc& td) {
+  __threadfence();
+  const float st = tensor_scale_from_amax(td.quant, __ldcg(&a.amax_slots[tensor]));
+  if (td.quant == Q_NVFP4_TENSOR) {
+    float* tab = reinterpret_cast<float*>(a.comp_thr + (size_t)tensor * 128);
+    for (int idx = threadIdx.x; idx < 127 * 7; idx += blockDim.x) {
+      const int e = idx / 7, k = idx % 7;
+      const float sf = e4m3_to_f32((uint8_t)e);
+      const float T = k == 0 ? __uint_as_float(1u) : (k == 1 ? 0.5f : k == 2 ? 1.25f : k == 3 ? 1.75f
+                                                     : k == 4 ? 2.5f : k == 5 ? 3.5f : 5.0f);
+      uint32_t lo = 0, hi = 0x7f800000u;
+      float res;
+      if (!(__fdiv_rn(__fdiv_rn(__uint_as_float(hi), st), sf) >= T)) {
+        res = __uint_as_float(0x7fc00000u);
+      } else if (__fdiv_rn(__fdiv_rn(0.0f, st), sf) >= T) {
+        res = 0.0f;
+      } else {
+        while (hi - lo > 1) {
+          const uint32_t mid = lo + (hi - lo) / 2;
+          if (__fdiv_rn(__fdiv_rn(__uint_as_float(mid), st), sf) >= T)
+            hi = mid;
+          else
+            lo = mid;
+        }
+        res = __uint_as_float(hi);
+      }
+      tab[e * 8 + k] = res;
+    }
+  }
+  if (threadIdx.x == 0) a.qscale[tensor] = st;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) atomicAdd(&a.sync[1 + tensor], 1u);
+}
+
 __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& ch, const Fp4Thr* s_nv,
-                                              uint8_t* stage) {
+                                              uint8_t* stage, Fp4Thr* s_comp) {
   const TensorDesc td = a.tensors[ch.tensor];
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
     const uint32_t* done = &a.sync[1 + ch.tensor];
+    const uint32_t ready = (uint32_t)td.nchunks + 1u;
     int ok = 1;
-    if (ld_acquire(done) < (uint32_t)td.nchunks) {
+    if (ld_acquire(done) < ready) {
       const unsigned long long t0 = globaltimer_ns();
-      while (ld_acquire(done) < (uint32_t)td.nchunks) {
+      while (ld_acquire(done) < ready) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
           ok = 0;
           atomicOr(&a.dec->err, 1);
@@ -725,9 +809,15 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
   __syncthreads();
   if (!s_ok) return;
   const int kind = td.quant;
-  const float s = tensor_scale_from_amax(kind, __ldcg(&a.amax_slots[ch.tensor]));
+  const float s = __ldcg(&a.qscale[ch.tensor]);
   const float r = __frcp_rn(s);
-  if (ch.start == td.off && threadIdx.x == 0) a.qscale[ch.tensor] = s;
+  const bool nv = kind == Q_NVFP4_TENSOR;
+  if (nv) {
+    const float4* src = reinterpret_cast<const float4*>(a.comp_thr + (size_t)ch.tensor * 128);
+    float4* dst = reinterpret_cast<float4*>(s_comp);
+    for (int i = threadIdx.x; i < 128 * 2; i += blockDim.x) dst[i] = __ldcg(src + i);
+    __syncthreads();
+  }
   const int64_t end = ch.start + ch.len;
   for (int64_t tb = ch.start; tb < end; tb += kTile) {
     const int64_t e0 = tb + (int64_t)threadIdx.x * kVec;
@@ -738,23 +828,23 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
       float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
       x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
       x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
-#pragma unroll
-      for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
     } else {
 #pragma unroll
       for (int k = 0; k < 8; k++) x[k] = 0.0f;
     }
-    if (kind == Q_NVFP4_TENSOR) {
+    if (nv) {
       if (tb + (int64_t)(threadIdx.x & ~31) * kVec < end) {
         const int64_t tile_in_tensor = (tb - td.off) / kTile;
         const int w = threadIdx.x >> 5;
         uint8_t* ws = stage + w * kWarpStage;
-        stage_fp4<false>(x, ws, s_nv);
+        stage_nvfp4_scaled(x, s, r, ws, s_nv, s_comp);
         __syncwarp();
         flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
         __syncwarp();
       }
     } else if (act) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
       store_elem8(Q_FP8_E4M3, x, a.qout + td.qoff + (e0 - td.off));
     }
   }
@@ -766,6 +856,7 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ Fp4Thr s_nv[128];
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
   __shared__ uint32_t s_next;
+  __shared__ __align__(16) Fp4Thr s_comp[128];
   const Decision* dec = a.dec;
   if (dec->skip) return;
   const Divisor dv = make_divisor(unscale_divisor<GDT>(dec->scale_used));
@@ -781,7 +872,7 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
     const uint32_t job = a.jobs[j];
     const Chunk ch = a.chunks[job & ~kRequantJob];
     if (job & kRequantJob)
-      requant_chunk(a, ch, s_nv, stage);
+      requant_chunk(a, ch, s_nv, stage, s_comp);
     else
       update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, stage);
     __syncthreads();
@@ -813,9 +904,9 @@ int apply_grid(int gdt, int opt, int device) {
 cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
                          const uint32_t* jobs, int njobs, const TensorDesc* tensors, float* master, float* s1,
                          float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
-                         uint32_t* sync, Decision* dec, int grid, cudaStream_t st) {
+                         uint32_t* sync, Fp4Thr* comp_thr, Decision* dec, int grid, cudaStream_t st) {
   ApplyArgs a{oc, use_scaler, chunks, jobs, njobs, tensors, master, s1, s2, grad, qout, amax_slots, qscale, sync,
-              dec};
+              comp_thr, dec};
 #define ODY_L(G, O)                                                    \
   if (gdt == G && opt == O) {                                          \
     apply_kernel<G, O><<<grid, kThreads, 0, st>>>(a);                  \

@@ -324,8 +324,8 @@ static cudaError_t dalloc(T** p, size_t bytes) {
 }
 
 // Job list of the apply kernel: every update chunk in arena order; the
-// requant chunks of a per-tensor-scaled tensor become eligible a grid-width
-// of jobs after that tensor's last update job and are interleaved, up to two
+// requant chunks of a per-tensor-scaled tensor become eligible two grid-
+// widths of jobs after that tensor's last update job and are interleaved, up to two
 // per update job, with the following tensors' update jobs; what is left
 // runs at the end.
 static void build_jobs(ody_ctx* c) {
@@ -343,7 +343,7 @@ static void build_jobs(ody_ctx* c) {
         c->jobs.push_back(0x80000000u | pending[head++].second);
     }
     if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR)
-      for (size_t k = first; k < ci; k++) pending.push_back({c->jobs.size() + W, (uint32_t)k});
+      for (size_t k = first; k < ci; k++) pending.push_back({c->jobs.size() + 2 * W, (uint32_t)k});
   }
   while (head < pending.size()) c->jobs.push_back(0x80000000u | pending[head++].second);
 }

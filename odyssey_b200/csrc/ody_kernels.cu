@@ -750,31 +750,59 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
 // divisions IEEE, as the encode defines them; the composite is monotone in
 // x).  Requant jobs then encode x directly with compares.  The done count
 // goes to nchunks + 1 when this is published.
+__device__ __forceinline__ bool reaches(float q, float d, float T) { return __fdiv_rn(q, d) >= T; }
+
+// Least float q >= 0 with RN(q / d) >= T (d > 0 finite, T > 0), NaN if none:
+// start at the product estimate T*d, which is within a few ulps, and walk to
+// the boundary one ulp at a time (non-negative floats are ordered like their
+// bit patterns).  A walk that does not settle within 64 steps falls back to
+// bisection over the bit patterns.
+__device__ float least_reaching(float d, float T) {
+  const uint32_t kInf = 0x7f800000u;
+  if (!reaches(__uint_as_float(kInf - 1u), d, T)) return __uint_as_float(0x7fc00000u);
+  uint32_t q = __float_as_uint(__fmul_rn(T, d));
+  if (q >= kInf) q = kInf - 1u;
+  int steps = 0;
+  while (!reaches(__uint_as_float(q), d, T) && steps < 64) {
+    q++;
+    steps++;
+  }
+  while (q > 0 && reaches(__uint_as_float(q - 1u), d, T) && steps < 64) {
+    q--;
+    steps++;
+  }
+  if (steps >= 64) {
+    uint32_t lo = 0, hi = kInf - 1u;
+    if (reaches(0.0f, d, T)) return 0.0f;
+    while (hi - lo > 1) {
+      const uint32_t mid = lo + (hi - lo) / 2;
+      if (reaches(__uint_as_float(mid), d, T))
+        hi = mid;
+      else
+        lo = mid;
+    }
+    q = hi;
+  }
+  return __uint_as_float(q);
+}
+
 __device__ __forceinline__ void finish_tensor(const ApplyArgs& a, int tensor, const TensorDesc& td) {
   __threadfence();
   const float st = tensor_scale_from_amax(td.quant, __ldcg(&a.amax_slots[tensor]));
   if (td.quant == Q_NVFP4_TENSOR) {
+    // RN(RN(x/st)/sf) >= T  <=>  RN(x/st) >= q*  with q* the least float
+    // whose quotient by sf reaches T, so the composite threshold is the
+    // least x whose quotient by st reaches q*
     float* tab = reinterpret_cast<float*>(a.comp_thr + (size_t)tensor * 128);
-    for (int idx = threadIdx.x; idx < 127 * 7; idx += blockDim.x) {
+    for (int idx = threadIdx.x; idx < 128 * 7; idx += blockDim.x) {
       const int e = idx / 7, k = idx % 7;
       const float sf = e4m3_to_f32((uint8_t)e);
       const float T = k == 0 ? __uint_as_float(1u) : (k == 1 ? 0.5f : k == 2 ? 1.25f : k == 3 ? 1.75f
                                                      : k == 4 ? 2.5f : k == 5 ? 3.5f : 5.0f);
-      uint32_t lo = 0, hi = 0x7f800000u;
-      float res;
-      if (!(__fdiv_rn(__fdiv_rn(__uint_as_float(hi), st), sf) >= T)) {
-        res = __uint_as_float(0x7fc00000u);
-      } else if (__fdiv_rn(__fdiv_rn(0.0f, st), sf) >= T) {
-        res = 0.0f;
-      } else {
-        while (hi - lo > 1) {
-          const uint32_t mid = lo + (hi - lo) / 2;
-          if (__fdiv_rn(__fdiv_rn(__uint_as_float(mid), st), sf) >= T)
-            hi = mid;
-          else
-            lo = mid;
-        }
-        res = __uint_as_float(hi);
+      float res = __uint_as_float(0x7fc00000u);
+      if (e >= 1 && e <= 126) {
+        const float qs = least_reaching(sf, T);
+        if (qs == qs) res = qs == 0.0f ? 0.0f : least_reaching(st, qs);
       }
       tab[e * 8 + k] = res;
     }

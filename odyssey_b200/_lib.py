@@ -9,7 +9,7 @@ import os
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libodyssey_mp.so")
+LIB_PATH = os.environ.get("ODYSSEY_MP_LIB") or os.path.join(_HERE, "libodyssey_mp.so")
 
 OK = 0
 ERR_ARG, ERR_SHAPE, ERR_DTYPE, ERR_CUDA, ERR_NCCL, ERR_COMM_TIMEOUT, ERR_DEVICE_BOUNDS, ERR_STATE = range(-1, -9, -1)

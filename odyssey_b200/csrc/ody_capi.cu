@@ -429,9 +429,9 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   if (!c->jobs.empty())
     ODY_CUDA(cudaMemcpyAsync(c->d_jobs, c->jobs.data(), sizeof(uint32_t) * c->jobs.size(), cudaMemcpyHostToDevice,
                              c->stream));
-  ODY_CUDA(dalloc(&c->sync, sizeof(uint32_t) * (nl + 1)));
+  ODY_CUDA(dalloc(&c->sync, sizeof(uint32_t) * (2 * nl + 1)));
   ODY_CUDA(dalloc(&c->comp_thr, sizeof(Fp4Thr) * 128 * (nl > 0 ? nl : 1)));
-  ODY_CUDA(cudaMemsetAsync(c->sync, 0, sizeof(uint32_t) * (nl + 1), c->stream));
+  ODY_CUDA(cudaMemsetAsync(c->sync, 0, sizeof(uint32_t) * (2 * nl + 1), c->stream));
   c->grid_stats = stats_grid(c->cfg.device);
   ODY_CUDA(dalloc(&c->partials, sizeof(StatsPartial) * c->grid_stats));
   ODY_CUDA(dalloc(&c->ticket, sizeof(unsigned)));
@@ -636,7 +636,7 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   if (!c->jobs.empty()) {
     e = launch_apply(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd, c->d_jobs,
                      (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout, c->amax, c->qscale,
-                     c->sync, c->comp_thr, c->dec, c->grid_apply, c->stream);
+                     c->sync, nl, c->comp_thr, c->dec, c->grid_apply, c->stream);
     if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("apply kernel: ") + cudaGetErrorString(e));
   }
   if (tev) ODY_CUDA(cudaEventRecord(tev[3], c->stream));

@@ -367,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 4) stats_kernel(StatsArgs a) {
   }
   block_sum2(s, c);
   for (int j = threadIdx.x; j < a.ntensors; j += blockDim.x) a.amax_slots[j] = 0u;
-  for (int j = threadIdx.x; j < a.ntensors + 1; j += blockDim.x) a.sync[j] = 0u;
+  for (int j = threadIdx.x; j < 2 * a.ntensors + 1; j += blockDim.x) a.sync[j] = 0u;
   if (threadIdx.x == 0) {
     *a.ticket = 0u;
     if (a.world_mode == 0) {
@@ -622,7 +622,8 @@ struct ApplyArgs {
   uint8_t* qout;
   uint32_t* amax_slots;
   float* qscale;
-  uint32_t* sync;  // [0] job ticket, [1..] update jobs done per tensor
+  uint32_t* sync;  // [0] job ticket, [1, 1+nt) update jobs done, [1+nt, 1+2nt) table flags
+  int ntensors;
   Fp4Thr* comp_thr;  // per tensor: 128 composite NVFP4 threshold rows
   Decision* dec;
 };
@@ -733,23 +734,21 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
     const float bm = block_amax_reduce(amax);
     if (threadIdx.x == 0) atomicMax(&a.amax_slots[ch.tensor], __float_as_uint(bm));
     // publish: every thread's stores of this chunk, then the done count
+    // (fire and forget: an update job never waits for anything)
     __threadfence();
     __syncthreads();
-    __shared__ int s_last;
-    if (threadIdx.x == 0)
-      s_last = atomicAdd(&a.sync[1 + ch.tensor], 1u) == (uint32_t)td.nchunks - 1u;
-    __syncthreads();
-    if (s_last) finish_tensor(a, ch.tensor, td);
+    if (threadIdx.x == 0) atomicAdd(&a.sync[1 + ch.tensor], 1u);
   }
 }
 
-// Run by the CTA that completed a tensor's last update chunk: the tensor's
-// amax is final, so its per-tensor scale is fixed.  For NVFP4 it also builds
+// Run by the CTA that claimed the tensor (the first to need it for a requant
+// job) once all its update jobs are done: the tensor's amax is final, so its
+// per-tensor scale is fixed.  For NVFP4 it also builds
 // the tensor's composite threshold table: for every E4M3 block scale sf and
 // ladder value T, the least float x with RN(RN(x / s_t) / sf) >= T (both
 // divisions IEEE, as the encode defines them; the composite is monotone in
-// x).  Requant jobs then encode x directly with compares.  The done count
-// goes to nchunks + 1 when this is published.
+// x).  Requant jobs then encode x directly with compares.  The tensor's flag
+// goes to 2 when this is published.
 __device__ __forceinline__ bool reaches(float q, float d, float T) { return __fdiv_rn(q, d) >= T; }
 
 // Least float q >= 0 with RN(q / d) >= T (d > 0 finite, T > 0), NaN if none:
@@ -810,32 +809,12 @@ __device__ __forceinline__ void finish_tensor(const ApplyArgs& a, int tensor, co
   if (threadIdx.x == 0) a.qscale[tensor] = st;
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) atomicAdd(&a.sync[1 + tensor], 1u);
+  if (threadIdx.x == 0) atomicExch(&a.sync[1 + a.ntensors + tensor], 2u);
 }
 
 __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& ch, const Fp4Thr* s_nv,
                                               uint8_t* stage, Fp4Thr* s_comp) {
   const TensorDesc td = a.tensors[ch.tensor];
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) {
-    const uint32_t* done = &a.sync[1 + ch.tensor];
-    const uint32_t ready = (uint32_t)td.nchunks + 1u;
-    int ok = 1;
-    if (ld_acquire(done) < ready) {
-      const unsigned long long t0 = globaltimer_ns();
-      while (ld_acquire(done) < ready) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          ok = 0;
-          atomicOr(&a.dec->err, 1);
-          break;
-        }
-        __nanosleep(256);
-      }
-    }
-    s_ok = ok;
-  }
-  __syncthreads();
-  if (!s_ok) return;
   const int kind = td.quant;
   const float s = __ldcg(&a.qscale[ch.tensor]);
   const float r = __frcp_rn(s);
@@ -878,12 +857,43 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
   }
 }
 
+// Readiness of tensor t for requant, decided by thread 0 of a CTA whose next
+// job is a requant job of t: first every update job of t must be done (their
+// counts are fire and forget), then t's scale and thresholds must be
+// published.  The first CTA to get here claims the publication (flag 0 -> 1)
+// and does it itself; the others wait for flag 2.  Nobody waits while
+// holding a claim, so the waits always end; they are still bounded by
+// %globaltimer and report through Decision::err.
+enum : int { kWaitFailed = 0, kReady = 1, kMustPublish = 2 };
+
+__device__ __forceinline__ bool wait_at_least(const ApplyArgs& a, const uint32_t* p, uint32_t v) {
+  if (ld_acquire(p) >= v) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire(p) < v) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(&a.dec->err, 1);
+      return false;
+    }
+    __nanosleep(256);
+  }
+  return true;
+}
+
+__device__ __forceinline__ int tensor_readiness(const ApplyArgs& a, int t) {
+  uint32_t* flag = &a.sync[1 + a.ntensors + t];
+  if (ld_acquire(flag) == 2u) return kReady;
+  if (!wait_at_least(a, &a.sync[1 + t], (uint32_t)a.tensors[t].nchunks)) return kWaitFailed;
+  if (atomicCAS(flag, 0u, 1u) == 0u) return kMustPublish;
+  return wait_at_least(a, flag, 2u) ? kReady : kWaitFailed;
+}
+
 template <int GDT, int OPT>
 __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
   __shared__ uint32_t s_next;
+  __shared__ int s_state, s_tensor, s_ready_t;
   __shared__ __align__(16) Fp4Thr s_comp[128];
   const Decision* dec = a.dec;
   if (dec->skip) return;
@@ -891,22 +901,49 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   const bool clipped = dec->clipped != 0;
   const float coef = dec->coef;
   load_thr_smem(s_mx, s_nv);
-  if (threadIdx.x == 0) s_next = atomicAdd(&a.sync[0], 1u);
-  __syncthreads();
-  uint32_t j = s_next;
-  while (j < (uint32_t)a.njobs) {
-    uint32_t nxt = 0;
+  if (threadIdx.x == 0) {
+    s_ready_t = -1;
+    s_next = atomicAdd(&a.sync[0], 1u);
+  }
+  uint32_t nxt = 0;
+  for (;;) {
+    // thread 0 has s_next; if it is a requant job of a tensor this CTA has
+    // not seen ready, settle that tensor's readiness now
+    if (threadIdx.x == 0) {
+      const uint32_t jn = s_next;
+      s_state = kReady;
+      s_tensor = -1;
+      if (jn < (uint32_t)a.njobs && (a.jobs[jn] & kRequantJob)) {
+        const int t = a.chunks[a.jobs[jn] & ~kRequantJob].tensor;
+        if (t != s_ready_t) {
+          s_state = tensor_readiness(a, t);
+          s_tensor = t;
+          if (s_state == kReady) s_ready_t = t;
+        }
+      }
+    }
+    __syncthreads();
+    if (s_state == kMustPublish) {
+      const int t = s_tensor;
+      finish_tensor(a, t, a.tensors[t]);
+      if (threadIdx.x == 0) {
+        s_state = kReady;
+        s_ready_t = t;
+      }
+      __syncthreads();
+    }
+    const uint32_t j = s_next;
+    if (j >= (uint32_t)a.njobs) break;
     if (threadIdx.x == 0) nxt = atomicAdd(&a.sync[0], 1u);  // next job, fetched early
     const uint32_t job = a.jobs[j];
     const Chunk ch = a.chunks[job & ~kRequantJob];
-    if (job & kRequantJob)
-      requant_chunk(a, ch, s_nv, stage, s_comp);
-    else
+    if (job & kRequantJob) {
+      if (s_state == kReady) requant_chunk(a, ch, s_nv, stage, s_comp);
+    } else {
       update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, stage);
+    }
     __syncthreads();
     if (threadIdx.x == 0) s_next = nxt;
-    __syncthreads();
-    j = s_next;
   }
 }
 
@@ -932,9 +969,10 @@ int apply_grid(int gdt, int opt, int device) {
 cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
                          const uint32_t* jobs, int njobs, const TensorDesc* tensors, float* master, float* s1,
                          float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
-                         uint32_t* sync, Fp4Thr* comp_thr, Decision* dec, int grid, cudaStream_t st) {
+                         uint32_t* sync, int ntensors, Fp4Thr* comp_thr, Decision* dec, int grid,
+                         cudaStream_t st) {
   ApplyArgs a{oc, use_scaler, chunks, jobs, njobs, tensors, master, s1, s2, grad, qout, amax_slots, qscale, sync,
-              comp_thr, dec};
+              ntensors, comp_thr, dec};
 #define ODY_L(G, O)                                                    \
   if (gdt == G && opt == O) {                                          \
     apply_kernel<G, O><<<grid, kThreads, 0, st>>>(a);                  \

@@ -323,14 +323,15 @@ static cudaError_t dalloc(T** p, size_t bytes) {
   return cudaMalloc((void**)p, bytes < 256 ? 256 : bytes);
 }
 
-// Job list of the apply kernel: every update chunk in arena order; the
-// requant chunks of a per-tensor-scaled tensor become eligible two grid-
-// widths of jobs after that tensor's last update job and are interleaved, up to two
+// Job list of the apply kernel: every update chunk in arena order; a per-
+// tensor-scaled tensor's publish job (its scale and thresholds) becomes
+// eligible one grid-width of jobs after that tensor's last update job and its
+// requant chunks two grid-widths after and are interleaved, up to two
 // per update job, with the following tensors' update jobs; what is left
 // runs at the end.
 static void build_jobs(ody_ctx* c) {
   c->jobs.clear();
-  std::vector<std::pair<size_t, uint32_t>> pending;  // (eligible position, chunk)
+  std::vector<std::pair<size_t, uint32_t>> pending;  // (eligible position, job word)
   size_t head = 0;
   const size_t W = (size_t)(c->grid_apply > 0 ? c->grid_apply : 1);
   size_t ci = 0;
@@ -340,12 +341,14 @@ static void build_jobs(ody_ctx* c) {
     for (int k = 0; k < d.nchunks; k++, ci++) {
       c->jobs.push_back((uint32_t)ci);
       for (int r = 0; r < 2 && head < pending.size() && pending[head].first <= c->jobs.size(); r++)
-        c->jobs.push_back(0x80000000u | pending[head++].second);
+        c->jobs.push_back(pending[head++].second);
     }
-    if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR)
-      for (size_t k = first; k < ci; k++) pending.push_back({c->jobs.size() + 2 * W, (uint32_t)k});
+    if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR) {
+      pending.push_back({c->jobs.size() + W, 0x40000000u | (uint32_t)li});
+      for (size_t k = first; k < ci; k++) pending.push_back({c->jobs.size() + 2 * W, 0x80000000u | (uint32_t)k});
+    }
   }
-  while (head < pending.size()) c->jobs.push_back(0x80000000u | pending[head++].second);
+  while (head < pending.size()) c->jobs.push_back(pending[head++].second);
 }
 
 extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const void* uid) {

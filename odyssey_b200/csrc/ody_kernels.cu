@@ -630,7 +630,8 @@ struct ApplyArgs {
 
 __device__ __forceinline__ void finish_tensor(const ApplyArgs& a, int tensor, const TensorDesc& td);
 
-constexpr uint32_t kRequantJob = 0x80000000u;
+constexpr uint32_t kRequantJob = 0x80000000u;  // low bits: chunk index
+constexpr uint32_t kPublishJob = 0x40000000u;  // low bits: tensor index
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
@@ -741,8 +742,8 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
   }
 }
 
-// Run by the CTA that claimed the tensor (the first to need it for a requant
-// job) once all its update jobs are done: the tensor's amax is final, so its
+// The publish job of a per-tensor-scaled tensor, run once all its update
+// jobs are done: the tensor's amax is final, so its
 // per-tensor scale is fixed.  For NVFP4 it also builds
 // the tensor's composite threshold table: for every E4M3 block scale sf and
 // ladder value T, the least float x with RN(RN(x / s_t) / sf) >= T (both
@@ -758,9 +759,11 @@ __device__ __forceinline__ bool reaches(float q, float d, float T) { return __fd
 // bisection over the bit patterns.
 __device__ float least_reaching(float d, float T) {
   const uint32_t kInf = 0x7f800000u;
-  if (!reaches(__uint_as_float(kInf - 1u), d, T)) return __uint_as_float(0x7fc00000u);
   uint32_t q = __float_as_uint(__fmul_rn(T, d));
-  if (q >= kInf) q = kInf - 1u;
+  if (q >= kInf) {
+    if (!reaches(__uint_as_float(kInf - 1u), d, T)) return __uint_as_float(0x7fc00000u);
+    q = kInf - 1u;
+  }
   int steps = 0;
   while (!reaches(__uint_as_float(q), d, T) && steps < 64) {
     q++;
@@ -857,14 +860,14 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
   }
 }
 
-// Readiness of tensor t for requant, decided by thread 0 of a CTA whose next
-// job is a requant job of t: first every update job of t must be done (their
-// counts are fire and forget), then t's scale and thresholds must be
-// published.  The first CTA to get here claims the publication (flag 0 -> 1)
-// and does it itself; the others wait for flag 2.  Nobody waits while
-// holding a claim, so the waits always end; they are still bounded by
-// %globaltimer and report through Decision::err.
-enum : int { kWaitFailed = 0, kReady = 1, kMustPublish = 2 };
+// Waits of the apply kernel (thread 0 of a CTA, before it starts a job).
+// A publish job of tensor t waits until every update job of t is done (their
+// counts are fire and forget) and then publishes t's scale and thresholds
+// (flag 2); a requant job of t waits for that flag.  A job only waits for
+// jobs that come earlier in the list, which running CTAs hold, so the waits
+// always end; they are still bounded by %globaltimer and report through
+// Decision::err.
+enum : int { kWaitFailed = 0, kReady = 1 };
 
 __device__ __forceinline__ bool wait_at_least(const ApplyArgs& a, const uint32_t* p, uint32_t v) {
   if (ld_acquire(p) >= v) return true;
@@ -879,21 +882,13 @@ __device__ __forceinline__ bool wait_at_least(const ApplyArgs& a, const uint32_t
   return true;
 }
 
-__device__ __forceinline__ int tensor_readiness(const ApplyArgs& a, int t) {
-  uint32_t* flag = &a.sync[1 + a.ntensors + t];
-  if (ld_acquire(flag) == 2u) return kReady;
-  if (!wait_at_least(a, &a.sync[1 + t], (uint32_t)a.tensors[t].nchunks)) return kWaitFailed;
-  if (atomicCAS(flag, 0u, 1u) == 0u) return kMustPublish;
-  return wait_at_least(a, flag, 2u) ? kReady : kWaitFailed;
-}
-
 template <int GDT, int OPT>
 __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
   __shared__ uint32_t s_next;
-  __shared__ int s_state, s_tensor, s_ready_t;
+  __shared__ int s_state, s_ready_t;
   __shared__ __align__(16) Fp4Thr s_comp[128];
   const Decision* dec = a.dec;
   if (dec->skip) return;
@@ -907,40 +902,36 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   }
   uint32_t nxt = 0;
   for (;;) {
-    // thread 0 has s_next; if it is a requant job of a tensor this CTA has
-    // not seen ready, settle that tensor's readiness now
+    // thread 0 has s_next; settle what that job waits for
     if (threadIdx.x == 0) {
       const uint32_t jn = s_next;
       s_state = kReady;
-      s_tensor = -1;
-      if (jn < (uint32_t)a.njobs && (a.jobs[jn] & kRequantJob)) {
-        const int t = a.chunks[a.jobs[jn] & ~kRequantJob].tensor;
-        if (t != s_ready_t) {
-          s_state = tensor_readiness(a, t);
-          s_tensor = t;
-          if (s_state == kReady) s_ready_t = t;
+      if (jn < (uint32_t)a.njobs) {
+        const uint32_t job = a.jobs[jn];
+        if (job & kPublishJob) {
+          const int t = (int)(job & ~kPublishJob);
+          s_state = wait_at_least(a, &a.sync[1 + t], (uint32_t)a.tensors[t].nchunks) ? kReady : kWaitFailed;
+        } else if (job & kRequantJob) {
+          const int t = a.chunks[job & ~kRequantJob].tensor;
+          if (t != s_ready_t) {
+            s_state = wait_at_least(a, &a.sync[1 + a.ntensors + t], 2u) ? kReady : kWaitFailed;
+            if (s_state == kReady) s_ready_t = t;
+          }
         }
       }
     }
     __syncthreads();
-    if (s_state == kMustPublish) {
-      const int t = s_tensor;
-      finish_tensor(a, t, a.tensors[t]);
-      if (threadIdx.x == 0) {
-        s_state = kReady;
-        s_ready_t = t;
-      }
-      __syncthreads();
-    }
     const uint32_t j = s_next;
     if (j >= (uint32_t)a.njobs) break;
     if (threadIdx.x == 0) nxt = atomicAdd(&a.sync[0], 1u);  // next job, fetched early
     const uint32_t job = a.jobs[j];
-    const Chunk ch = a.chunks[job & ~kRequantJob];
-    if (job & kRequantJob) {
-      if (s_state == kReady) requant_chunk(a, ch, s_nv, stage, s_comp);
+    if (job & kPublishJob) {
+      const int t = (int)(job & ~kPublishJob);
+      if (s_state == kReady) finish_tensor(a, t, a.tensors[t]);
+    } else if (job & kRequantJob) {
+      if (s_state == kReady) requant_chunk(a, a.chunks[job & ~kRequantJob], s_nv, stage, s_comp);
     } else {
-      update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, stage);
+      update_chunk<GDT, OPT>(a, a.chunks[job], dv, clipped, coef, s_mx, s_nv, stage);
     }
     __syncthreads();
     if (threadIdx.x == 0) s_next = nxt;

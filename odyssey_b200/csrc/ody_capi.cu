@@ -109,7 +109,6 @@ struct ody_ctx {
   Chunk* d_chunks_upd = nullptr;
   uint32_t* d_jobs = nullptr;
   uint32_t* sync = nullptr;  // job ticket + per-tensor done counts
-  Fp4Thr* comp_thr = nullptr;  // per tensor: composite NVFP4 thresholds
   TensorDesc* d_tdesc = nullptr;
   StatsPartial* partials = nullptr;
   unsigned* ticket = nullptr;
@@ -323,15 +322,14 @@ static cudaError_t dalloc(T** p, size_t bytes) {
   return cudaMalloc((void**)p, bytes < 256 ? 256 : bytes);
 }
 
-// Job list of the apply kernel: every update chunk in arena order; a per-
-// tensor-scaled tensor's publish job (its scale and thresholds) becomes
-// eligible one grid-width of jobs after that tensor's last update job and its
-// requant chunks two grid-widths after and are interleaved, up to two
+// Job list of the apply kernel: every update chunk in arena order; the
+// requant chunks of a per-tensor-scaled tensor become eligible two grid-widths
+// of jobs after that tensor's last update job and are interleaved, up to two
 // per update job, with the following tensors' update jobs; what is left
 // runs at the end.
 static void build_jobs(ody_ctx* c) {
   c->jobs.clear();
-  std::vector<std::pair<size_t, uint32_t>> pending;  // (eligible position, job word)
+  std::vector<std::pair<size_t, uint32_t>> pending;  // (eligible position, chunk)
   size_t head = 0;
   const size_t W = (size_t)(c->grid_apply > 0 ? c->grid_apply : 1);
   size_t ci = 0;
@@ -341,14 +339,12 @@ static void build_jobs(ody_ctx* c) {
     for (int k = 0; k < d.nchunks; k++, ci++) {
       c->jobs.push_back((uint32_t)ci);
       for (int r = 0; r < 2 && head < pending.size() && pending[head].first <= c->jobs.size(); r++)
-        c->jobs.push_back(pending[head++].second);
+        c->jobs.push_back(0x80000000u | pending[head++].second);
     }
-    if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR) {
-      pending.push_back({c->jobs.size() + W, 0x40000000u | (uint32_t)li});
-      for (size_t k = first; k < ci; k++) pending.push_back({c->jobs.size() + 2 * W, 0x80000000u | (uint32_t)k});
-    }
+    if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR)
+      for (size_t k = first; k < ci; k++) pending.push_back({c->jobs.size() + 2 * W, (uint32_t)k});
   }
-  while (head < pending.size()) c->jobs.push_back(pending[head++].second);
+  while (head < pending.size()) c->jobs.push_back(0x80000000u | pending[head++].second);
 }
 
 extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const void* uid) {
@@ -432,9 +428,8 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   if (!c->jobs.empty())
     ODY_CUDA(cudaMemcpyAsync(c->d_jobs, c->jobs.data(), sizeof(uint32_t) * c->jobs.size(), cudaMemcpyHostToDevice,
                              c->stream));
-  ODY_CUDA(dalloc(&c->sync, sizeof(uint32_t) * (2 * nl + 1)));
-  ODY_CUDA(dalloc(&c->comp_thr, sizeof(Fp4Thr) * 128 * (nl > 0 ? nl : 1)));
-  ODY_CUDA(cudaMemsetAsync(c->sync, 0, sizeof(uint32_t) * (2 * nl + 1), c->stream));
+  ODY_CUDA(dalloc(&c->sync, sizeof(uint32_t) * (nl + 1)));
+  ODY_CUDA(cudaMemsetAsync(c->sync, 0, sizeof(uint32_t) * (nl + 1), c->stream));
   c->grid_stats = stats_grid(c->cfg.device);
   ODY_CUDA(dalloc(&c->partials, sizeof(StatsPartial) * c->grid_stats));
   ODY_CUDA(dalloc(&c->ticket, sizeof(unsigned)));
@@ -577,8 +572,6 @@ static OptConsts make_consts(const ody_config& cfg, int64_t t) {
   if (t > 0) {
     o.bc1 = (float)(1.0 - pow(cfg.beta1, (double)t));
     o.bc2 = (float)(1.0 - pow(cfg.beta2, (double)t));
-    o.rbc1 = 1.0f / o.bc1;  // IEEE float division: the correctly rounded reciprocal
-    o.rbc2 = 1.0f / o.bc2;
   }
   return o;
 }
@@ -639,7 +632,7 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   if (!c->jobs.empty()) {
     e = launch_apply(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd, c->d_jobs,
                      (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout, c->amax, c->qscale,
-                     c->sync, nl, c->comp_thr, c->dec, c->grid_apply, c->stream);
+                     c->sync, c->dec, c->grid_apply, c->stream);
     if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("apply kernel: ") + cudaGetErrorString(e));
   }
   if (tev) ODY_CUDA(cudaEventRecord(tev[3], c->stream));
@@ -874,7 +867,7 @@ extern "C" void ody_ctx_destroy(ody_ctx* c) {
     if (api) api->commDestroy(c->comm);
   }
   void* bufs[] = {c->master, c->s1, c->s2, c->grad, c->qout, c->qscale, c->amax, c->d_chunks_upd,
-                  c->d_jobs, c->sync, c->comp_thr, c->d_tdesc, c->partials, c->ticket, c->scaler, c->dec,
+                  c->d_jobs, c->sync, c->d_tdesc, c->partials, c->ticket, c->scaler, c->dec,
                   c->local_stats, c->gathered};
   for (void* b : bufs)
     if (b) cudaFree(b);

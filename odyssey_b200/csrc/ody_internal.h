@@ -99,8 +99,7 @@ cudaError_t launch_finalize(const double* gathered, int world, DevScaler* scaler
 cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
                          const uint32_t* jobs, int njobs, const TensorDesc* tensors, float* master, float* s1,
                          float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
-                         uint32_t* sync, int ntensors, Fp4Thr* comp_thr, Decision* dec, int grid,
-                         cudaStream_t st);
+                         uint32_t* sync, Decision* dec, int grid, cudaStream_t st);
 int apply_grid(int gdt, int opt, int device);
 int stats_grid(int device);
 

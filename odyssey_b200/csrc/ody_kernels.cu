@@ -367,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 4) stats_kernel(StatsArgs a) {
   }
   block_sum2(s, c);
   for (int j = threadIdx.x; j < a.ntensors; j += blockDim.x) a.amax_slots[j] = 0u;
-  for (int j = threadIdx.x; j < 2 * a.ntensors + 1; j += blockDim.x) a.sync[j] = 0u;
+  for (int j = threadIdx.x; j < a.ntensors + 1; j += blockDim.x) a.sync[j] = 0u;
   if (threadIdx.x == 0) {
     *a.ticket = 0u;
     if (a.world_mode == 0) {
@@ -448,23 +448,10 @@ __device__ __forceinline__ bool any_nonfinite8(const float v[8]) {
 }
 
 // the threshold ladder without special cases (finite x, positive finite scale)
-// compare producing an all-ones (true) or zero (false) mask
-__device__ __forceinline__ uint32_t ge_mask(float a, float b) {
-  uint32_t d;
-  asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(d) : "f"(a), "f"(b));
-  return d;
-}
-
 __device__ __forceinline__ uint32_t fp4_encode_plain(float x, const float* t) {
   const float a = fabsf(x);
-  // each true compare contributes -1; the first threshold counts twice
-  // (magnitudes 0, 2, 3, .., 7: the 0.5 code is never produced)
-  const uint32_t m1 = ge_mask(a, t[1]);
-  const uint32_t neg = (m1 + m1 + ge_mask(a, t[2])) + (ge_mask(a, t[3]) + ge_mask(a, t[4])) +
-                       (ge_mask(a, t[5]) + ge_mask(a, t[6]));
-  const uint32_t mag = 0u - neg;
-  const uint32_t sgn = ge_mask(-x, t[0]) & 8u;  // x < 0 with RN(|x|/s) != 0
-  return sgn | mag;
+  const uint32_t mag = 2u * (a >= t[1]) + (a >= t[2]) + (a >= t[3]) + (a >= t[4]) + (a >= t[5]) + (a >= t[6]);
+  return ((uint32_t)((x < 0.0f) && (a >= t[0])) << 3) | mag;
 }
 
 template <bool MX>
@@ -494,41 +481,6 @@ __device__ __forceinline__ void stage_fp4(const float v[8], uint8_t* ws, const F
   if (j == (MX ? 3 : 1)) ws[blk * bb + bb - 1] = e;
 }
 
-// NVFP4 with a per-tensor scale s (r = RN(1/s)): the reference encode of
-// x' = RN(x / s).  The block amax of x' is RN(amax(|x|) / s) (division is
-// monotone), and the codes come from the tensor's composite thresholds on x
-// itself; blocks that need the special cases divide and take the general
-// encode.
-__device__ __forceinline__ void stage_nvfp4_scaled(const float v[8], float s, float r, uint8_t* ws,
-                                                   const Fp4Thr* thr, const Fp4Thr* comp) {
-  float am = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
-  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-  const float amq = div_by(am, s, r);
-  const uint8_t e = e4m3_scale_from_f32(block_scale_value(amq));
-  const bool z = e == 0;
-  const bool special = z || any_nonfinite8(v);
-  const int lane = threadIdx.x & 31;
-  const int blk = lane >> 1, j = lane & 1;
-  uint8_t* dst = ws + blk * 9 + 4 * j;
-  if (!special) {
-    const float* t = comp[e].t;
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-      dst[i] = (uint8_t)((fp4_encode_plain(v[2 * i], t) << 4) | fp4_encode_plain(v[2 * i + 1], t));
-  } else {
-    const float* t = thr[e].t;
-    float q[8];
-#pragma unroll
-    for (int k = 0; k < 8; k++) q[k] = div_by(v[k], s, r);
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-      dst[i] = (uint8_t)((fp4_encode(q[2 * i], t, z) << 4) | fp4_encode(q[2 * i + 1], t, z));
-  }
-  if (j == 1) ws[blk * 9 + 8] = e;
-}
-
 // write a warp's staged bytes: whole 16-byte (NVFP4) / 8-byte (MXFP4) stores
 // when the destination is aligned and the whole slice may be written, else
 // bytes up to `limit`
@@ -549,6 +501,20 @@ __device__ __forceinline__ void flush_warp(const uint8_t* ws, uint8_t* dst, int6
   }
 }
 
+// Exact division x / s with s's reciprocal r = RN(1/s) precomputed: the
+// product estimate is corrected once with the exactly computed remainder
+// (Markstein's correction: q0 = x*r is within one ulp, x - q0*s is exact by
+// FMA, and q0 + rem*r rounded once is the correctly rounded quotient when r
+// is the correctly rounded reciprocal, provided nothing under- or overflows:
+// the remainder is a multiple of about ulp(x) * 2^-24, exact only while |x|
+// stays above 2^-100).  Zero, non-finite and extreme magnitudes take the
+// IEEE division.
+__device__ __forceinline__ float div_by(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float q = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
+  const float aq = fabsf(q0), ax = fabsf(x);
+  return (aq >= 0x1p-125f && aq <= 0x1p+125f && ax >= 0x1p-100f && ax <= 0x1p+125f) ? q : __fdiv_rn(x, s);
+}
 
 __device__ __forceinline__ void store_elem8(int kind, const float v[8], uint8_t* dst) {
   if (kind == Q_FP16 || kind == Q_BF16) {
@@ -622,16 +588,11 @@ struct ApplyArgs {
   uint8_t* qout;
   uint32_t* amax_slots;
   float* qscale;
-  uint32_t* sync;  // [0] job ticket, [1, 1+nt) update jobs done, [1+nt, 1+2nt) table flags
-  int ntensors;
-  Fp4Thr* comp_thr;  // per tensor: 128 composite NVFP4 threshold rows
+  uint32_t* sync;  // [0] job ticket, [1..] update jobs done per tensor
   Decision* dec;
 };
 
-__device__ __forceinline__ void finish_tensor(const ApplyArgs& a, int tensor, const TensorDesc& td);
-
-constexpr uint32_t kRequantJob = 0x80000000u;  // low bits: chunk index
-constexpr uint32_t kPublishJob = 0x40000000u;  // low bits: tensor index
+constexpr uint32_t kRequantJob = 0x80000000u;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
@@ -735,99 +696,38 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
     const float bm = block_amax_reduce(amax);
     if (threadIdx.x == 0) atomicMax(&a.amax_slots[ch.tensor], __float_as_uint(bm));
     // publish: every thread's stores of this chunk, then the done count
-    // (fire and forget: an update job never waits for anything)
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) atomicAdd(&a.sync[1 + ch.tensor], 1u);
   }
 }
 
-// The publish job of a per-tensor-scaled tensor, run once all its update
-// jobs are done: the tensor's amax is final, so its
-// per-tensor scale is fixed.  For NVFP4 it also builds
-// the tensor's composite threshold table: for every E4M3 block scale sf and
-// ladder value T, the least float x with RN(RN(x / s_t) / sf) >= T (both
-// divisions IEEE, as the encode defines them; the composite is monotone in
-// x).  Requant jobs then encode x directly with compares.  The tensor's flag
-// goes to 2 when this is published.
-__device__ __forceinline__ bool reaches(float q, float d, float T) { return __fdiv_rn(q, d) >= T; }
-
-// Least float q >= 0 with RN(q / d) >= T (d > 0 finite, T > 0), NaN if none:
-// start at the product estimate T*d, which is within a few ulps, and walk to
-// the boundary one ulp at a time (non-negative floats are ordered like their
-// bit patterns).  A walk that does not settle within 64 steps falls back to
-// bisection over the bit patterns.
-__device__ float least_reaching(float d, float T) {
-  const uint32_t kInf = 0x7f800000u;
-  uint32_t q = __float_as_uint(__fmul_rn(T, d));
-  if (q >= kInf) {
-    if (!reaches(__uint_as_float(kInf - 1u), d, T)) return __uint_as_float(0x7fc00000u);
-    q = kInf - 1u;
-  }
-  int steps = 0;
-  while (!reaches(__uint_as_float(q), d, T) && steps < 64) {
-    q++;
-    steps++;
-  }
-  while (q > 0 && reaches(__uint_as_float(q - 1u), d, T) && steps < 64) {
-    q--;
-    steps++;
-  }
-  if (steps >= 64) {
-    uint32_t lo = 0, hi = kInf - 1u;
-    if (reaches(0.0f, d, T)) return 0.0f;
-    while (hi - lo > 1) {
-      const uint32_t mid = lo + (hi - lo) / 2;
-      if (reaches(__uint_as_float(mid), d, T))
-        hi = mid;
-      else
-        lo = mid;
-    }
-    q = hi;
-  }
-  return __uint_as_float(q);
-}
-
-__device__ __forceinline__ void finish_tensor(const ApplyArgs& a, int tensor, const TensorDesc& td) {
-  __threadfence();
-  const float st = tensor_scale_from_amax(td.quant, __ldcg(&a.amax_slots[tensor]));
-  if (td.quant == Q_NVFP4_TENSOR) {
-    // RN(RN(x/st)/sf) >= T  <=>  RN(x/st) >= q*  with q* the least float
-    // whose quotient by sf reaches T, so the composite threshold is the
-    // least x whose quotient by st reaches q*
-    float* tab = reinterpret_cast<float*>(a.comp_thr + (size_t)tensor * 128);
-    for (int idx = threadIdx.x; idx < 128 * 7; idx += blockDim.x) {
-      const int e = idx / 7, k = idx % 7;
-      const float sf = e4m3_to_f32((uint8_t)e);
-      const float T = k == 0 ? __uint_as_float(1u) : (k == 1 ? 0.5f : k == 2 ? 1.25f : k == 3 ? 1.75f
-                                                     : k == 4 ? 2.5f : k == 5 ? 3.5f : 5.0f);
-      float res = __uint_as_float(0x7fc00000u);
-      if (e >= 1 && e <= 126) {
-        const float qs = least_reaching(sf, T);
-        if (qs == qs) res = qs == 0.0f ? 0.0f : least_reaching(st, qs);
-      }
-      tab[e * 8 + k] = res;
-    }
-  }
-  if (threadIdx.x == 0) a.qscale[tensor] = st;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) atomicExch(&a.sync[1 + a.ntensors + tensor], 2u);
-}
-
 __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& ch, const Fp4Thr* s_nv,
-                                              uint8_t* stage, Fp4Thr* s_comp) {
+                                              uint8_t* stage) {
   const TensorDesc td = a.tensors[ch.tensor];
-  const int kind = td.quant;
-  const float s = __ldcg(&a.qscale[ch.tensor]);
-  const float r = __frcp_rn(s);
-  const bool nv = kind == Q_NVFP4_TENSOR;
-  if (nv) {
-    const float4* src = reinterpret_cast<const float4*>(a.comp_thr + (size_t)ch.tensor * 128);
-    float4* dst = reinterpret_cast<float4*>(s_comp);
-    for (int i = threadIdx.x; i < 128 * 2; i += blockDim.x) dst[i] = __ldcg(src + i);
-    __syncthreads();
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    const uint32_t* done = &a.sync[1 + ch.tensor];
+    int ok = 1;
+    if (ld_acquire(done) < (uint32_t)td.nchunks) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (ld_acquire(done) < (uint32_t)td.nchunks) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          ok = 0;
+          atomicOr(&a.dec->err, 1);
+          break;
+        }
+        __nanosleep(256);
+      }
+    }
+    s_ok = ok;
   }
+  __syncthreads();
+  if (!s_ok) return;
+  const int kind = td.quant;
+  const float s = tensor_scale_from_amax(kind, __ldcg(&a.amax_slots[ch.tensor]));
+  const float r = __frcp_rn(s);
+  if (ch.start == td.off && threadIdx.x == 0) a.qscale[ch.tensor] = s;
   const int64_t end = ch.start + ch.len;
   for (int64_t tb = ch.start; tb < end; tb += kTile) {
     const int64_t e0 = tb + (int64_t)threadIdx.x * kVec;
@@ -838,48 +738,26 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
       float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
       x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
       x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
+#pragma unroll
+      for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
     } else {
 #pragma unroll
       for (int k = 0; k < 8; k++) x[k] = 0.0f;
     }
-    if (nv) {
+    if (kind == Q_NVFP4_TENSOR) {
       if (tb + (int64_t)(threadIdx.x & ~31) * kVec < end) {
         const int64_t tile_in_tensor = (tb - td.off) / kTile;
         const int w = threadIdx.x >> 5;
         uint8_t* ws = stage + w * kWarpStage;
-        stage_nvfp4_scaled(x, s, r, ws, s_nv, s_comp);
+        stage_fp4<false>(x, ws, s_nv);
         __syncwarp();
         flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
         __syncwarp();
       }
     } else if (act) {
-#pragma unroll
-      for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
       store_elem8(Q_FP8_E4M3, x, a.qout + td.qoff + (e0 - td.off));
     }
   }
-}
-
-// Waits of the apply kernel (thread 0 of a CTA, before it starts a job).
-// A publish job of tensor t waits until every update job of t is done (their
-// counts are fire and forget) and then publishes t's scale and thresholds
-// (flag 2); a requant job of t waits for that flag.  A job only waits for
-// jobs that come earlier in the list, which running CTAs hold, so the waits
-// always end; they are still bounded by %globaltimer and report through
-// Decision::err.
-enum : int { kWaitFailed = 0, kReady = 1 };
-
-__device__ __forceinline__ bool wait_at_least(const ApplyArgs& a, const uint32_t* p, uint32_t v) {
-  if (ld_acquire(p) >= v) return true;
-  const unsigned long long t0 = globaltimer_ns();
-  while (ld_acquire(p) < v) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-      atomicOr(&a.dec->err, 1);
-      return false;
-    }
-    __nanosleep(256);
-  }
-  return true;
 }
 
 template <int GDT, int OPT>
@@ -888,53 +766,28 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ Fp4Thr s_nv[128];
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
   __shared__ uint32_t s_next;
-  __shared__ int s_state, s_ready_t;
-  __shared__ __align__(16) Fp4Thr s_comp[128];
   const Decision* dec = a.dec;
   if (dec->skip) return;
   const Divisor dv = make_divisor(unscale_divisor<GDT>(dec->scale_used));
   const bool clipped = dec->clipped != 0;
   const float coef = dec->coef;
   load_thr_smem(s_mx, s_nv);
-  if (threadIdx.x == 0) {
-    s_ready_t = -1;
-    s_next = atomicAdd(&a.sync[0], 1u);
-  }
-  uint32_t nxt = 0;
-  for (;;) {
-    // thread 0 has s_next; settle what that job waits for
-    if (threadIdx.x == 0) {
-      const uint32_t jn = s_next;
-      s_state = kReady;
-      if (jn < (uint32_t)a.njobs) {
-        const uint32_t job = a.jobs[jn];
-        if (job & kPublishJob) {
-          const int t = (int)(job & ~kPublishJob);
-          s_state = wait_at_least(a, &a.sync[1 + t], (uint32_t)a.tensors[t].nchunks) ? kReady : kWaitFailed;
-        } else if (job & kRequantJob) {
-          const int t = a.chunks[job & ~kRequantJob].tensor;
-          if (t != s_ready_t) {
-            s_state = wait_at_least(a, &a.sync[1 + a.ntensors + t], 2u) ? kReady : kWaitFailed;
-            if (s_state == kReady) s_ready_t = t;
-          }
-        }
-      }
-    }
-    __syncthreads();
-    const uint32_t j = s_next;
-    if (j >= (uint32_t)a.njobs) break;
+  if (threadIdx.x == 0) s_next = atomicAdd(&a.sync[0], 1u);
+  __syncthreads();
+  uint32_t j = s_next;
+  while (j < (uint32_t)a.njobs) {
+    uint32_t nxt = 0;
     if (threadIdx.x == 0) nxt = atomicAdd(&a.sync[0], 1u);  // next job, fetched early
     const uint32_t job = a.jobs[j];
-    if (job & kPublishJob) {
-      const int t = (int)(job & ~kPublishJob);
-      if (s_state == kReady) finish_tensor(a, t, a.tensors[t]);
-    } else if (job & kRequantJob) {
-      if (s_state == kReady) requant_chunk(a, a.chunks[job & ~kRequantJob], s_nv, stage, s_comp);
-    } else {
-      update_chunk<GDT, OPT>(a, a.chunks[job], dv, clipped, coef, s_mx, s_nv, stage);
-    }
+    const Chunk ch = a.chunks[job & ~kRequantJob];
+    if (job & kRequantJob)
+      requant_chunk(a, ch, s_nv, stage);
+    else
+      update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, stage);
     __syncthreads();
     if (threadIdx.x == 0) s_next = nxt;
+    __syncthreads();
+    j = s_next;
   }
 }
 
@@ -960,10 +813,9 @@ int apply_grid(int gdt, int opt, int device) {
 cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
                          const uint32_t* jobs, int njobs, const TensorDesc* tensors, float* master, float* s1,
                          float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
-                         uint32_t* sync, int ntensors, Fp4Thr* comp_thr, Decision* dec, int grid,
-                         cudaStream_t st) {
+                         uint32_t* sync, Decision* dec, int grid, cudaStream_t st) {
   ApplyArgs a{oc, use_scaler, chunks, jobs, njobs, tensors, master, s1, s2, grad, qout, amax_slots, qscale, sync,
-              ntensors, comp_thr, dec};
+              dec};
 #define ODY_L(G, O)                                                    \
   if (gdt == G && opt == O) {                                          \
     apply_kernel<G, O><<<grid, kThreads, 0, st>>>(a);                  \

@@ -35,24 +35,8 @@ struct OptConsts {
   float lr, mu, wd;          // sgd.mojo:27-121
   float b1, omb1, b2, omb2;  // adam.mojo:123-140
   float bc1, bc2, eps;       // adam.mojo:142-163
-  float rbc1, rbc2;          // RN(1/bc1), RN(1/bc2) for the exact division below
   int use_wd, use_mu;
 };
-
-// Exact division x / s with s's reciprocal r = RN(1/s) precomputed: the
-// product estimate is corrected once with the exactly computed remainder
-// (Markstein's correction: q0 = x*r is within one ulp, x - q0*s is exact by
-// FMA, and q0 + rem*r rounded once is the correctly rounded quotient when r
-// is the correctly rounded reciprocal, provided nothing under- or overflows:
-// the remainder is a multiple of about ulp(x) * 2^-24, exact only while |x|
-// stays above 2^-100).  Zero, non-finite and extreme magnitudes take the
-// IEEE division.
-__device__ __forceinline__ float div_by(float x, float s, float r) {
-  const float q0 = __fmul_rn(x, r);
-  const float q = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
-  const float aq = fabsf(q0), ax = fabsf(x);
-  return (aq >= 0x1p-125f && aq <= 0x1p+125f && ax >= 0x1p-100f && ax <= 0x1p+125f) ? q : __fdiv_rn(x, s);
-}
 
 // sgd.mojo:89-118: e = g + wd*p; v' = mu*v + e; p' = p - lr*v'
 __device__ __forceinline__ void sgd_elem(float& p, float g, float& vel, const OptConsts& c) {
@@ -72,8 +56,8 @@ __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
   if (!DECOUPLED && c.use_wd) e = __fadd_rn(g, __fmul_rn(c.wd, p));
   m = __fadd_rn(__fmul_rn(c.b1, m), __fmul_rn(c.omb1, e));
   v = __fadd_rn(__fmul_rn(c.b2, v), __fmul_rn(c.omb2, __fmul_rn(e, e)));
-  const float mh = div_by(m, c.bc1, c.rbc1);
-  const float vh = div_by(v, c.bc2, c.rbc2);
+  const float mh = __fdiv_rn(m, c.bc1);
+  const float vh = __fdiv_rn(v, c.bc2);
   const float den = __fadd_rn(__fsqrt_rn(vh), c.eps);
   float np = __fsub_rn(p, __fmul_rn(c.lr, __fdiv_rn(mh, den)));
   if (DECOUPLED && c.use_wd) np = __fsub_rn(np, __fmul_rn(c.wd, np));

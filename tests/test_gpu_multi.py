@@ -1,0 +1,56 @@
+"""Multi-GPU parity: the ZeRO-1-sharded step on 2 GPUs (one process each,
+NCCL allgather of the per-rank {nonfinite, sumsq}) against the oracle's
+unsharded step.  Every rank must take the identical skip/backoff decision,
+and each rank's tensors must match the oracle (master within 2 ulp, codes
+bit-exact).  Skipped when fewer than 2 GPUs are visible."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_two_rank_resnet18_matches_unsharded_oracle(oracle, tmp_path):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    steps, inf_every = 5, 3
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", "29533",
+           os.path.join(ROOT, "tests", "dist_worker.py"), str(tmp_path), str(steps), str(inf_every)]
+    p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
+    ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(2)]
+    # identical decisions on both ranks
+    np.testing.assert_array_equal(ranks[0]["results"], ranks[1]["results"])
+
+    from odyssey_b200 import workloads as W
+    wl = W.resnet18()
+    wl.inf_every = inf_every
+    specs = [{"numel": n, "grad_dtype": oracle.BF16, "quant": oracle.Q_FP8_E4M3_TENSOR} for n in wl.numels]
+    model = oracle.Model(specs, oracle.ADAMW, 1e-3, weight_decay=0.01, scaler_kwargs={"initial_scale": 65536.0})
+    for i, m in enumerate(wl.master(0)):
+        model.master[i][:] = m
+    t = 1
+    for s in range(steps):
+        r = model.step(wl.grads(s, 1), t)
+        got = ranks[0]["results"][s]
+        assert got[0] == r.skipped and got[1] == r.nonfinite and got[4] == r.scale_next
+        if np.isfinite(r.sumsq):
+            assert abs(got[2] - r.sumsq) <= 1e-12 * r.sumsq
+        if not r.skipped:
+            t += 1
+    seen = []
+    for z in ranks:
+        for i in z["owned"]:
+            seen.append(int(i))
+            d = np.abs(z[f"master{i}"].view(np.int32).astype(np.int64) - model.master[i].view(np.int32))
+            assert d.max() <= 2, i
+            np.testing.assert_array_equal(z[f"codes{i}"], model.qout[i][: z[f"codes{i}"].size])
+            assert z[f"scale{i}"] == model.qscale[i][0]
+    assert sorted(seen) == list(range(len(wl.numels)))

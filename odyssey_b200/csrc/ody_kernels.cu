@@ -317,7 +317,16 @@ __device__ __forceinline__ void stats_raw8(const Raw8& r, bool use_scaler, const
                                            long long& bad) {
   float v[8];
   unpack8<GDT>(r, v);
-  unscale8<GDT>(v, use_scaler, dv);
+  if (GDT == DT_BF16 && use_scaler && dv.pow2) {
+    // a bfloat16 times an exact power of two: exact unless float32-subnormal,
+    // and a subnormal (or its bfloat16 rounding) squares to 0 in float32, so
+    // the rounding back to bfloat16 cannot change a square or a finiteness
+    // test and is skipped here (the update pass does it)
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = __fmul_rn(v[k], dv.r);
+  } else {
+    unscale8<GDT>(v, use_scaler, dv);
+  }
   const float s = sq8(v);
   // a non-finite square sum means a NaN/Inf element or squares that overflow
   // float32; only then are the elements counted one by one

@@ -190,6 +190,22 @@ __device__ __forceinline__ void unpack8(const Raw8& r, float out[8]) {
 
 template <int GDT>
 __device__ __forceinline__ void unscale8(float v[8], bool use_scaler, const Divisor& dv) {
+  if (GDT == DT_BF16 && use_scaler && dv.pow2) {
+    // exact products; only float32-subnormal ones need the bfloat16 rounding,
+    // tested once for the 8 values
+    float mn = 3.0e38f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      v[k] = __fmul_rn(v[k], dv.r);
+      mn = fminf(mn, fabsf(v[k]));
+    }
+    if (mn < 1.17549435e-38f) {
+#pragma unroll
+      for (int k = 0; k < 8; k++)
+        if (fabsf(v[k]) < 1.17549435e-38f) v[k] = bf16_bits_to_f32(f32_to_bf16_bits(v[k]));
+    }
+    return;
+  }
   if (use_scaler) {
 #pragma unroll
     for (int k = 0; k < 8; k++) v[k] = unscale_elem<GDT>(v[k], dv);

@@ -37,6 +37,11 @@ TOTAL = NT * PER
 ALG_BYTES_STEP = 26.5625        # grads 2 + master/m/v r+w 24 + NVFP4 codes 0.5625 (B/param)
 ALG_BYTES_UPDATE = 26.5625      # apply kernel: grads 2 + master/m/v r+w 24 + NVFP4 codes 0.5625
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes per param of one apply_kernel launch, measured with ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum of the 8-tensor case
+# `--tensors 8`, divided by its 134,217,728 params; traffic grows with the
+# params a launch processes)
+TRAFFIC_BYTES_PER_PARAM_APPLY = 30.45
 
 
 def env_int(k, d):
@@ -310,7 +315,9 @@ def main():
             "passes_ms_per_step": {k: v / max(nsteps, 1) for k, v in passes.items()},
             "roofline": {"kernel": "apply_kernel (update + per-tensor requant)", "bound": "hbm", "achieved": upd_gbs, "peak": peak,
                          "unit": "GB/s", "frac": upd_gbs / peak, "peak_source": peak_kind,
-                         "alg_bytes_per_launch": ALG_BYTES_UPDATE * nloc, "traffic": None},
+                         "alg_bytes_per_launch": ALG_BYTES_UPDATE * nloc,
+                         "traffic": TRAFFIC_BYTES_PER_PARAM_APPLY * nloc,
+                         "traffic_source": "ncu capture of an 8-tensor case scaled by params"},
             "e2e": {"value": TOTAL / (e2e_ms * 1e-3), "unit": "params/s", "ms_per_step": e2e_ms,
                     "wall_ms_per_step": wall * 1e3 / args.e2e_steps,
                     "h2d_bytes_per_step": 2 * nloc, "d2h_bytes_per_step": 80},

@@ -321,7 +321,7 @@ def main():
             "e2e": {"value": TOTAL / (e2e_ms * 1e-3), "unit": "params/s", "ms_per_step": e2e_ms,
                     "wall_ms_per_step": wall * 1e3 / args.e2e_steps,
                     "h2d_bytes_per_step": 2 * nloc, "d2h_bytes_per_step": 80},
-            "gpu_launches": args.steps * (3 if world == 1 else 4),
+            "gpu_launches": args.steps * (2 if world == 1 else 3),
             "clocks": clk.summary(),
             "last_step": {k: res[k] for k in ("grad_norm", "clip_coef", "clipped", "skipped", "scale_used")},
         }

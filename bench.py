@@ -205,7 +205,9 @@ def main():
 
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # host-side plumbing only (NCCL id broadcast, barriers, max over ranks);
+        # the step's own exchange runs on the library's NCCL communicator
+        dist.init_process_group("gloo")
     wl = flat1b(ntensors=NT)
     kw = wl.step_kwargs()
     kw["device"] = local
@@ -234,9 +236,17 @@ def main():
         torch.cuda.synchronize()
 
     t = 1
+    w0 = time.perf_counter()
     for _ in range(args.warmup):
         ctx.step(t)
         t += 1
+    # every rank must run the same number of steps (each step has a
+    # collective): the untimed clock-warm-up count is agreed from the slowest
+    # rank's warm-up time
+    per_step = torch.tensor([(time.perf_counter() - w0) / max(args.warmup, 1)], dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(per_step, op=dist.ReduceOp.MAX)
+    n_clock_warm = max(3, min(2000, int(0.6 / max(per_step.item(), 1e-6))))
     stream = torch.cuda.ExternalStream(ctx.stream_handle())
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ctx.set_timing(True)
@@ -244,8 +254,7 @@ def main():
     barrier()
     with Clocks(local) as clk:
         # keep the GPU loaded while the clock sampler starts (untimed steps)
-        w_end = time.perf_counter() + 0.6
-        while time.perf_counter() < w_end:
+        for _ in range(n_clock_warm):
             ctx.step(t)
             t += 1
         ctx.pass_times()
@@ -263,7 +272,7 @@ def main():
     ctx.set_timing(False)
     if world > 1:
         x = torch.tensor([ms_total, passes["update"], passes["stats"], passes["requant"], passes["exchange"]],
-                         device="cuda", dtype=torch.float64)
+                         dtype=torch.float64)
         dist.all_reduce(x, op=dist.ReduceOp.MAX)
         ms_total, passes["update"], passes["stats"], passes["requant"], passes["exchange"] = x.tolist()
     ms_step = ms_total / args.steps
@@ -294,7 +303,7 @@ def main():
     barrier()
     e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
     if world > 1:
-        x = torch.tensor([e2e_ms], device="cuda", dtype=torch.float64)
+        x = torch.tensor([e2e_ms], dtype=torch.float64)
         dist.all_reduce(x, op=dist.ReduceOp.MAX)
         e2e_ms = x.item()
 

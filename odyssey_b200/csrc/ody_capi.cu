@@ -678,11 +678,15 @@ extern "C" int ody_step_wait(ody_ctx* c, ody_step_result* out) {
       if (api && c->comm) api->commGetAsyncError(c->comm, &st);
       auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
       if ((st != ncclSuccess && st != ncclInProgress) || ms > c->cfg.comm_timeout_ms) {
+        const bool failed = st != ncclSuccess && st != ncclInProgress;
+        const std::string what = failed ? std::string("step: communicator failed: ") + api->getErrorString(st)
+                                        : "step: no completion within " + std::to_string(c->cfg.comm_timeout_ms) +
+                                              " ms";
         if (api && c->comm) api->commAbort(c->comm);
         c->comm = nullptr;
         c->broken = true;
         c->pending = false;
-        return ctx_fail(c, ODY_ERR_COMM_TIMEOUT, "step: communicator failed or timed out");
+        return ctx_fail(c, failed ? ODY_ERR_NCCL : ODY_ERR_COMM_TIMEOUT, what);
       }
     }
   } else {

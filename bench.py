@@ -246,7 +246,7 @@ def main():
     per_step = torch.tensor([(time.perf_counter() - w0) / max(args.warmup, 1)], dtype=torch.float64)
     if world > 1:
         dist.all_reduce(per_step, op=dist.ReduceOp.MAX)
-    n_clock_warm = max(3, min(2000, int(0.6 / max(per_step.item(), 1e-6))))
+    n_clock_warm = max(3, min(5000, int(1.5 / max(per_step.item(), 1e-6))))
     stream = torch.cuda.ExternalStream(ctx.stream_handle())
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ctx.set_timing(True)

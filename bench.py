@@ -188,6 +188,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tensors", type=int, default=64,
                     help="number of 4096x4096 tensors (64 = the 1B workload; fewer only for profiling)")
+    ap.add_argument("--quant", default="nvfp4_tensor",
+                    help="re-quantisation kind (the workload's is nvfp4_tensor; others only for comparisons)")
     args = ap.parse_args()
     global NT, TOTAL
     NT, TOTAL = args.tensors, args.tensors * PER
@@ -211,6 +213,7 @@ def main():
     wl = flat1b(ntensors=NT)
     kw = wl.step_kwargs()
     kw["device"] = local
+    kw["quant"] = args.quant
     if world > 1:
         ctx = ody.MixedPrecisionStep.from_process_group(wl.numels, **kw)
     else:

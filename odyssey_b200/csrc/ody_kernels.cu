@@ -754,13 +754,27 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
   const float r = __frcp_rn(s);
   if (ch.start == td.off && threadIdx.x == 0) a.qscale[ch.tensor] = s;
   const int64_t end = ch.start + ch.len;
+  // the next tile's master values are loaded before this tile is encoded
+  float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0;
+  {
+    const int64_t e0 = ch.start + (int64_t)threadIdx.x * kVec;
+    if (e0 < end) {
+      const float4* pp = reinterpret_cast<const float4*>(a.master + e0);
+      n0 = __ldcg(pp);
+      n1 = __ldcg(pp + 1);
+    }
+  }
   for (int64_t tb = ch.start; tb < end; tb += kTile) {
     const int64_t e0 = tb + (int64_t)threadIdx.x * kVec;
     const bool act = e0 < end;
     float x[8];
+    const float4 p0 = n0, p1 = n1;
+    if (e0 + kTile < end) {
+      const float4* pp = reinterpret_cast<const float4*>(a.master + e0 + kTile);
+      n0 = __ldcg(pp);
+      n1 = __ldcg(pp + 1);
+    }
     if (act) {
-      const float4* pp = reinterpret_cast<const float4*>(a.master + e0);
-      float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
       x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
       x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
 #pragma unroll

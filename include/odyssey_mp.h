@@ -179,6 +179,19 @@ int ody_ctx_pass_times(ody_ctx* ctx, double* ms_out, int64_t* steps_out);
 /* Quantised weights of one tensor in the reference's byte layout, and its
  * per-tensor scale (1.0 for kinds without one). */
 int ody_get_quant(ody_ctx* ctx, int32_t index, void* dst, size_t bytes, float* tensor_scale);
+/* The full low-precision model after a sharded step (ZeRO-1's consumer; the
+ * reference holds the whole model in one process, so the layout is that of
+ * AnyTensor.to_* per tensor, tensor_dtype_conv.mojo:281-366).  The gathered
+ * buffer holds every tensor's quantised region in global order;
+ * ody_ctx_quant_layout gives tensor index's byte offset in it and its
+ * meaningful bytes (ody_quant_bytes), and *total the buffer size
+ * (index < 0: total only). */
+int ody_ctx_quant_layout(const ody_ctx* ctx, int32_t index, int64_t* offset, int64_t* bytes, int64_t* total);
+/* Every rank's quantised weights and per-tensor scales into every rank's
+ * dst (device, *total bytes) and scales (device, one float per tensor):
+ * one NCCL broadcast per rank of its contiguous slice, grouped.  Collective:
+ * all ranks call it.  Synchronous, bounded by comm_timeout_ms. */
+int ody_ctx_gather_quant(ody_ctx* ctx, void* dst, float* scales);
 /* GradientScaler state (mixed_precision.mojo:77-93). */
 int ody_get_scaler(ody_ctx* ctx, float* scale, int64_t* steps_since_growth, int64_t* num_steps,
                    int64_t* step_count, int64_t* overflow_count);

@@ -82,6 +82,8 @@ _SIGS = {
     "ody_step_wait": (C.c_int, [_p, _p]),
     "ody_ctx_set_timing": (C.c_int, [_p, _i32]),
     "ody_ctx_pass_times": (C.c_int, [_p, _p, _p]),
+    "ody_ctx_quant_layout": (C.c_int, [_p, _i32, _p, _p, _p]),
+    "ody_ctx_gather_quant": (C.c_int, [_p, _p, _p]),
     "ody_get_quant": (C.c_int, [_p, _i32, _p, C.c_size_t, _p]),
     "ody_get_scaler": (C.c_int, [_p, _p, _p, _p, _p, _p]),
     "ody_set_scaler": (C.c_int, [_p, C.c_float, _i64, _i64, _i64, _i64]),

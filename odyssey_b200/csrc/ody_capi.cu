@@ -39,6 +39,9 @@ struct NcclApi {
   ncclResult_t (*getUniqueId)(ncclUniqueId*) = nullptr;
   ncclResult_t (*commInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
   ncclResult_t (*allGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*groupStart)() = nullptr;
+  ncclResult_t (*groupEnd)() = nullptr;
   ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*commAbort)(ncclComm_t) = nullptr;
   ncclResult_t (*commGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
@@ -63,11 +66,15 @@ static NcclApi* nccl_api(std::string& why) {
   api.getUniqueId = (decltype(api.getUniqueId))dlsym(h, "ncclGetUniqueId");
   api.commInitRankConfig = (decltype(api.commInitRankConfig))dlsym(h, "ncclCommInitRankConfig");
   api.allGather = (decltype(api.allGather))dlsym(h, "ncclAllGather");
+  api.broadcast = (decltype(api.broadcast))dlsym(h, "ncclBroadcast");
+  api.groupStart = (decltype(api.groupStart))dlsym(h, "ncclGroupStart");
+  api.groupEnd = (decltype(api.groupEnd))dlsym(h, "ncclGroupEnd");
   api.commDestroy = (decltype(api.commDestroy))dlsym(h, "ncclCommDestroy");
   api.commAbort = (decltype(api.commAbort))dlsym(h, "ncclCommAbort");
   api.commGetAsyncError = (decltype(api.commGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
   api.getErrorString = (decltype(api.getErrorString))dlsym(h, "ncclGetErrorString");
-  if (!api.getUniqueId || !api.commInitRankConfig || !api.allGather || !api.commDestroy ||
+  if (!api.getUniqueId || !api.commInitRankConfig || !api.allGather || !api.broadcast || !api.groupStart ||
+      !api.groupEnd || !api.commDestroy ||
       !api.commAbort || !api.commGetAsyncError || !api.getErrorString) {
     why = "libnccl.so.2 lacks a required symbol";
     return nullptr;
@@ -96,6 +103,12 @@ struct ody_ctx {
   std::vector<int32_t> local_of;   // global index -> local index or -1
   std::vector<TensorDesc> tdesc;   // local tensors
   std::vector<Chunk> chunks_upd;
+  // layout of the gathered quantised model: every tensor's region in global
+  // order (the same region sizes as the local arenas), and each rank's slice
+  std::vector<int64_t> gq_off;      // per global tensor
+  std::vector<int64_t> rank_qbeg, rank_qend;   // per rank, bytes
+  std::vector<int32_t> rank_tbeg, rank_tend;   // per rank, tensor indices
+  int64_t gq_total = 0;
   std::vector<uint32_t> jobs;  // apply-kernel job list (bit 31: requant job)
   int64_t n_total = 0, q_total = 0;
   cudaStream_t stream = nullptr;
@@ -144,6 +157,8 @@ static cudaError_t timing_collect(ody_ctx* c, int64_t slot) {
   c->tsteps += 1;
   return cudaSuccess;
 }
+
+static bool is_device_ptr(const void* p);
 
 static int ctx_fail(ody_ctx* c, int code, const std::string& msg) {
   g_err = msg;
@@ -388,6 +403,31 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   }
   c->n_total = off;
   c->q_total = qoff;
+  c->gq_off.assign(nt, 0);
+  c->rank_qbeg.assign(world, 0);
+  c->rank_qend.assign(world, 0);
+  c->rank_tbeg.assign(world, 0);
+  c->rank_tend.assign(world, 0);
+  {
+    int64_t g = 0;
+    std::vector<bool> seen(world, false);
+    for (int i = 0; i < nt; i++) {
+      const int r = c->owner[i];
+      const int64_t npad = (c->specs[i].numel + kPad - 1) / kPad * kPad;
+      if (!seen[r]) {
+        seen[r] = true;
+        c->rank_qbeg[r] = g;
+        c->rank_tbeg[r] = i;
+      }
+      c->gq_off[i] = g;
+      g += quant_region(c->specs[i].quant, npad);
+      c->rank_qend[r] = g;
+      c->rank_tend[r] = i + 1;
+    }
+    for (int r = 0; r < world; r++)
+      if (!seen[r]) c->rank_qbeg[r] = c->rank_qend[r] = g, c->rank_tbeg[r] = c->rank_tend[r] = nt;
+    c->gq_total = g;
+  }
   const int nl = (int)c->tdesc.size();
   // a blocking stream: work on it is ordered after work the caller queued on
   // the legacy default stream (e.g. PyTorch producing a device buffer that
@@ -728,6 +768,75 @@ extern "C" int ody_ctx_pass_times(ody_ctx* c, double* ms_out, int64_t* steps_out
   if (steps_out) *steps_out = c->tsteps;
   for (int k = 0; k < 4; k++) c->tms[k] = 0.0;
   c->tsteps = 0;
+  return ODY_OK;
+}
+
+extern "C" int ody_ctx_quant_layout(const ody_ctx* c, int32_t i, int64_t* offset, int64_t* bytes,
+                                    int64_t* total) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return fail(ODY_ERR_STATE, "context not finalized");
+  if (total) *total = c->gq_total;
+  if (i < 0) return ODY_OK;
+  if (i >= (int)c->specs.size()) return fail(ODY_ERR_ARG, "tensor index out of range");
+  if (offset) *offset = c->gq_off[i];
+  if (bytes) *bytes = ody_quant_bytes(c->specs[i].quant, c->specs[i].numel);
+  return ODY_OK;
+}
+
+extern "C" int ody_ctx_gather_quant(ody_ctx* c, void* dst, float* scales) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  if (c->broken) return ctx_fail(c, ODY_ERR_STATE, "context unusable after a communicator failure");
+  if (!dst || !scales) return ctx_fail(c, ODY_ERR_ARG, "null destination");
+  if (!is_device_ptr(dst) || !is_device_ptr(scales))
+    return ctx_fail(c, ODY_ERR_ARG, "gather destinations must be device memory");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  const int r = c->rank;
+  const int64_t nb = c->rank_qend[r] - c->rank_qbeg[r];
+  const int nts = c->rank_tend[r] - c->rank_tbeg[r];
+  if (c->world == 1) {
+    if (nb) ODY_CUDA(cudaMemcpyAsync(dst, c->qout, (size_t)nb, cudaMemcpyDeviceToDevice, c->stream));
+    if (nts) ODY_CUDA(cudaMemcpyAsync(scales, c->qscale, sizeof(float) * nts, cudaMemcpyDeviceToDevice, c->stream));
+    ODY_CUDA(cudaStreamSynchronize(c->stream));
+    return ODY_OK;
+  }
+  std::string why;
+  NcclApi* api = nccl_api(why);
+  if (!api) return ctx_fail(c, ODY_ERR_NCCL, why);
+  // one broadcast per rank of its contiguous slice, grouped: an allgather of
+  // unequal slices
+  api->groupStart();
+  for (int q = 0; q < c->world; q++) {
+    const int64_t qb = c->rank_qend[q] - c->rank_qbeg[q];
+    if (qb > 0)
+      api->broadcast(q == r ? (const void*)c->qout : nullptr, (uint8_t*)dst + c->rank_qbeg[q], (size_t)qb,
+                     ncclUint8, q, c->comm, c->stream);
+    const int tq = c->rank_tend[q] - c->rank_tbeg[q];
+    if (tq > 0)
+      api->broadcast(q == r ? (const void*)c->qscale : nullptr, scales + c->rank_tbeg[q], (size_t)tq,
+                     ncclFloat32, q, c->comm, c->stream);
+  }
+  ncclResult_t ge = api->groupEnd();
+  if (ge != ncclSuccess && ge != ncclInProgress)
+    return ctx_fail(c, ODY_ERR_NCCL, std::string("ncclGroupEnd: ") + api->getErrorString(ge));
+  int rc = wait_nccl(c, api, "gather of the quantised weights");
+  if (rc != ODY_OK) return rc;
+  ODY_CUDA(cudaEventRecord(c->done, c->stream));
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t q = cudaEventQuery(c->done);
+    if (q == cudaSuccess) break;
+    if (q != cudaErrorNotReady) return ctx_fail(c, ODY_ERR_CUDA, std::string("gather: ") + cudaGetErrorString(q));
+    ncclResult_t st = ncclSuccess;
+    api->commGetAsyncError(c->comm, &st);
+    auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+    if ((st != ncclSuccess && st != ncclInProgress) || ms > c->cfg.comm_timeout_ms) {
+      api->commAbort(c->comm);
+      c->comm = nullptr;
+      c->broken = true;
+      return ctx_fail(c, ODY_ERR_COMM_TIMEOUT, "gather of the quantised weights: communicator failed or timed out");
+    }
+  }
   return ODY_OK;
 }
 

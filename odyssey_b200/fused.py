@@ -127,6 +127,24 @@ class MixedPrecisionStep:
         L.check(L.lib().ody_get_quant(self._ctx, i, L.ptr(out), nb, C.byref(ts)), self._ctx)
         return QuantizedTensor(out, self.quants[i], self.numels[i], ts.value)
 
+    def quant_layout(self, i=-1):
+        """(offset, bytes, total) of tensor i in the gathered quantised model."""
+        off, nb, tot = C.c_int64(0), C.c_int64(0), C.c_int64(0)
+        L.check(L.lib().ody_ctx_quant_layout(self._ctx, i, C.byref(off), C.byref(nb), C.byref(tot)), self._ctx)
+        return off.value, nb.value, tot.value
+
+    def gather_quant(self):
+        """The whole model's quantised weights on this rank's GPU (collective):
+        (uint8 CUDA tensor in quant_layout order, float32 CUDA tensor of the
+        per-tensor scales)."""
+        import torch
+        total = self.quant_layout()[2]
+        dev = torch.device("cuda", self.cfg.device)
+        buf = torch.empty(max(total, 1), dtype=torch.uint8, device=dev)
+        scales = torch.empty(max(len(self.numels), 1), dtype=torch.float32, device=dev)
+        L.check(L.lib().ody_ctx_gather_quant(self._ctx, buf.data_ptr(), scales.data_ptr()), self._ctx)
+        return buf, scales
+
     # ---- the step ----
     def step(self, t=1):
         r = L.StepResult()

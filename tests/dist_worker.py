@@ -45,7 +45,12 @@ def main():
         res.append([r["skipped"], r["nonfinite_count"], r["sumsq"], r["grad_norm"], r["scale_next"]])
         if not r["skipped"]:
             t += 1
-    arrays = {"owned": np.array(ctx.owned), "results": np.array(res, np.float64)}
+    buf, scales = ctx.gather_quant()
+    gathered = buf.cpu().numpy()
+    arrays = {"owned": np.array(ctx.owned), "results": np.array(res, np.float64), "scales": scales.cpu().numpy()}
+    for i in range(len(wl.numels)):
+        off, nb, _ = ctx.quant_layout(i)
+        arrays[f"gathered{i}"] = gathered[off:off + nb]
     for i in ctx.owned:
         arrays[f"master{i}"] = ctx.master(i)
         q = ctx.get_quant(i)

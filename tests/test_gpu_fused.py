@@ -216,3 +216,20 @@ def test_async_pipeline_matches_sync(oracle):
         np.testing.assert_array_equal(a.master(i), b.master(i))
     a.close()
     b.close()
+
+
+def test_gather_quant_single_rank(oracle):
+    """With one rank the gathered model is the local quantised arena in
+    global tensor order."""
+    wl = W.Workload("gq", [(1000,), (33,), (70000,)], "bfloat16", "none", "adamw",
+                    dict(learning_rate=1e-3, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.01),
+                    0.05, 1e-3, 1024.0)
+    ctx, model, _ = run_pair(oracle, wl, 2, quants=["nvfp4_tensor", "mxfp4", "fp8_tensor"])
+    buf, scales = ctx.gather_quant()
+    g = buf.cpu().numpy()
+    for i in range(3):
+        off, nb, total = ctx.quant_layout(i)
+        assert off % 256 == 0 and off + nb <= total
+        np.testing.assert_array_equal(g[off:off + nb], model.qout[i][:nb])
+        assert scales[i].item() == model.qscale[i][0]
+    ctx.close()

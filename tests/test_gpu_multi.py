@@ -54,3 +54,8 @@ def test_two_rank_resnet18_matches_unsharded_oracle(oracle, tmp_path):
             np.testing.assert_array_equal(z[f"codes{i}"], model.qout[i][: z[f"codes{i}"].size])
             assert z[f"scale{i}"] == model.qscale[i][0]
     assert sorted(seen) == list(range(len(wl.numels)))
+    # the gathered model on each rank: every tensor's codes and scale
+    for z in ranks:
+        for i in range(len(wl.numels)):
+            np.testing.assert_array_equal(z[f"gathered{i}"], model.qout[i][: z[f"gathered{i}"].size])
+            assert z["scales"][i] == model.qscale[i][0]

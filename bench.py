@@ -9,6 +9,14 @@ per-tensor scale.  With N GPUs the 64 tensors are ZeRO-1-sharded (8 whole
 tensors per rank at N=8): total work is fixed, scaling is "strong".
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload flat1b|resnet18|lenet]
+
+`--workload resnet18` (configs[3], 62 tensors, 11.2 M params, AdamW, BF16
+grads, FP8-E4M3 per-tensor) and `--workload lenet` (configs[0], 10 tensors,
+61,706 params, SGD-momentum, FP16 grads, FP16 out) are secondary lines: the
+same step on the reference's smaller configurations, where launch latency
+rather than HBM bandwidth bounds the step.  Their gradients are fixed across
+steps (no inf injection), as for the 1B model.
 
 One step = one pass of the hot path (stats -> [allgather] -> update ->
 requant) over the whole model.  `value` is params/s of the whole job with
@@ -36,6 +44,26 @@ PER = SIDE * SIDE
 TOTAL = NT * PER
 ALG_BYTES_STEP = 26.5625        # grads 2 + master/m/v r+w 24 + NVFP4 codes 0.5625 (B/param)
 ALG_BYTES_UPDATE = 26.5625      # apply kernel: grads 2 + master/m/v r+w 24 + NVFP4 codes 0.5625
+WORKLOAD = "flat1b"
+QUANT_BYTES = {"none": 0.0, "fp16": 2.0, "bf16": 2.0, "fp8": 1.0, "bf8": 1.0, "fp8_tensor": 1.0,
+               "mxfp4": 17 / 32, "nvfp4": 9 / 16, "nvfp4_tensor": 9 / 16}
+GRAD_BYTES = {"float32": 4, "float16": 2, "bfloat16": 2}
+
+
+def alg_bytes_per_param(wl, quant):
+    """HBM bytes one parameter needs per step: its gradient read, master and
+    optimizer states read and written, and its re-quantised code written."""
+    nstates = {"sgd": 1 if wl.hyper.get("momentum", 0.0) > 0 else 0, "adam": 2, "adamw": 2}[wl.optimizer]
+    return GRAD_BYTES[wl.grad_dtype] + 8 * (1 + nstates) + QUANT_BYTES[quant]
+
+
+def make_workload(name, ntensors):
+    from odyssey_b200 import workloads as W
+    if name == "flat1b":
+        return W.flat1b(ntensors=ntensors, side=SIDE)
+    wl = W.lenet() if name == "lenet" else W.resnet18()
+    wl.inf_every = 0
+    return wl
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes per param of one apply_kernel launch, measured with ncu
 # (dram__bytes_read.sum + dram__bytes_write.sum of the 8-tensor case
@@ -122,19 +150,27 @@ def cpu_info():
     return model, os.cpu_count()
 
 
-def cpu_reference_sample(seconds=12.0, ntensors=1):
+def cpu_reference_sample(seconds=12.0, ntensors=1, quant="nvfp4_tensor"):
     """The oracle (CPU restatement of the reference path) on the host cores:
-    the same AdamW + clip + NVFP4-per-tensor step over `ntensors` of the
-    workload's 4096x4096 tensors, repeated for about `seconds`."""
+    the workload's step (for the 1B model over `ntensors` of its 4096x4096
+    tensors; the smaller models whole), repeated for about `seconds`."""
     from oracle import oracle as O
-    from odyssey_b200 import workloads as W
     O.build()
     threads = os.cpu_count() or 1
     O.set_threads(threads)
-    wl = W.flat1b(ntensors=ntensors, side=SIDE)
-    specs = [{"numel": n, "grad_dtype": O.BF16, "quant": O.Q_NVFP4_TENSOR} for n in wl.numels]
-    m = O.Model(specs, O.ADAMW, 1e-3, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.01,
-                clip_enabled=True, max_norm=1.0, scaler_kwargs={"initial_scale": 4096.0})
+    wl = make_workload(WORKLOAD, ntensors)
+    gdt = {"float32": O.F32, "float16": O.F16, "bfloat16": O.BF16}[wl.grad_dtype]
+    qk = {"none": 0, "fp16": 1, "bf16": 2, "fp8": 3, "bf8": 4, "fp8_tensor": 5, "mxfp4": 6, "nvfp4": 7,
+          "nvfp4_tensor": 8}[quant]
+    specs = [{"numel": n, "grad_dtype": gdt, "quant": qk} for n in wl.numels]
+    hy = wl.hyper
+    opt = {"sgd": O.SGD, "adam": O.ADAM, "adamw": O.ADAMW}[wl.optimizer]
+    sk = {k: v for k, v in wl.step_kwargs().items() if k in ("initial_scale", "growth_factor", "backoff_factor",
+                                                               "growth_interval", "min_scale", "max_scale")}
+    m = O.Model(specs, opt, hy["learning_rate"], momentum=hy.get("momentum", 0.0), beta1=hy.get("beta1", 0.9),
+                beta2=hy.get("beta2", 0.999), epsilon=hy.get("epsilon", 1e-8),
+                weight_decay=hy.get("weight_decay", 0.0), clip_enabled=wl.clip is not None,
+                max_norm=wl.clip or 1.0, scaler_kwargs=sk)
     for i, x in enumerate(wl.master(0)):
         m.master[i][:] = x
     grads = wl.grads(0)
@@ -149,16 +185,17 @@ def cpu_reference_sample(seconds=12.0, ntensors=1):
         t += 1
     sec = statistics.median(times)
     params = sum(wl.numels)
+    what = (f"{ntensors} x 4096x4096 tensor(s) ({params} params) of the 1B workload" if WORKLOAD == "flat1b"
+            else f"the whole {wl.name} model ({params} params)")
     return {"value": params / sec, "unit": "params/s", "cores": threads, "kind": "port",
-            "sample": f"{ntensors} x 4096x4096 tensor(s) ({params} params) of the 1B workload, "
-                      f"AdamW+clip+NVFP4-per-tensor, {len(times)} steps, median {sec * 1e3:.1f} ms/step, "
-                      f"{threads} OpenMP threads on {cpu_info()[0]}"}
+            "sample": f"{what}, {wl.optimizer}{'+clip' if wl.clip else ''}+{quant}, {len(times)} steps, "
+                      f"median {sec * 1e3:.3f} ms/step, {threads} OpenMP threads on {cpu_info()[0]}"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    cb = cpu_reference_sample(seconds=max(3.0, min(30.0, 2.0 * args.steps)))
+    cb = cpu_reference_sample(seconds=max(3.0, min(30.0, 2.0 * args.steps)), quant=QUANT)
     line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "params/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": TOTAL / cb["value"] * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -169,7 +206,18 @@ def run_reference(args, rank, world):
     return 0
 
 
+GDT_SHORT = {"float32": "f32", "float16": "f16", "bfloat16": "bf16"}
+QUANT = "nvfp4_tensor"
+
+
 def config_dict(world):
+    if WORKLOAD != "flat1b":
+        wl = make_workload(WORKLOAD, NT)
+        return {"workload": wl.name + (" (configs[0])" if WORKLOAD == "lenet" else " (configs[3])"),
+                "params": TOTAL, "tensors": len(wl.numels), "grad_dtype": GDT_SHORT[wl.grad_dtype],
+                "master_dtype": "f32", "optimizer": wl.optimizer, "clip_max_norm": wl.clip, "quant": QUANT,
+                "loss_scale": wl.loss_scale, "parallelism": f"zero1 whole-tensor shards x{world}",
+                "l2": "model smaller than L2; no flush (secondary, latency-bound line)"}
     name = "flat1b_adamw_clip_bf16_nvfp4 (configs[4])" if NT == 64 else f"flat_{NT}x4096^2 (profiling case)"
     return {"workload": name, "params": TOTAL, "tensors": NT,
             "tensor_shape": [SIDE, SIDE], "grad_dtype": "bf16", "master_dtype": "f32", "optimizer": "adamw",
@@ -188,11 +236,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tensors", type=int, default=64,
                     help="number of 4096x4096 tensors (64 = the 1B workload; fewer only for profiling)")
-    ap.add_argument("--quant", default="nvfp4_tensor",
-                    help="re-quantisation kind (the workload's is nvfp4_tensor; others only for comparisons)")
+    ap.add_argument("--quant", default=None,
+                    help="re-quantisation kind (default: the workload's own; others only for comparisons)")
+    ap.add_argument("--workload", default="flat1b", choices=["flat1b", "resnet18", "lenet"],
+                    help="flat1b = the headline 1B model; resnet18 / lenet = secondary lines")
     args = ap.parse_args()
-    global NT, TOTAL
-    NT, TOTAL = args.tensors, args.tensors * PER
+    global NT, TOTAL, WORKLOAD, QUANT, ALG_BYTES_STEP, ALG_BYTES_UPDATE
+    WORKLOAD, NT = args.workload, args.tensors
+    wl = make_workload(WORKLOAD, NT)
+    QUANT = args.quant or wl.quant
+    TOTAL = wl.total
+    ALG_BYTES_STEP = ALG_BYTES_UPDATE = alg_bytes_per_param(wl, QUANT)
     world = env_int("WORLD_SIZE", 1)
     rank = env_int("RANK", 0)
     local = env_int("LOCAL_RANK", 0)
@@ -203,32 +257,33 @@ def main():
     import torch.distributed as dist
     import odyssey_b200 as ody
     from odyssey_b200 import _lib as L
-    from odyssey_b200.workloads import flat1b
 
     torch.cuda.set_device(local)
     if world > 1:
         # host-side plumbing only (NCCL id broadcast, barriers, max over ranks);
         # the step's own exchange runs on the library's NCCL communicator
         dist.init_process_group("gloo")
-    wl = flat1b(ntensors=NT)
     kw = wl.step_kwargs()
     kw["device"] = local
-    kw["quant"] = args.quant
+    kw["quant"] = QUANT
     if world > 1:
         ctx = ody.MixedPrecisionStep.from_process_group(wl.numels, **kw)
     else:
         ctx = ody.MixedPrecisionStep(wl.numels, **kw)
     owned = ctx.owned
-    nloc = len(owned) * PER
+    nloc = sum(wl.numels[i] for i in owned)
+    gdt = getattr(torch, wl.grad_dtype)
+    gsz = GRAD_BYTES[wl.grad_dtype]
 
     # synthetic inputs generated on the device (seeded), copied into the arenas
     gen = torch.Generator(device="cuda")
     for i in owned:
+        n = wl.numels[i]
         gen.manual_seed(1000 + i)
-        m = torch.randn(PER, device="cuda", generator=gen) * 0.02
+        m = torch.randn(n, device="cuda", generator=gen) * wl.master_std
         ctx.upload(L.BUF_MASTER, i, m)
         gen.manual_seed(5000 + i)
-        g = (torch.randn(PER, device="cuda", generator=gen) * (1e-3 * 4096.0)).to(torch.bfloat16)
+        g = (torch.randn(n, device="cuda", generator=gen) * (wl.grad_std * wl.loss_scale)).to(gdt)
         ctx.upload(L.BUF_GRAD, i, g)
         del m, g
     torch.cuda.synchronize()
@@ -252,15 +307,19 @@ def main():
     n_clock_warm = max(3, min(5000, int(1.5 / max(per_step.item(), 1e-6))))
     stream = torch.cuda.ExternalStream(ctx.stream_handle())
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ctx.set_timing(True)
-    ctx.pass_times()
     barrier()
     with Clocks(local) as clk:
-        # keep the GPU loaded while the clock sampler starts (untimed steps)
-        for _ in range(n_clock_warm):
-            ctx.step(t)
-            t += 1
+        # keep the GPU loaded while the clock sampler starts (untimed steps);
+        # per-pass times are taken here, so that the timed steps carry no
+        # extra events
+        ctx.set_timing(True)
         ctx.pass_times()
+        for _ in range(n_clock_warm):
+            ctx.step_async(t)
+            t += 1
+            ctx.wait()
+        passes, nsteps = ctx.pass_times()
+        ctx.set_timing(False)
         barrier()
         ev0.record(stream)
         for _ in range(args.steps):
@@ -271,8 +330,6 @@ def main():
         ev1.synchronize()
     barrier()
     ms_total = ev0.elapsed_time(ev1)
-    passes, nsteps = ctx.pass_times()
-    ctx.set_timing(False)
     if world > 1:
         x = torch.tensor([ms_total, passes["update"], passes["stats"], passes["requant"], passes["exchange"]],
                          dtype=torch.float64)
@@ -282,13 +339,13 @@ def main():
     value = TOTAL / (ms_step * 1e-3)
 
     # ---- end to end through the C ABI: pinned host gradients -> step -> result
-    pinned = [torch.empty(PER, dtype=torch.bfloat16, pin_memory=True) for _ in owned]
+    pinned = [torch.empty(wl.numels[i] * gsz, dtype=torch.uint8, pin_memory=True) for i in owned]
     for k, i in enumerate(owned):
-        pinned[k].copy_(torch.from_numpy(ctx.download(L.BUF_GRAD, i)).view(torch.bfloat16))
+        pinned[k].copy_(torch.from_numpy(ctx.download(L.BUF_GRAD, i).view(np.uint8)))
     lib = L.lib()
     for _ in range(1):
         for k, i in enumerate(owned):
-            L.check(lib.ody_upload_async(ctx._ctx, L.BUF_GRAD, i, pinned[k].data_ptr(), PER * 2), ctx._ctx)
+            L.check(lib.ody_upload_async(ctx._ctx, L.BUF_GRAD, i, pinned[k].data_ptr(), pinned[k].numel()), ctx._ctx)
         ctx.step(t)
         t += 1
     barrier()
@@ -297,7 +354,7 @@ def main():
     e0.record(stream)
     for _ in range(args.e2e_steps):
         for k, i in enumerate(owned):
-            L.check(lib.ody_upload_async(ctx._ctx, L.BUF_GRAD, i, pinned[k].data_ptr(), PER * 2), ctx._ctx)
+            L.check(lib.ody_upload_async(ctx._ctx, L.BUF_GRAD, i, pinned[k].data_ptr(), pinned[k].numel()), ctx._ctx)
         ctx.step(t)  # synchronous: includes the device->host read of the step result
         t += 1
     e1.record(stream)
@@ -310,6 +367,23 @@ def main():
         dist.all_reduce(x, op=dist.ReduceOp.MAX)
         e2e_ms = x.item()
 
+    # N > 1: the all-gather of the re-quantised model after the sharded step
+    # (not part of the step; reported beside it)
+    gather = None
+    if world > 1:
+        gq_total = ctx.quant_layout()[2]
+        ctx.gather_quant()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(5):
+            ctx.gather_quant()
+        g1.record(stream)
+        g1.synchronize()
+        x = torch.tensor([g0.elapsed_time(g1) / 5], dtype=torch.float64)
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        gather = {"ms": x.item(), "bytes": gq_total, "gbs": gq_total / (x.item() * 1e-3) / 1e9}
+
     if rank == 0:
         peak, peak_kind = peaks()
         upd_ms = passes["update"] / max(nsteps, 1)
@@ -317,7 +391,7 @@ def main():
         step_gbs_gpu = ALG_BYTES_STEP * nloc / (ms_step * 1e-3) / 1e9
         cb = None
         if world == 1 and not args.no_cpu_baseline:
-            cb = cpu_reference_sample()
+            cb = cpu_reference_sample(quant=QUANT)
         line = {
             "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
@@ -328,17 +402,21 @@ def main():
             "roofline": {"kernel": "apply_kernel (update + per-tensor requant)", "bound": "hbm", "achieved": upd_gbs, "peak": peak,
                          "unit": "GB/s", "frac": upd_gbs / peak, "peak_source": peak_kind,
                          "alg_bytes_per_launch": ALG_BYTES_UPDATE * nloc,
-                         "traffic": TRAFFIC_BYTES_PER_PARAM_APPLY * nloc,
-                         "traffic_source": "ncu capture of an 8-tensor case scaled by params"},
+                         "traffic": (TRAFFIC_BYTES_PER_PARAM_APPLY * nloc
+                                     if WORKLOAD == "flat1b" and QUANT == "nvfp4_tensor" else None),
+                         "traffic_source": ("ncu capture of an 8-tensor case scaled by params"
+                                            if WORKLOAD == "flat1b" and QUANT == "nvfp4_tensor" else None)},
             "e2e": {"value": TOTAL / (e2e_ms * 1e-3), "unit": "params/s", "ms_per_step": e2e_ms,
                     "wall_ms_per_step": wall * 1e3 / args.e2e_steps,
-                    "h2d_bytes_per_step": 2 * nloc, "d2h_bytes_per_step": 80},
+                    "h2d_bytes_per_step": gsz * nloc, "d2h_bytes_per_step": 80},
             "gpu_launches": args.steps * (2 if world == 1 else 3),
             "clocks": clk.summary(),
             "last_step": {k: res[k] for k in ("grad_norm", "clip_coef", "clipped", "skipped", "scale_used")},
         }
         if cb:
             line["cpu_baseline"] = cb
+        if gather:
+            line["gather_quant"] = gather
         print(json.dumps(line), flush=True)
     ctx.close()
     if world > 1:

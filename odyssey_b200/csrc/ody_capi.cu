@@ -7,6 +7,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <chrono>
 #include <string>
 #include <vector>
@@ -462,7 +463,10 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   if (!c->chunks_upd.empty())
     ODY_CUDA(cudaMemcpyAsync(c->d_chunks_upd, c->chunks_upd.data(), sizeof(Chunk) * c->chunks_upd.size(),
                              cudaMemcpyHostToDevice, c->stream));
+  // a model smaller than one chunk per resident CTA launches one CTA per
+  // update chunk: idle CTAs of a persistent grid only add launch latency
   c->grid_apply = apply_grid(c->gdt, c->cfg.optimizer, c->cfg.device);
+  if ((size_t)c->grid_apply > c->chunks_upd.size()) c->grid_apply = (int)std::max<size_t>(1, c->chunks_upd.size());
   build_jobs(c);
   ODY_CUDA(dalloc(&c->d_jobs, sizeof(uint32_t) * (c->jobs.size() + 1)));
   if (!c->jobs.empty())
@@ -470,7 +474,14 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
                              c->stream));
   ODY_CUDA(dalloc(&c->sync, sizeof(uint32_t) * (nl + 1)));
   ODY_CUDA(cudaMemsetAsync(c->sync, 0, sizeof(uint32_t) * (nl + 1), c->stream));
-  c->grid_stats = stats_grid(c->cfg.device);
+  // at least 16 groups of 8 gradients per thread, at most the resident grid
+  // (the fixed-order partial reduction makes the sum depend on the grid, which
+  // is fixed for the context's lifetime)
+  {
+    const int64_t per_cta = (int64_t)kThreads * 16 * 8;
+    const int64_t want = (c->n_total + per_cta - 1) / per_cta;
+    c->grid_stats = (int)std::max<int64_t>(1, std::min<int64_t>(stats_grid(c->cfg.device), want));
+  }
   ODY_CUDA(dalloc(&c->partials, sizeof(StatsPartial) * c->grid_stats));
   ODY_CUDA(dalloc(&c->ticket, sizeof(unsigned)));
   ODY_CUDA(cudaMemsetAsync(c->ticket, 0, sizeof(unsigned), c->stream));

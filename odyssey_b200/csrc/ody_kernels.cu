@@ -570,6 +570,68 @@ __device__ __forceinline__ float tensor_scale_from_amax(int kind, uint32_t amax_
   return s;
 }
 
+// NVFP4 with a per-tensor scale s_t encodes q = RN(x / s_t) against the
+// block-scale thresholds Q = X_T(bs).  x -> RN(x / s_t) is monotone, so
+// RN(|x| / s_t) >= Q exactly when |x| >= X'(Q), the least float whose IEEE
+// quotient by s_t reaches Q; the block amax of q is RN(amax|x| / s_t) for the
+// same reason.  A requant job therefore builds the composite table X'(X_T(bs))
+// for s_t once (one exact double product per threshold) and then encodes
+// the raw master with compares only, dividing once per block instead of once
+// per element.
+// The composite table covers the block-scale codes 64..127 (E4M3 2.0 up):
+// with s_t = amax / 2688 a block's q amax is at most 2688, so its scale code
+// is at most 0x7e, and only a block whose amax is below about 1/224 of the
+// tensor's falls under the table and divides element by element.
+constexpr int kCxFirst = 64;
+constexpr int kCxCount = 128 - kCxFirst;
+
+__device__ __forceinline__ float composite_threshold(float Q, float s) {
+  // RN(y) >= Q exactly when y is at least the midpoint m between Q and its
+  // predecessor (at a tie RN picks the even encoding: Q itself when Q's last
+  // bit is 0, else the predecessor, and then y must exceed m).  With
+  // y = x / s that is x >= m * s, a product exact in double (m has at most
+  // 26 significant bits, s 24); the least such float is m * s rounded up.
+  // Q = +Inf: RN overflows from 2^128 - 2^103 up (a tie rounded to Inf).
+  if (!(Q > 0.0f)) return Q;  // NaN: "never"; 0: every x
+  const uint32_t qb = __float_as_uint(Q);
+  const double m = qb == 0x7f800000u ? 0x1p128 - 0x1p103
+                                      : 0.5 * ((double)__uint_as_float(qb - 1u) + (double)Q);
+  const double P = m * (double)s;
+  float x = __double2float_ru(P);
+  if ((qb & 1u) && (double)x == P) x = __uint_as_float(__float_as_uint(x) + 1u);
+  return x;
+}
+
+// one warp's slice of an NVFP4 per-tensor-scaled tile from the raw master
+// values x (s_t > 0 finite); blocks with a non-finite element, an infinite
+// q amax or a zero block scale divide element by element as the reference does
+__device__ __forceinline__ void stage_nvfp4_tensor(const float x[8], uint8_t* ws, const Fp4Thr* thr_q,
+                                                   const Fp4Thr* thr_x, float st) {
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; k++) am = amax_acc(am, x[k]);
+  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+  const float amq = __fdiv_rn(am, st);
+  const uint8_t e = e4m3_scale_from_f32(block_scale_value(amq));
+  const bool z = e == 0;
+  const bool special = e < kCxFirst || amq == __uint_as_float(0x7f800000u) || any_nonfinite8(x);
+  const int lane = threadIdx.x & 31;
+  uint8_t* dst = ws + (lane >> 1) * 9 + 4 * (lane & 1);
+  if (!special) {
+    const float* t = thr_x[e - kCxFirst].t;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      dst[i] = (uint8_t)((fp4_encode_plain(x[2 * i], t) << 4) | fp4_encode_plain(x[2 * i + 1], t));
+  } else {
+    const float* t = thr_q[e].t;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      dst[i] = (uint8_t)((fp4_encode(__fdiv_rn(x[2 * i], st), t, z) << 4) |
+                         fp4_encode(__fdiv_rn(x[2 * i + 1], st), t, z));
+  }
+  if (lane & 1) ws[(lane >> 1) * 9 + 8] = e;
+}
+
 __device__ __forceinline__ float block_amax_reduce(float v) {
   __shared__ float sm[32];
 #pragma unroll
@@ -728,7 +790,7 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
 }
 
 __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& ch, const Fp4Thr* s_nv,
-                                              uint8_t* stage) {
+                                              Fp4Thr* s_cx, int* s_cx_tensor, uint8_t* stage) {
   const TensorDesc td = a.tensors[ch.tensor];
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
@@ -753,6 +815,16 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
   const float s = tensor_scale_from_amax(kind, __ldcg(&a.amax_slots[ch.tensor]));
   const float r = __frcp_rn(s);
   if (ch.start == td.off && threadIdx.x == 0) a.qscale[ch.tensor] = s;
+  if (kind == Q_NVFP4_TENSOR && *s_cx_tensor != ch.tensor) {
+    // composite thresholds for this tensor's scale (kept for the CTA's next
+    // requant job of the same tensor)
+    float* cx = reinterpret_cast<float*>(s_cx);
+    const float* q = reinterpret_cast<const float*>(s_nv);
+    for (int i = threadIdx.x; i < kCxCount * 8; i += blockDim.x)
+      cx[i] = (i & 7) == 7 ? 0.0f : composite_threshold(q[kCxFirst * 8 + i], s);
+    __syncthreads();
+    if (threadIdx.x == 0) *s_cx_tensor = ch.tensor;
+  }
   const int64_t end = ch.start + ch.len;
   // the next tile's master values are loaded before this tile is encoded
   float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0;
@@ -777,8 +849,10 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
     if (act) {
       x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
       x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
+      if (kind != Q_NVFP4_TENSOR) {
 #pragma unroll
-      for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
+        for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
+      }
     } else {
 #pragma unroll
       for (int k = 0; k < 8; k++) x[k] = 0.0f;
@@ -788,7 +862,7 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
         const int64_t tile_in_tensor = (tb - td.off) / kTile;
         const int w = threadIdx.x >> 5;
         uint8_t* ws = stage + w * kWarpStage;
-        stage_fp4<false>(x, ws, s_nv);
+        stage_nvfp4_tensor(x, ws, s_nv, s_cx, s);
         __syncwarp();
         flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
         __syncwarp();
@@ -804,6 +878,8 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
+  __shared__ Fp4Thr s_cx[kCxCount];
+  __shared__ int s_cx_tensor;
   __shared__ uint32_t s_next;
   const Decision* dec = a.dec;
   if (dec->skip) return;
@@ -811,7 +887,10 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   const bool clipped = dec->clipped != 0;
   const float coef = dec->coef;
   load_thr_smem(s_mx, s_nv);
-  if (threadIdx.x == 0) s_next = atomicAdd(&a.sync[0], 1u);
+  if (threadIdx.x == 0) {
+    s_next = atomicAdd(&a.sync[0], 1u);
+    s_cx_tensor = -1;
+  }
   __syncthreads();
   uint32_t j = s_next;
   while (j < (uint32_t)a.njobs) {
@@ -820,7 +899,7 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
     const uint32_t job = a.jobs[j];
     const Chunk ch = a.chunks[job & ~kRequantJob];
     if (job & kRequantJob)
-      requant_chunk(a, ch, s_nv, stage);
+      requant_chunk(a, ch, s_nv, s_cx, &s_cx_tensor, stage);
     else
       update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, stage);
     __syncthreads();

@@ -233,3 +233,52 @@ def test_gather_quant_single_rank(oracle):
         np.testing.assert_array_equal(g[off:off + nb], model.qout[i][:nb])
         assert scales[i].item() == model.qscale[i][0]
     ctx.close()
+
+
+def _wide_master(rng, n, lo_exp, hi_exp, zeros=0.02, specials=()):
+    """float32 values with log-uniform magnitudes 2^[lo_exp, hi_exp), random
+    signs, some exact zeros and the given special values at random places."""
+    e = rng.uniform(lo_exp, hi_exp, n)
+    x = (np.exp2(e) * rng.choice([-1.0, 1.0], n)).astype(np.float32)
+    x[rng.random(n) < zeros] = 0.0
+    for v in specials:
+        x[rng.integers(n)] = v
+    return x
+
+
+def test_nvfp4_tensor_scale_sweep(oracle):
+    """NVFP4 with a per-tensor scale over tensors whose scales span the float
+    range (subnormal to huge amax, wide in-tensor spread, signed zeros, NaN
+    and Inf elements): the raw-master encode with composite thresholds
+    against the oracle's element-by-element division, bit for bit.  SGD with
+    lr 0 keeps the masters as written."""
+    from odyssey_b200 import MixedPrecisionStep
+    rng = np.random.Generator(np.random.PCG64(77))
+    ranges = [(-149, -126), (-140, -100), (-60, -20), (-30, 0), (-8, -2), (-2, 2), (0, 30), (20, 60),
+              (90, 127), (100, 127.9), (-149, 127.9)]
+    masters = []
+    for lo, hi in ranges:
+        masters.append(_wide_master(rng, 4096 + int(rng.integers(0, 300)), lo, hi))
+    masters.append(_wide_master(rng, 3000, -10, 0, specials=[np.nan]))
+    masters.append(_wide_master(rng, 3000, -10, 0, specials=[-np.inf]))
+    masters.append(_wide_master(rng, 3000, -10, 0, specials=[np.float32(3.4e38), -0.0]))
+    masters.append(np.zeros(100, np.float32))
+    numels = [m.size for m in masters]
+    ctx = MixedPrecisionStep(numels, grad_dtype="float32", quant="nvfp4_tensor", optimizer="sgd",
+                             learning_rate=0.0, momentum=0.0, weight_decay=0.0, use_gradient_scaler=False)
+    specs = [{"numel": n, "grad_dtype": 0, "quant": QK["nvfp4_tensor"]} for n in numels]
+    model = oracle.Model(specs, OPT["sgd"], 0.0, use_scaler=False, scaler_kwargs={"initial_scale": 1.0})
+    for i, m in enumerate(masters):
+        ctx.set_master(i, m)
+        model.master[i][:] = m
+    grads = [np.zeros(n, np.float32) for n in numels]
+    for i, g in enumerate(grads):
+        ctx.set_grad(i, g)
+    ctx.step(1)
+    model.step(grads, 1)
+    for i in range(len(numels)):
+        q = ctx.get_quant(i)
+        np.testing.assert_array_equal(q.data, model.qout[i][:q.data.size], err_msg=f"tensor {i} {ranges[i:i+1]}")
+        assert np.float32(q.tensor_scale) == model.qscale[i][0] or (
+            np.isnan(q.tensor_scale) and np.isnan(model.qscale[i][0])), i
+    ctx.close()

@@ -238,6 +238,10 @@ def main():
                     help="number of 4096x4096 tensors (64 = the 1B workload; fewer only for profiling)")
     ap.add_argument("--quant", default=None,
                     help="re-quantisation kind (default: the workload's own; others only for comparisons)")
+    ap.add_argument("--clock-warm-s", type=float, default=1.5,
+                    help="untimed steps run for about this long while the clock sampler starts (0 for ncu captures)")
+    ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
+                    help="replay each step as one CUDA graph launch (auto: on with one GPU)")
     ap.add_argument("--workload", default="flat1b", choices=["flat1b", "resnet18", "lenet"],
                     help="flat1b = the headline 1B model; resnet18 / lenet = secondary lines")
     args = ap.parse_args()
@@ -270,6 +274,9 @@ def main():
         ctx = ody.MixedPrecisionStep.from_process_group(wl.numels, **kw)
     else:
         ctx = ody.MixedPrecisionStep(wl.numels, **kw)
+    use_graph = args.graph == "on" or (args.graph == "auto" and world == 1)
+    if use_graph:
+        ctx.set_graph(True)
     owned = ctx.owned
     nloc = sum(wl.numels[i] for i in owned)
     gdt = getattr(torch, wl.grad_dtype)
@@ -304,7 +311,7 @@ def main():
     per_step = torch.tensor([(time.perf_counter() - w0) / max(args.warmup, 1)], dtype=torch.float64)
     if world > 1:
         dist.all_reduce(per_step, op=dist.ReduceOp.MAX)
-    n_clock_warm = max(3, min(5000, int(1.5 / max(per_step.item(), 1e-6))))
+    n_clock_warm = max(3, min(5000, int(args.clock_warm_s / max(per_step.item(), 1e-6))))
     stream = torch.cuda.ExternalStream(ctx.stream_handle())
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -410,6 +417,7 @@ def main():
                     "wall_ms_per_step": wall * 1e3 / args.e2e_steps,
                     "h2d_bytes_per_step": gsz * nloc, "d2h_bytes_per_step": 80},
             "gpu_launches": args.steps * (2 if world == 1 else 3),
+            "graph_mode": use_graph,
             "clocks": clk.summary(),
             "last_step": {k: res[k] for k in ("grad_norm", "clip_coef", "clipped", "skipped", "scale_used")},
         }

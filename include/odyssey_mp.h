@@ -176,6 +176,16 @@ int ody_step_wait(ody_ctx* ctx, ody_step_result* out);
 int ody_ctx_set_timing(ody_ctx* ctx, int32_t enable);
 int ody_ctx_pass_times(ody_ctx* ctx, double* ms_out, int64_t* steps_out);
 
+/* Graph mode (one GPU): the first step after enabling captures the step's
+ * launches (stats, apply, result read-back) into one CUDA graph; later steps
+ * replay it with one graph launch, updating only the optimizer constants of
+ * step t.  Host launch overhead per step drops to one graph launch, which is
+ * what bounds small models (LeNet: 61,706 params).  Ignored while per-pass
+ * timing is on, and with world_size > 1 (the NCCL exchange stays eager).
+ * The reference has no equivalent (its step is a CPU call); results are
+ * identical to the eager path. */
+int ody_ctx_set_graph(ody_ctx* ctx, int32_t enable);
+
 /* Quantised weights of one tensor in the reference's byte layout, and its
  * per-tensor scale (1.0 for kinds without one). */
 int ody_get_quant(ody_ctx* ctx, int32_t index, void* dst, size_t bytes, float* tensor_scale);

@@ -82,6 +82,7 @@ _SIGS = {
     "ody_step_wait": (C.c_int, [_p, _p]),
     "ody_ctx_set_timing": (C.c_int, [_p, _i32]),
     "ody_ctx_pass_times": (C.c_int, [_p, _p, _p]),
+    "ody_ctx_set_graph": (C.c_int, [_p, _i32]),
     "ody_ctx_quant_layout": (C.c_int, [_p, _i32, _p, _p, _p]),
     "ody_ctx_gather_quant": (C.c_int, [_p, _p, _p]),
     "ody_get_quant": (C.c_int, [_p, _i32, _p, C.c_size_t, _p]),

@@ -141,6 +141,12 @@ struct ody_ctx {
   std::vector<int64_t> tpending;  // ring slots recorded but not yet read
   int64_t tnext = 0, tsteps = 0;
   double tms[4] = {0, 0, 0, 0};
+  // graph mode: the captured step and its apply-kernel node
+  bool graph_mode = false;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t gexec = nullptr;
+  cudaGraphNode_t gapply = nullptr;
+  OptConsts goc;
 };
 
 static constexpr int kTimingRing = 64;
@@ -378,6 +384,17 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   for (int i = 0; i < nt; i++) numels[i] = c->specs[i].numel;
   ody_plan_shards(numels.data(), nt, world, c->owner.data());
   c->local_of.assign(nt, -1);
+  // chunk length: 8 tiles, halved while the model would give fewer than four
+  // chunks per resident apply CTA (small models spread over more CTAs
+  // instead of walking long chunks tile by tile)
+  int64_t chunk = kChunk;
+  {
+    int64_t nloc = 0;
+    for (int i = 0; i < nt; i++)
+      if (c->owner[i] == rank) nloc += (c->specs[i].numel + kPad - 1) / kPad * kPad;
+    const int64_t full = apply_grid(c->gdt, c->cfg.optimizer, c->cfg.device);
+    while (chunk > kTile && nloc / chunk < 4 * full) chunk /= 2;
+  }
   int64_t off = 0, qoff = 0;
   for (int i = 0; i < nt; i++) {
     if (c->owner[i] != rank) continue;
@@ -391,10 +408,10 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
     c->local_of[i] = (int32_t)c->tdesc.size();
     const int li = (int)c->tdesc.size();
     c->tdesc.push_back(d);
-    for (int64_t s = 0; s < d.npad; s += kChunk) {
+    for (int64_t s = 0; s < d.npad; s += chunk) {
       Chunk ch;
       ch.start = d.off + s;
-      ch.len = (int32_t)((d.npad - s) < kChunk ? (d.npad - s) : kChunk);
+      ch.len = (int32_t)((d.npad - s) < chunk ? (d.npad - s) : chunk);
       ch.tensor = li;
       c->chunks_upd.push_back(ch);
       c->tdesc[li].nchunks++;
@@ -474,11 +491,11 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
                              c->stream));
   ODY_CUDA(dalloc(&c->sync, sizeof(uint32_t) * (nl + 1)));
   ODY_CUDA(cudaMemsetAsync(c->sync, 0, sizeof(uint32_t) * (nl + 1), c->stream));
-  // at least 16 groups of 8 gradients per thread, at most the resident grid
-  // (the fixed-order partial reduction makes the sum depend on the grid, which
-  // is fixed for the context's lifetime)
+  // one unrolled round (4 groups of 8 gradients) per thread, at most the
+  // resident grid (the fixed-order partial reduction makes the sum depend on
+  // the grid, which is fixed for the context's lifetime)
   {
-    const int64_t per_cta = (int64_t)kThreads * 16 * 8;
+    const int64_t per_cta = (int64_t)kThreads * 4 * 8;
     const int64_t want = (c->n_total + per_cta - 1) / per_cta;
     c->grid_stats = (int)std::max<int64_t>(1, std::min<int64_t>(stats_grid(c->cfg.device), want));
   }
@@ -641,6 +658,87 @@ static DecideParams make_decide(const ody_config& cfg) {
   return d;
 }
 
+static void drop_graph(ody_ctx* c) {
+  if (c->gexec) cudaGraphExecDestroy(c->gexec);
+  if (c->graph) cudaGraphDestroy(c->graph);
+  c->gexec = nullptr;
+  c->graph = nullptr;
+  c->gapply = nullptr;
+}
+
+// One step as one graph launch (one GPU).  The first call captures stats ->
+// apply -> result read-back from the context's stream; later calls update the
+// apply node's arguments when the optimizer constants of step t differ and
+// relaunch.
+static int step_graph(ody_ctx* c, const OptConsts& oc, const DecideParams& dp) {
+  const int nl = (int)c->tdesc.size();
+  if (!c->gexec) {
+    ODY_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = launch_stats(c->gdt, c->grad, c->n_total, c->cfg.use_gradient_scaler, c->scaler, c->partials,
+                                 c->grid_stats, c->ticket, 0, c->local_stats, dp, c->dec, c->amax, c->sync, nl,
+                                 c->stream);
+    if (e == cudaSuccess)
+      e = launch_apply(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd, c->d_jobs,
+                       (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout, c->amax,
+                       c->qscale, c->sync, c->dec, c->grid_apply, c->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(c->h_dec, c->dec, sizeof(Decision), cudaMemcpyDeviceToHost, c->stream);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+    if (e == cudaSuccess) e = e2;
+    if (e != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return ctx_fail(c, ODY_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    }
+    c->graph = g;
+    size_t n = 0;
+    ODY_CUDA(cudaGraphGetNodes(g, nullptr, &n));
+    std::vector<cudaGraphNode_t> nodes(n);
+    ODY_CUDA(cudaGraphGetNodes(g, nodes.data(), &n));
+    const void* fn = apply_kernel_fn(c->gdt, c->cfg.optimizer);
+    for (cudaGraphNode_t nd : nodes) {
+      cudaGraphNodeType ty;
+      ODY_CUDA(cudaGraphNodeGetType(nd, &ty));
+      if (ty != cudaGraphNodeTypeKernel) continue;
+      cudaKernelNodeParams kp;
+      ODY_CUDA(cudaGraphKernelNodeGetParams(nd, &kp));
+      if (kp.func == fn) c->gapply = nd;
+    }
+    if (!c->gapply) {
+      drop_graph(c);
+      return ctx_fail(c, ODY_ERR_CUDA, "graph capture: apply kernel node not found");
+    }
+    e = cudaGraphInstantiate(&c->gexec, g, 0);
+    if (e != cudaSuccess) {
+      c->gexec = nullptr;
+      drop_graph(c);
+      return ctx_fail(c, ODY_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    }
+    c->goc = oc;
+  } else if (memcmp(&c->goc, &oc, sizeof(OptConsts)) != 0) {
+    ODY_CUDA(set_apply_node(c->gexec, c->gapply, c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler,
+                            c->d_chunks_upd, c->d_jobs, (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2,
+                            c->grad, c->qout, c->amax, c->qscale, c->sync, c->dec, c->grid_apply));
+    c->goc = oc;
+  }
+  ODY_CUDA(cudaGraphLaunch(c->gexec, c->stream));
+  ODY_CUDA(cudaEventRecord(c->done, c->stream));
+  c->pending = true;
+  return ODY_OK;
+}
+
+extern "C" int ody_ctx_set_graph(ody_ctx* c, int32_t enable) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  if (!enable && c->gexec) {
+    ODY_CUDA(cudaStreamSynchronize(c->stream));
+    drop_graph(c);
+  }
+  c->graph_mode = enable != 0;
+  return ODY_OK;
+}
+
 extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   if (!c) return fail(ODY_ERR_ARG, "null context");
   if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
@@ -651,6 +749,7 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   const OptConsts oc = make_consts(c->cfg, t);
   const DecideParams dp = make_decide(c->cfg);
   const int nl = (int)c->tdesc.size();
+  if (c->graph_mode && c->world == 1 && !c->timing && !c->jobs.empty()) return step_graph(c, oc, dp);
   cudaEvent_t* tev = nullptr;
   if (c->timing) {
     const int64_t slot = c->tnext++;
@@ -996,6 +1095,7 @@ extern "C" void ody_ctx_destroy(ody_ctx* c) {
   for (void* b : bufs)
     if (b) cudaFree(b);
   for (auto& e : c->tev) cudaEventDestroy(e);
+  drop_graph(c);
   if (c->h_dec) cudaFreeHost(c->h_dec);
   if (c->done) cudaEventDestroy(c->done);
   if (c->stream) cudaStreamDestroy(c->stream);

@@ -35,7 +35,7 @@ struct TensorDesc {
 // One entry of the chunk table: a kTile-aligned slice of one tensor.
 struct Chunk {
   int64_t start;   // element offset in the arenas
-  int32_t len;     // elements (multiple of kPad, <= kChunk)
+  int32_t len;     // elements (a multiple of kTile, or the tensor's padded tail; <= kChunk)
   int32_t tensor;  // index into the TensorDesc table
 };
 
@@ -101,6 +101,14 @@ cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, 
                          float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
                          uint32_t* sync, Decision* dec, int grid, cudaStream_t st);
 int apply_grid(int gdt, int opt, int device);
+// the apply kernel instance for (gdt, opt), and an update of its node in an
+// instantiated graph with new launch arguments
+const void* apply_kernel_fn(int gdt, int opt);
+cudaError_t set_apply_node(cudaGraphExec_t exec, cudaGraphNode_t node, int gdt, int opt, const OptConsts& oc,
+                           int use_scaler, const Chunk* chunks, const uint32_t* jobs, int njobs,
+                           const TensorDesc* tensors, float* master, float* s1, float* s2, const void* grad,
+                           uint8_t* qout, uint32_t* amax_slots, float* qscale, uint32_t* sync, Decision* dec,
+                           int grid);
 int stats_grid(int device);
 
 // stateless whole-tensor operations (device pointers)

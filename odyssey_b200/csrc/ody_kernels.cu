@@ -355,6 +355,10 @@ __device__ __forceinline__ void stats_raw8(const Raw8& r, bool use_scaler, const
 
 template <int GDT>
 __global__ void __launch_bounds__(kThreads, 4) stats_kernel(StatsArgs a) {
+  // the apply kernel is launched as this grid's programmatic dependent: its
+  // CTAs may start their prologue now and wait (griddepcontrol.wait) for
+  // this grid's completion and memory flush before reading anything it writes
+  asm volatile("griddepcontrol.launch_dependents;");
   const Divisor dv = make_divisor(unscale_divisor<GDT>(a.scaler->scale));
   constexpr int U = 4;
   double acc[U] = {0.0, 0.0, 0.0, 0.0};
@@ -430,6 +434,7 @@ cudaError_t launch_stats(int gdt, const void* grad, int64_t n, int use_scaler, D
 // decision.
 __global__ void finalize_kernel(const double* gathered, int world, DevScaler* sc, DecideParams dp,
                                 Decision* dec, uint32_t* amax_slots, int ntensors) {
+  asm volatile("griddepcontrol.launch_dependents;");
   for (int j = threadIdx.x; j < ntensors; j += blockDim.x) amax_slots[j] = 0u;
   if (threadIdx.x == 0) {
     double c = 0.0, s = 0.0;
@@ -881,12 +886,15 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ Fp4Thr s_cx[kCxCount];
   __shared__ int s_cx_tensor;
   __shared__ uint32_t s_next;
+  // prologue independent of the preceding stats/finalize grid
+  load_thr_smem(s_mx, s_nv);
+  // wait for the preceding grid (a no-op without a programmatic dependency)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const Decision* dec = a.dec;
   if (dec->skip) return;
   const Divisor dv = make_divisor(unscale_divisor<GDT>(dec->scale_used));
   const bool clipped = dec->clipped != 0;
   const float coef = dec->coef;
-  load_thr_smem(s_mx, s_nv);
   if (threadIdx.x == 0) {
     s_next = atomicAdd(&a.sync[0], 1u);
     s_cx_tensor = -1;
@@ -934,16 +942,56 @@ cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, 
                          uint32_t* sync, Decision* dec, int grid, cudaStream_t st) {
   ApplyArgs a{oc, use_scaler, chunks, jobs, njobs, tensors, master, s1, s2, grad, qout, amax_slots, qscale, sync,
               dec};
-#define ODY_L(G, O)                                                    \
-  if (gdt == G && opt == O) {                                          \
-    apply_kernel<G, O><<<grid, kThreads, 0, st>>>(a);                  \
-    return cudaGetLastError();                                         \
+  // programmatic dependent launch: the CTAs start while the stats (or
+  // finalize) grid is still running and wait on it inside the kernel
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+#define ODY_L(G, O)                                  \
+  if (gdt == G && opt == O) {                        \
+    return cudaLaunchKernelEx(&cfg, apply_kernel<G, O>, a); \
   }
   ODY_L(DT_F32, OPT_SGD) ODY_L(DT_F32, OPT_ADAM) ODY_L(DT_F32, OPT_ADAMW)
   ODY_L(DT_F16, OPT_SGD) ODY_L(DT_F16, OPT_ADAM) ODY_L(DT_F16, OPT_ADAMW)
   ODY_L(DT_BF16, OPT_SGD) ODY_L(DT_BF16, OPT_ADAM) ODY_L(DT_BF16, OPT_ADAMW)
 #undef ODY_L
   return cudaErrorInvalidValue;
+}
+
+const void* apply_kernel_fn(int gdt, int opt) {
+#define ODY_F(G, O) \
+  if (gdt == G && opt == O) return reinterpret_cast<const void*>(&apply_kernel<G, O>);
+  ODY_F(DT_F32, OPT_SGD) ODY_F(DT_F32, OPT_ADAM) ODY_F(DT_F32, OPT_ADAMW)
+  ODY_F(DT_F16, OPT_SGD) ODY_F(DT_F16, OPT_ADAM) ODY_F(DT_F16, OPT_ADAMW)
+  ODY_F(DT_BF16, OPT_SGD) ODY_F(DT_BF16, OPT_ADAM) ODY_F(DT_BF16, OPT_ADAMW)
+#undef ODY_F
+  return nullptr;
+}
+
+cudaError_t set_apply_node(cudaGraphExec_t exec, cudaGraphNode_t node, int gdt, int opt, const OptConsts& oc,
+                           int use_scaler, const Chunk* chunks, const uint32_t* jobs, int njobs,
+                           const TensorDesc* tensors, float* master, float* s1, float* s2, const void* grad,
+                           uint8_t* qout, uint32_t* amax_slots, float* qscale, uint32_t* sync, Decision* dec,
+                           int grid) {
+  ApplyArgs a{oc, use_scaler, chunks, jobs, njobs, tensors, master, s1, s2, grad, qout, amax_slots, qscale, sync,
+              dec};
+  void* args[1] = {&a};
+  cudaKernelNodeParams kp = {};
+  kp.func = const_cast<void*>(apply_kernel_fn(gdt, opt));
+  if (!kp.func) return cudaErrorInvalidValue;
+  kp.gridDim = dim3(grid);
+  kp.blockDim = dim3(kThreads);
+  kp.sharedMemBytes = 0;
+  kp.kernelParams = args;
+  kp.extra = nullptr;
+  return cudaGraphExecKernelNodeSetParams(exec, node, &kp);
 }
 
 // ---------------------------------------------------------------------------

@@ -162,6 +162,11 @@ class MixedPrecisionStep:
     def set_timing(self, enable=True):
         L.check(L.lib().ody_ctx_set_timing(self._ctx, int(bool(enable))), self._ctx)
 
+    def set_graph(self, enable=True):
+        """Replay each step as one CUDA graph launch (one GPU; see
+        ody_ctx_set_graph)."""
+        L.check(L.lib().ody_ctx_set_graph(self._ctx, int(bool(enable))), self._ctx)
+
     def pass_times(self):
         """{'stats','exchange','update','requant'} milliseconds accumulated over
         the timed steps since the last call, and the step count."""

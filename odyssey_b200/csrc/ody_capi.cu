@@ -344,27 +344,39 @@ static cudaError_t dalloc(T** p, size_t bytes) {
   return cudaMalloc((void**)p, bytes < 256 ? 256 : bytes);
 }
 
-// Job list of the apply kernel: every update chunk in arena order; the
-// requant chunks of a per-tensor-scaled tensor become eligible two grid-widths
-// of jobs after that tensor's last update job and are interleaved, up to two
-// per update job, with the following tensors' update jobs; what is left
-// runs at the end.
+// Job list of the apply kernel: every update chunk, tensors in descending
+// size (stable), so that the largest per-tensor-scaled tensors finish their
+// updates first.  The requant chunks of a per-tensor-scaled tensor become
+// eligible two grid-widths of jobs after that tensor's last update job and
+// are interleaved, up to two per update job, with the following tensors'
+// update jobs; what is left runs at the end.  A model of fewer than eight
+// grid-widths of update jobs puts every requant job at the end (measured
+// faster there: its interleaved requant jobs would mostly wait).
 static void build_jobs(ody_ctx* c) {
   c->jobs.clear();
   std::vector<std::pair<size_t, uint32_t>> pending;  // (eligible position, chunk)
   size_t head = 0;
   const size_t W = (size_t)(c->grid_apply > 0 ? c->grid_apply : 1);
+  const size_t nl = c->tdesc.size();
+  const size_t delay = c->chunks_upd.size() >= 8 * W ? 2 * W : SIZE_MAX / 2;
+  std::vector<size_t> first(nl), order(nl);
   size_t ci = 0;
-  for (size_t li = 0; li < c->tdesc.size(); li++) {
+  for (size_t li = 0; li < nl; li++) {
+    first[li] = ci;
+    ci += (size_t)c->tdesc[li].nchunks;
+    order[li] = li;
+  }
+  std::stable_sort(order.begin(), order.end(),
+                     [&](size_t x, size_t y) { return c->tdesc[x].nchunks > c->tdesc[y].nchunks; });
+  for (size_t li : order) {
     const TensorDesc& d = c->tdesc[li];
-    const size_t first = ci;
-    for (int k = 0; k < d.nchunks; k++, ci++) {
-      c->jobs.push_back((uint32_t)ci);
+    for (int k = 0; k < d.nchunks; k++) {
+      c->jobs.push_back((uint32_t)(first[li] + k));
       for (int r = 0; r < 2 && head < pending.size() && pending[head].first <= c->jobs.size(); r++)
         c->jobs.push_back(0x80000000u | pending[head++].second);
     }
     if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR)
-      for (size_t k = first; k < ci; k++) pending.push_back({c->jobs.size() + 2 * W, (uint32_t)k});
+      for (int k = 0; k < d.nchunks; k++) pending.push_back({c->jobs.size() + delay, (uint32_t)(first[li] + k)});
   }
   while (head < pending.size()) c->jobs.push_back(0x80000000u | pending[head++].second);
 }

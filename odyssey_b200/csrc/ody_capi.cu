@@ -925,16 +925,24 @@ extern "C" int ody_ctx_gather_quant(ody_ctx* c, void* dst, float* scales) {
   std::string why;
   NcclApi* api = nccl_api(why);
   if (!api) return ctx_fail(c, ODY_ERR_NCCL, why);
-  // one broadcast per rank of its contiguous slice, grouped: an allgather of
-  // unequal slices
+  // equal slices laid out in rank order (the 1B model on 2/4/8 ranks): one
+  // allgather; otherwise one broadcast per rank of its contiguous slice,
+  // grouped (an allgather of unequal slices)
+  bool eq_codes = true, eq_scales = true;
+  for (int q = 0; q < c->world; q++) {
+    eq_codes = eq_codes && c->rank_qend[q] - c->rank_qbeg[q] == nb && c->rank_qbeg[q] == (int64_t)q * nb;
+    eq_scales = eq_scales && c->rank_tend[q] - c->rank_tbeg[q] == nts && c->rank_tbeg[q] == q * nts;
+  }
   api->groupStart();
+  if (eq_codes && nb > 0) api->allGather(c->qout, dst, (size_t)nb, ncclUint8, c->comm, c->stream);
+  if (eq_scales && nts > 0) api->allGather(c->qscale, scales, (size_t)nts, ncclFloat32, c->comm, c->stream);
   for (int q = 0; q < c->world; q++) {
     const int64_t qb = c->rank_qend[q] - c->rank_qbeg[q];
-    if (qb > 0)
+    if (!eq_codes && qb > 0)
       api->broadcast(q == r ? (const void*)c->qout : nullptr, (uint8_t*)dst + c->rank_qbeg[q], (size_t)qb,
                      ncclUint8, q, c->comm, c->stream);
     const int tq = c->rank_tend[q] - c->rank_tbeg[q];
-    if (tq > 0)
+    if (!eq_scales && tq > 0)
       api->broadcast(q == r ? (const void*)c->qscale : nullptr, scales + c->rank_tbeg[q], (size_t)tq,
                      ncclFloat32, q, c->comm, c->stream);
   }

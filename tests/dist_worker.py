@@ -1,7 +1,9 @@
 """Rank program of the multi-GPU parity test (tests/test_gpu_multi.py).
 
-Launched by torch.distributed.run, one process per GPU.  Every rank
-generates the same seeded model and gradients, builds a ZeRO-1-sharded
+Launched by torch.distributed.run, one process per GPU, on the ResNet-18
+workload (unequal shards) or a 4-tensor flat model (equal shards: the
+gather takes its allgather path).  Every rank generates the same seeded
+model and gradients, builds a ZeRO-1-sharded
 MixedPrecisionStep (whole tensors per rank, NCCL allgather of the
 {nonfinite, sumsq} pair), runs the steps, and saves its owned tensors'
 master weights and codes plus the step results to <out>/rank<r>.npz.
@@ -17,6 +19,7 @@ sys.path.insert(0, ROOT)
 
 def main():
     out, steps, inf_every = sys.argv[1], int(sys.argv[2]), int(sys.argv[3])
+    which = sys.argv[4] if len(sys.argv) > 4 else "resnet18"
     import torch
     import torch.distributed as dist
 
@@ -27,7 +30,7 @@ def main():
     torch.cuda.set_device(local)
     dist.init_process_group("gloo")
     rank = dist.get_rank()
-    wl = W.resnet18()
+    wl = W.resnet18() if which == "resnet18" else W.flat1b(ntensors=4, side=512)
     wl.inf_every = inf_every
     kw = wl.step_kwargs()
     kw["device"] = local

@@ -14,15 +14,22 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def test_two_rank_resnet18_matches_unsharded_oracle(oracle, tmp_path):
+GDT = {"float32": 0, "float16": 1, "bfloat16": 2}
+OPT = {"sgd": 0, "adam": 1, "adamw": 2}
+QK = {"none": 0, "fp16": 1, "bf16": 2, "fp8": 3, "bf8": 4, "fp8_tensor": 5, "mxfp4": 6, "nvfp4": 7,
+      "nvfp4_tensor": 8}
+
+
+@pytest.mark.parametrize("which,port", [("resnet18", 29533), ("flat", 29534)])
+def test_two_rank_matches_unsharded_oracle(oracle, tmp_path, which, port):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     steps, inf_every = 5, 3
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
-           "--master-addr", "127.0.0.1", "--master-port", "29533",
-           os.path.join(ROOT, "tests", "dist_worker.py"), str(tmp_path), str(steps), str(inf_every)]
+           "--master-addr", "127.0.0.1", "--master-port", str(port),
+           os.path.join(ROOT, "tests", "dist_worker.py"), str(tmp_path), str(steps), str(inf_every), which]
     p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert p.returncode == 0, p.stdout[-3000:] + p.stderr[-3000:]
     ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(2)]
@@ -30,10 +37,17 @@ def test_two_rank_resnet18_matches_unsharded_oracle(oracle, tmp_path):
     np.testing.assert_array_equal(ranks[0]["results"], ranks[1]["results"])
 
     from odyssey_b200 import workloads as W
-    wl = W.resnet18()
+    wl = W.resnet18() if which == "resnet18" else W.flat1b(ntensors=4, side=512)
     wl.inf_every = inf_every
-    specs = [{"numel": n, "grad_dtype": oracle.BF16, "quant": oracle.Q_FP8_E4M3_TENSOR} for n in wl.numels]
-    model = oracle.Model(specs, oracle.ADAMW, 1e-3, weight_decay=0.01, scaler_kwargs={"initial_scale": 65536.0})
+    kw = wl.step_kwargs()
+    hy = wl.hyper
+    specs = [{"numel": n, "grad_dtype": GDT[wl.grad_dtype], "quant": QK[wl.quant]} for n in wl.numels]
+    sk = {k: kw[k] for k in ("initial_scale", "growth_factor", "backoff_factor", "growth_interval", "min_scale",
+                             "max_scale") if k in kw}
+    model = oracle.Model(specs, OPT[wl.optimizer], hy["learning_rate"], beta1=hy.get("beta1", 0.9),
+                         beta2=hy.get("beta2", 0.999), epsilon=hy.get("epsilon", 1e-8),
+                         weight_decay=hy.get("weight_decay", 0.0), clip_enabled=wl.clip is not None,
+                         max_norm=wl.clip or 1.0, scaler_kwargs=sk)
     for i, m in enumerate(wl.master(0)):
         model.master[i][:] = m
     t = 1

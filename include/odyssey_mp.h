@@ -63,6 +63,9 @@ extern "C" {
 #define ODY_BUF_STATE1 1 /* SGD velocity / Adam(W) first moment m (float32) */
 #define ODY_BUF_STATE2 2 /* Adam(W) second moment v (float32) */
 #define ODY_BUF_GRAD 3   /* scaled gradients, in the context's gradient dtype */
+/* with data-parallel gradients attached: tensor index's slice of this rank's
+ * full-model gradient buffer (any tensor, owned or not) */
+#define ODY_BUF_DP_GRAD 4
 
 /*
  * Step configuration.  Field names follow the reference: optimizer hyper-
@@ -185,6 +188,20 @@ int ody_ctx_pass_times(ody_ctx* ctx, double* ms_out, int64_t* steps_out);
  * The reference has no equivalent (its step is a CPU call); results are
  * identical to the eager path. */
 int ody_ctx_set_graph(ody_ctx* ctx, int32_t enable);
+
+/* Data-parallel gradients (collective over the context's ranks, at most 8).
+ * Allocates this rank's full-model gradient buffer (every tensor, in the
+ * context's gradient dtype, padded like the arenas; filled through
+ * ODY_BUF_DP_GRAD) and maps every other rank's buffer here through CUDA IPC
+ * (peer access over NVLink).  From then on each step starts with the
+ * gradient reduce-scatter fused into pass 1: this rank's shard is summed
+ * over all ranks in float32 in rank order, rounded once to the gradient
+ * dtype, written to the shard's gradient arena and its statistics taken in
+ * the same kernel.  The sum (not the mean) is the gradient; fold 1/N into
+ * the loss scale for a mean.  The reference is single-process, so this
+ * extends its step to data-parallel training
+ * (examples/mixed_precision_training.mojo:132-216 with per-rank backward). */
+int ody_ctx_dp_attach(ody_ctx* ctx);
 
 /* Quantised weights of one tensor in the reference's byte layout, and its
  * per-tensor scale (1.0 for kinds without one). */

@@ -17,7 +17,7 @@ F32, F16, BF16 = 0, 1, 2
 SGD, ADAM, ADAMW = 0, 1, 2
 (Q_NONE, Q_FP16, Q_BF16, Q_FP8_E4M3, Q_FP8_E5M2, Q_FP8_E4M3_TENSOR, Q_MXFP4, Q_NVFP4,
  Q_NVFP4_TENSOR) = range(9)
-BUF_MASTER, BUF_STATE1, BUF_STATE2, BUF_GRAD = range(4)
+BUF_MASTER, BUF_STATE1, BUF_STATE2, BUF_GRAD, BUF_DP_GRAD = range(5)
 
 QUANT_NAMES = {
     "none": Q_NONE, "fp16": Q_FP16, "bf16": Q_BF16, "fp8": Q_FP8_E4M3, "fp8_e4m3": Q_FP8_E4M3,
@@ -83,6 +83,7 @@ _SIGS = {
     "ody_ctx_set_timing": (C.c_int, [_p, _i32]),
     "ody_ctx_pass_times": (C.c_int, [_p, _p, _p]),
     "ody_ctx_set_graph": (C.c_int, [_p, _i32]),
+    "ody_ctx_dp_attach": (C.c_int, [_p]),
     "ody_ctx_quant_layout": (C.c_int, [_p, _i32, _p, _p, _p]),
     "ody_ctx_gather_quant": (C.c_int, [_p, _p, _p]),
     "ody_get_quant": (C.c_int, [_p, _i32, _p, C.c_size_t, _p]),

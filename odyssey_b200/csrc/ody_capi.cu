@@ -141,6 +141,16 @@ struct ody_ctx {
   std::vector<int64_t> tpending;  // ring slots recorded but not yet read
   int64_t tnext = 0, tsteps = 0;
   double tms[4] = {0, 0, 0, 0};
+  // data-parallel gradients (ody_ctx_dp_attach): the full-model gradient
+  // buffer, each tensor's offset in it, the ranks' buffers as mapped here
+  bool dp_on = false;
+  void* dp_buf = nullptr;
+  int64_t dp_total = 0, dp_shard_off = 0;
+  std::vector<int64_t> dp_off;
+  std::vector<void*> dp_opened;  // peers' buffers opened through CUDA IPC
+  const void** d_peers = nullptr;
+  double* bar_send = nullptr;
+  double* bar_recv = nullptr;
   // graph mode: the captured step and its apply-kernel node
   bool graph_mode = false;
   cudaGraph_t graph = nullptr;
@@ -562,6 +572,12 @@ static int locate(ody_ctx* c, int32_t which, int32_t i, void** base, size_t* byt
   if (!c) return fail(ODY_ERR_ARG, "null context");
   if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
   if (i < 0 || i >= (int)c->specs.size()) return ctx_fail(c, ODY_ERR_ARG, "tensor index out of range");
+  if (which == ODY_BUF_DP_GRAD) {
+    if (!c->dp_on) return ctx_fail(c, ODY_ERR_STATE, "data-parallel gradients not attached (ody_ctx_dp_attach)");
+    *base = (uint8_t*)c->dp_buf + (size_t)c->dp_off[i] * dtype_size(c->gdt);
+    *bytes = (size_t)c->specs[i].numel * dtype_size(c->gdt);
+    return ODY_OK;
+  }
   const int li = c->local_of[i];
   if (li < 0)
     return ctx_fail(c, ODY_ERR_ARG, "tensor " + std::to_string(i) + " is owned by rank " +
@@ -670,6 +686,19 @@ static DecideParams make_decide(const ody_config& cfg) {
   return d;
 }
 
+// pass 1: the stats kernel over the local gradients, or with data-parallel
+// gradients attached the fused reduce-scatter + stats kernel
+static cudaError_t launch_pass1(ody_ctx* c, const DecideParams& dp, int world_mode) {
+  const int nl = (int)c->tdesc.size();
+  if (c->dp_on)
+    return launch_rs_stats(c->gdt, c->d_peers, c->world, c->dp_shard_off, c->grad, c->n_total,
+                           c->cfg.use_gradient_scaler, c->scaler, c->partials, c->grid_stats, c->ticket, world_mode,
+                           c->local_stats, dp, c->dec, c->amax, c->sync, nl, c->stream);
+  return launch_stats(c->gdt, c->grad, c->n_total, c->cfg.use_gradient_scaler, c->scaler, c->partials,
+                      c->grid_stats, c->ticket, world_mode, c->local_stats, dp, c->dec, c->amax, c->sync, nl,
+                      c->stream);
+}
+
 static void drop_graph(ody_ctx* c) {
   if (c->gexec) cudaGraphExecDestroy(c->gexec);
   if (c->graph) cudaGraphDestroy(c->graph);
@@ -686,9 +715,7 @@ static int step_graph(ody_ctx* c, const OptConsts& oc, const DecideParams& dp) {
   const int nl = (int)c->tdesc.size();
   if (!c->gexec) {
     ODY_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t e = launch_stats(c->gdt, c->grad, c->n_total, c->cfg.use_gradient_scaler, c->scaler, c->partials,
-                                 c->grid_stats, c->ticket, 0, c->local_stats, dp, c->dec, c->amax, c->sync, nl,
-                                 c->stream);
+    cudaError_t e = launch_pass1(c, dp, 0);
     if (e == cudaSuccess)
       e = launch_apply(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd, c->d_jobs,
                        (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout, c->amax,
@@ -739,6 +766,79 @@ static int step_graph(ody_ctx* c, const OptConsts& oc, const DecideParams& dp) {
   return ODY_OK;
 }
 
+extern "C" int ody_ctx_dp_attach(ody_ctx* c) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  if (c->broken) return ctx_fail(c, ODY_ERR_STATE, "context unusable after a communicator failure");
+  if (c->dp_on) return ctx_fail(c, ODY_ERR_STATE, "data-parallel gradients already attached");
+  if (c->world > 8) return ctx_fail(c, ODY_ERR_ARG, "data-parallel gradients support at most 8 ranks");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  const int nt = (int)c->specs.size();
+  const size_t esz = dtype_size(c->gdt);
+  c->dp_off.assign(nt, 0);
+  int64_t g = 0;
+  for (int i = 0; i < nt; i++) {
+    c->dp_off[i] = g;
+    g += (c->specs[i].numel + kPad - 1) / kPad * kPad;
+  }
+  c->dp_total = g;
+  const int r = c->rank;
+  c->dp_shard_off = c->rank_tend[r] > c->rank_tbeg[r] ? c->dp_off[c->rank_tbeg[r]] : 0;
+  for (int i = 0; i < nt; i++)
+    if (c->local_of[i] >= 0 && c->dp_off[i] - c->dp_shard_off != c->tdesc[c->local_of[i]].off)
+      return ctx_fail(c, ODY_ERR_STATE, "shard is not contiguous in the global layout");
+  ODY_CUDA(dalloc(&c->dp_buf, (size_t)g * esz));
+  ODY_CUDA(cudaMemsetAsync(c->dp_buf, 0, (size_t)g * esz, c->stream));
+  std::vector<const void*> peers(c->world, nullptr);
+  peers[r] = c->dp_buf;
+  if (c->world > 1) {
+    std::string why;
+    NcclApi* api = nccl_api(why);
+    if (!api) return ctx_fail(c, ODY_ERR_NCCL, why);
+    cudaIpcMemHandle_t h;
+    ODY_CUDA(cudaIpcGetMemHandle(&h, c->dp_buf));
+    uint8_t* dh = nullptr;
+    ODY_CUDA(dalloc(&dh, sizeof(h) * (c->world + 1)));
+    ODY_CUDA(cudaMemcpyAsync(dh, &h, sizeof(h), cudaMemcpyHostToDevice, c->stream));
+    ncclResult_t nr = api->allGather(dh, dh + sizeof(h), sizeof(h), ncclUint8, c->comm, c->stream);
+    if (nr != ncclSuccess && nr != ncclInProgress) {
+      cudaFree(dh);
+      return ctx_fail(c, ODY_ERR_NCCL, std::string("ncclAllGather (IPC handles): ") + api->getErrorString(nr));
+    }
+    int rc = wait_nccl(c, api, "ncclAllGather (IPC handles)");
+    if (rc != ODY_OK) {
+      cudaFree(dh);
+      return rc;
+    }
+    std::vector<cudaIpcMemHandle_t> all(c->world);
+    cudaError_t e = cudaMemcpyAsync(all.data(), dh + sizeof(h), sizeof(h) * c->world, cudaMemcpyDeviceToHost,
+                                    c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(dh);
+    if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("IPC handles: ") + cudaGetErrorString(e));
+    for (int q = 0; q < c->world; q++) {
+      if (q == r) continue;
+      void* p = nullptr;
+      e = cudaIpcOpenMemHandle(&p, all[q], cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess)
+        return ctx_fail(c, ODY_ERR_CUDA, "opening rank " + std::to_string(q) +
+                                             "'s gradient buffer (peer access over NVLink required): " +
+                                             cudaGetErrorString(e));
+      c->dp_opened.push_back(p);
+      peers[q] = p;
+    }
+    ODY_CUDA(dalloc(&c->bar_send, sizeof(double)));
+    ODY_CUDA(dalloc(&c->bar_recv, sizeof(double) * c->world));
+    ODY_CUDA(cudaMemsetAsync(c->bar_send, 0, sizeof(double), c->stream));
+  }
+  ODY_CUDA(dalloc(&c->d_peers, sizeof(void*) * c->world));
+  ODY_CUDA(cudaMemcpyAsync(c->d_peers, peers.data(), sizeof(void*) * c->world, cudaMemcpyHostToDevice, c->stream));
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  if (c->gexec) drop_graph(c);  // the captured pass 1 changes
+  c->dp_on = true;
+  return ODY_OK;
+}
+
 extern "C" int ody_ctx_set_graph(ody_ctx* c, int32_t enable) {
   if (!c) return fail(ODY_ERR_ARG, "null context");
   if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
@@ -773,9 +873,21 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
     tev = &c->tev[(size_t)(slot % kTimingRing) * 5];
     ODY_CUDA(cudaEventRecord(tev[0], c->stream));
   }
-  cudaError_t e = launch_stats(c->gdt, c->grad, c->n_total, c->cfg.use_gradient_scaler, c->scaler, c->partials,
-                               c->grid_stats, c->ticket, c->world > 1 ? 1 : 0, c->local_stats, dp, c->dec,
-                               c->amax, c->sync, nl, c->stream);
+  cudaError_t e;
+  if (c->dp_on && c->world > 1) {
+    // every rank's gradients are written before any rank reads them: an
+    // 8-byte allgather orders this rank's kernel after every rank's
+    // preceding work on its stream
+    std::string why;
+    NcclApi* api = nccl_api(why);
+    if (!api) return ctx_fail(c, ODY_ERR_NCCL, why);
+    ncclResult_t r = api->allGather(c->bar_send, c->bar_recv, 1, ncclFloat64, c->comm, c->stream);
+    if (r != ncclSuccess && r != ncclInProgress)
+      return ctx_fail(c, ODY_ERR_NCCL, std::string("ncclAllGather (gradient barrier): ") + api->getErrorString(r));
+    int rc = wait_nccl(c, api, "ncclAllGather (gradient barrier)");
+    if (rc != ODY_OK) return rc;
+  }
+  e = launch_pass1(c, dp, c->world > 1 ? 1 : 0);
   if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("stats kernel: ") + cudaGetErrorString(e));
   if (tev) ODY_CUDA(cudaEventRecord(tev[1], c->stream));
   if (c->world > 1) {
@@ -1116,6 +1228,10 @@ extern "C" void ody_ctx_destroy(ody_ctx* c) {
     if (b) cudaFree(b);
   for (auto& e : c->tev) cudaEventDestroy(e);
   drop_graph(c);
+  for (void* p : c->dp_opened) cudaIpcCloseMemHandle(p);
+  void* dpb[] = {c->dp_buf, (void*)c->d_peers, c->bar_send, c->bar_recv};
+  for (void* b : dpb)
+    if (b) cudaFree(b);
   if (c->h_dec) cudaFreeHost(c->h_dec);
   if (c->done) cudaEventDestroy(c->done);
   if (c->stream) cudaStreamDestroy(c->stream);

@@ -100,6 +100,12 @@ cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, 
                          const uint32_t* jobs, int njobs, const TensorDesc* tensors, float* master, float* s1,
                          float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
                          uint32_t* sync, Decision* dec, int grid, cudaStream_t st);
+// pass 1 with the data-parallel gradient reduce-scatter fused in (up to 8
+// ranks; peers: device array of the ranks' full gradient buffers)
+cudaError_t launch_rs_stats(int gdt, const void* const* peers, int world, int64_t shard_off, void* grad, int64_t n,
+                            int use_scaler, DevScaler* scaler, StatsPartial* partials, int grid, unsigned* ticket,
+                            int world_mode, double* local_stats, const DecideParams& dp, Decision* dec,
+                            uint32_t* amax_slots, uint32_t* sync, int ntensors, cudaStream_t st);
 int apply_grid(int gdt, int opt, int device);
 // the apply kernel instance for (gdt, opt), and an update of its node in an
 // instantiated graph with new launch arguments

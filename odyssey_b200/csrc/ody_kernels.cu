@@ -353,6 +353,8 @@ __device__ __forceinline__ void stats_raw8(const Raw8& r, bool use_scaler, const
   acc += (double)s;
 }
 
+__device__ __forceinline__ void stats_finish(const StatsArgs& a, double acc_all, long long bad);
+
 template <int GDT>
 __global__ void __launch_bounds__(kThreads, 4) stats_kernel(StatsArgs a) {
   // the apply kernel is launched as this grid's programmatic dependent: its
@@ -374,7 +376,13 @@ __global__ void __launch_bounds__(kThreads, 4) stats_kernel(StatsArgs a) {
     for (int u = 0; u < U; u++) stats_raw8<GDT>(r[u], a.use_scaler, dv, acc[u], bad);
   }
   for (; i < ngroups; i += stride) stats_raw8<GDT>(ld_raw8<GDT>(a.grad, i * 8), a.use_scaler, dv, acc[0], bad);
-  double acc_all = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  stats_finish(a, (acc[0] + acc[1]) + (acc[2] + acc[3]), bad);
+}
+
+// The CTA's partial, and in the last CTA to finish the fixed-order reduction
+// of all partials and the step decision (or the local pair for the
+// allgather).
+__device__ __forceinline__ void stats_finish(const StatsArgs& a, double acc_all, long long bad) {
   block_sum2(acc_all, bad);
   __shared__ bool last;
   if (threadIdx.x == 0) {
@@ -426,6 +434,120 @@ cudaError_t launch_stats(int gdt, const void* grad, int64_t n, int use_scaler, D
     stats_kernel<DT_F16><<<grid, kThreads, 0, st>>>(a);
   else
     stats_kernel<DT_BF16><<<grid, kThreads, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Data-parallel gradients: reduce-scatter fused with pass 1.  Every rank
+// holds a full-model gradient buffer (its own backward's output) in the
+// flat, 64-element-padded global layout; peers[q] is rank q's buffer mapped
+// into this process (CUDA IPC; this rank's own at q = rank).  This rank's
+// shard is the contiguous range [shard_off, shard_off + n) of that layout,
+// laid out exactly like its local gradient arena.  Each group of 8
+// gradients is read from every rank over NVLink (peer loads), summed in
+// float32 in rank order (one rounding per add, so the result is the same on
+// every run and every rank count split), rounded once to the gradient dtype
+// and stored into the local arena, and its unscale / finiteness / square-sum
+// statistics are taken on the stored value, as pass 1 would.  The ranks'
+// readiness is ordered by an NCCL collective before this kernel, and no
+// rank overwrites its buffer before the stats allgather after it, which
+// needs every rank's kernel finished.
+// ---------------------------------------------------------------------------
+struct RsArgs {
+  const void* const* peers;
+  int world;
+  int64_t shard_off;
+  void* out;
+};
+
+template <int GDT>
+__device__ __forceinline__ Raw8 pack8(const float v[8]) {
+  Raw8 r;
+  if (GDT == DT_F32) {
+    r.a = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]), __float_as_uint(v[3]));
+    r.b = make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]), __float_as_uint(v[7]));
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t lo = GDT == DT_BF16 ? f32_to_bf16_bits(v[2 * k]) : f32_to_f16_bits(v[2 * k]);
+      const uint32_t hi = GDT == DT_BF16 ? f32_to_bf16_bits(v[2 * k + 1]) : f32_to_f16_bits(v[2 * k + 1]);
+      w[k] = lo | (hi << 16);
+    }
+    r.a = make_uint4(w[0], w[1], w[2], w[3]);
+    r.b = make_uint4(0, 0, 0, 0);
+  }
+  return r;
+}
+
+template <int GDT>
+__device__ __forceinline__ void st_raw8(void* g, int64_t e0, const Raw8& r) {
+  if (GDT == DT_F32) {
+    uint4* p = reinterpret_cast<uint4*>(reinterpret_cast<float*>(g) + e0);
+    p[0] = r.a;
+    p[1] = r.b;
+  } else {
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(g) + e0) = r.a;
+  }
+}
+
+template <int GDT>
+__device__ __forceinline__ Raw8 reduce8(const RsArgs& rs, int64_t e0) {
+  // ranks in batches of four: the batch's loads are in flight together, the
+  // adds stay in rank order
+  constexpr int kBatch = 4;
+  float acc[8];
+#pragma unroll
+  for (int k = 0; k < 8; k++) acc[k] = 0.0f;
+#pragma unroll
+  for (int q0 = 0; q0 < 8; q0 += kBatch) {
+    if (q0 < rs.world) {
+      Raw8 raw[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; j++)
+        if (q0 + j < rs.world) raw[j] = ld_raw8<GDT>(rs.peers[q0 + j], rs.shard_off + e0);
+#pragma unroll
+      for (int j = 0; j < kBatch; j++) {
+        if (q0 + j < rs.world) {
+          float v[8];
+          unpack8<GDT>(raw[j], v);
+#pragma unroll
+          for (int k = 0; k < 8; k++) acc[k] = (q0 + j == 0) ? v[k] : __fadd_rn(acc[k], v[k]);
+        }
+      }
+    }
+  }
+  const Raw8 r = pack8<GDT>(acc);
+  st_raw8<GDT>(rs.out, e0, r);
+  return r;
+}
+
+template <int GDT>
+__global__ void __launch_bounds__(kThreads, 4) rs_stats_kernel(StatsArgs a, RsArgs rs) {
+  const Divisor dv = make_divisor(unscale_divisor<GDT>(a.scaler->scale));
+  double acc = 0.0;
+  long long bad = 0;
+  const int64_t ngroups = a.n / 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ngroups; i += stride)
+    stats_raw8<GDT>(reduce8<GDT>(rs, i * 8), a.use_scaler, dv, acc, bad);
+  stats_finish(a, acc, bad);
+}
+
+cudaError_t launch_rs_stats(int gdt, const void* const* peers, int world, int64_t shard_off, void* grad, int64_t n,
+                            int use_scaler, DevScaler* scaler, StatsPartial* partials, int grid, unsigned* ticket,
+                            int world_mode, double* local_stats, const DecideParams& dp, Decision* dec,
+                            uint32_t* amax_slots, uint32_t* sync, int ntensors, cudaStream_t st) {
+  if (world < 1 || world > 8) return cudaErrorInvalidValue;
+  StatsArgs a{grad, n, use_scaler, scaler, partials, ticket, world_mode, local_stats, dp, dec,
+              amax_slots, sync, ntensors};
+  RsArgs rs{peers, world, shard_off, grad};
+  if (gdt == DT_F32)
+    rs_stats_kernel<DT_F32><<<grid, kThreads, 0, st>>>(a, rs);
+  else if (gdt == DT_F16)
+    rs_stats_kernel<DT_F16><<<grid, kThreads, 0, st>>>(a, rs);
+  else
+    rs_stats_kernel<DT_BF16><<<grid, kThreads, 0, st>>>(a, rs);
   return cudaGetLastError();
 }
 

@@ -87,7 +87,9 @@ class MixedPrecisionStep:
 
     # ---- buffers ----
     def _esz(self, which):
-        return 4 if which != L.BUF_GRAD else (4 if self.grad_dtype == L.F32 else 2)
+        if which not in (L.BUF_GRAD, L.BUF_DP_GRAD):
+            return 4
+        return 4 if self.grad_dtype == L.F32 else 2
 
     def upload(self, which, index, array, sync=True):
         a = L.contiguous(array)
@@ -161,6 +163,17 @@ class MixedPrecisionStep:
 
     def set_timing(self, enable=True):
         L.check(L.lib().ody_ctx_set_timing(self._ctx, int(bool(enable))), self._ctx)
+
+    def dp_attach(self):
+        """Data-parallel gradients (collective; see ody_ctx_dp_attach): every
+        rank fills its full-model gradients with set_dp_grad, and each step
+        reduce-scatters them (rank-order float32 sum) fused with pass 1."""
+        L.check(L.lib().ody_ctx_dp_attach(self._ctx), self._ctx)
+
+    def set_dp_grad(self, i, a, sync=True):
+        """This rank's gradient of tensor i (any tensor) in the data-parallel
+        buffer."""
+        return self.upload(L.BUF_DP_GRAD, i, a, sync)
 
     def set_graph(self, enable=True):
         """Replay each step as one CUDA graph launch (one GPU; see

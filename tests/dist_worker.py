@@ -2,7 +2,8 @@
 
 Launched by torch.distributed.run, one process per GPU, on the ResNet-18
 workload (unequal shards) or a 4-tensor flat model (equal shards: the
-gather takes its allgather path).  Every rank generates the same seeded
+gather takes its allgather path); with a "dp_" prefix every rank feeds its
+own full-model gradients and the step reduce-scatters them.  Every rank generates the same seeded
 model and gradients, builds a ZeRO-1-sharded
 MixedPrecisionStep (whole tensors per rank, NCCL allgather of the
 {nonfinite, sumsq} pair), runs the steps, and saves its owned tensors'
@@ -30,20 +31,29 @@ def main():
     torch.cuda.set_device(local)
     dist.init_process_group("gloo")
     rank = dist.get_rank()
-    wl = W.resnet18() if which == "resnet18" else W.flat1b(ntensors=4, side=512)
+    dp = which.startswith("dp_")
+    base = which[3:] if dp else which
+    wl = W.resnet18() if base == "resnet18" else W.flat1b(ntensors=4, side=512)
     wl.inf_every = inf_every
     kw = wl.step_kwargs()
     kw["device"] = local
     ctx = MixedPrecisionStep.from_process_group(wl.numels, **kw)
+    if dp:
+        ctx.dp_attach()
     master = wl.master(0)
     for i in ctx.owned:
         ctx.set_master(i, master[i])
     res = []
     t = 1
     for s in range(steps):
-        grads = wl.grads(s, 1)
-        for i in ctx.owned:
-            ctx.set_grad(i, grads[i])
+        if dp:
+            # data-parallel: every rank's own full-model gradients
+            for i, g in enumerate(wl.grads(s, 1 + rank)):
+                ctx.set_dp_grad(i, g)
+        else:
+            grads = wl.grads(s, 1)
+            for i in ctx.owned:
+                ctx.set_grad(i, grads[i])
         r = ctx.step(t)
         res.append([r["skipped"], r["nonfinite_count"], r["sumsq"], r["grad_norm"], r["scale_next"]])
         if not r["skipped"]:

@@ -314,3 +314,36 @@ def test_graph_mode_matches_eager(oracle, which):
     b.set_graph(False)
     a.close()
     b.close()
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_dp_single_rank_matches_plain(oracle, graph):
+    """Data-parallel gradients on one rank: the fused reduce-scatter + pass 1
+    reads the full-model buffer and must give exactly the plain step (a sum
+    over one rank is the gradient itself)."""
+    from odyssey_b200 import MixedPrecisionStep
+    wl = W.resnet18()
+    wl.inf_every = 3
+    kw = wl.step_kwargs()
+    a = MixedPrecisionStep(wl.numels, **kw)
+    b = MixedPrecisionStep(wl.numels, **kw)
+    b.set_graph(graph)
+    b.dp_attach()
+    for i, m in enumerate(wl.master(0)):
+        a.set_master(i, m)
+        b.set_master(i, m)
+    t = 1
+    for s in range(5):
+        for i, g in enumerate(wl.grads(s)):
+            a.set_grad(i, g)
+            b.set_dp_grad(i, g)
+        ra, rb = a.step(t), b.step(t)
+        assert ra == rb, s
+        if not ra["skipped"]:
+            t += 1
+    for i in range(len(wl.numels)):
+        np.testing.assert_array_equal(a.master(i), b.master(i))
+        np.testing.assert_array_equal(a.download(3, i), b.download(3, i))  # reduced gradients
+        np.testing.assert_array_equal(a.get_quant(i).data, b.get_quant(i).data)
+    a.close()
+    b.close()

@@ -20,7 +20,43 @@ QK = {"none": 0, "fp16": 1, "bf16": 2, "fp8": 3, "bf8": 4, "fp8_tensor": 5, "mxf
       "nvfp4_tensor": 8}
 
 
-@pytest.mark.parametrize("which,port", [("resnet18", 29533), ("flat", 29534)])
+def dp_reduce(wl, step, world):
+    """The data-parallel gradient: the ranks' gradients upcast to float32,
+    summed in rank order (one rounding per add), rounded to the gradient
+    dtype."""
+    per = [wl.grads(step, 1 + r) for r in range(world)]
+    out = []
+    for i in range(len(wl.numels)):
+        acc = None
+        for r in range(world):
+            g = per[r][i]
+            x = W_bf16_to_f32(g) if wl.grad_dtype == "bfloat16" else g.astype(np.float32)
+            acc = x.copy() if acc is None else (acc + x).astype(np.float32)
+        if wl.grad_dtype == "bfloat16":
+            out.append(W_f32_to_bf16(acc))
+        elif wl.grad_dtype == "float16":
+            out.append(acc.astype(np.float16))
+        else:
+            out.append(acc)
+    return out
+
+
+def W_bf16_to_f32(h):
+    from odyssey_b200 import workloads as W
+    return W.bf16_bits_to_f32(h)
+
+
+def W_f32_to_bf16(x):
+    """float32 -> bfloat16 bits, round to nearest even, NaN kept NaN."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    r = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
+    nan = np.isnan(x)
+    r[nan] = ((u[nan] >> np.uint32(16)) | np.uint32(0x40)).astype(np.uint16)
+    return r
+
+
+@pytest.mark.parametrize("which,port", [("resnet18", 29533), ("flat", 29534), ("dp_resnet18", 29535),
+                                        ("dp_flat", 29536)])
 def test_two_rank_matches_unsharded_oracle(oracle, tmp_path, which, port):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < 2:
@@ -37,7 +73,9 @@ def test_two_rank_matches_unsharded_oracle(oracle, tmp_path, which, port):
     np.testing.assert_array_equal(ranks[0]["results"], ranks[1]["results"])
 
     from odyssey_b200 import workloads as W
-    wl = W.resnet18() if which == "resnet18" else W.flat1b(ntensors=4, side=512)
+    dp = which.startswith("dp_")
+    base = which[3:] if dp else which
+    wl = W.resnet18() if base == "resnet18" else W.flat1b(ntensors=4, side=512)
     wl.inf_every = inf_every
     kw = wl.step_kwargs()
     hy = wl.hyper
@@ -52,7 +90,7 @@ def test_two_rank_matches_unsharded_oracle(oracle, tmp_path, which, port):
         model.master[i][:] = m
     t = 1
     for s in range(steps):
-        r = model.step(wl.grads(s, 1), t)
+        r = model.step(dp_reduce(wl, s, 2) if dp else wl.grads(s, 1), t)
         got = ranks[0]["results"][s]
         assert got[0] == r.skipped and got[1] == r.nonfinite and got[4] == r.scale_next
         if np.isfinite(r.sumsq):

@@ -242,6 +242,10 @@ def main():
                     help="untimed steps run for about this long while the clock sampler starts (0 for ncu captures)")
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
                     help="replay each step as one CUDA graph launch (auto: on with one GPU)")
+    ap.add_argument("--dp", default="none", choices=["none", "fused", "nccl"],
+                    help="data-parallel gradients: every rank holds full-model gradients and each step first "
+                         "reduce-scatters them, fused with pass 1 (fused) or by ncclReduceScatter (nccl, "
+                         "for comparison); none = gradients already reduced (the headline)")
     ap.add_argument("--workload", default="flat1b", choices=["flat1b", "resnet18", "lenet"],
                     help="flat1b = the headline 1B model; resnet18 / lenet = secondary lines")
     args = ap.parse_args()
@@ -295,6 +299,49 @@ def main():
         del m, g
     torch.cuda.synchronize()
 
+    # data-parallel gradients: each rank's own full-model gradients (seeded
+    # per rank), reduce-scattered inside the timed step
+    rs_step = None
+    if args.dp != "none":
+        if args.dp == "fused":
+            ctx.dp_attach()
+        full = torch.empty(sum((n + 63) // 64 * 64 for n in wl.numels), dtype=gdt, device="cuda")
+        off = 0
+        for i, n in enumerate(wl.numels):
+            gen.manual_seed(5000 + i + 100000 * rank)
+            g = (torch.randn(n, device="cuda", generator=gen) * (wl.grad_std * wl.loss_scale)).to(gdt)
+            if args.dp == "fused":
+                ctx.upload(L.BUF_DP_GRAD, i, g)
+            else:
+                full[off:off + n].copy_(g)
+            off += (n + 63) // 64 * 64
+            del g
+        if args.dp == "fused":
+            del full
+        else:
+            # ncclReduceScatter of the full buffer straight into this rank's
+            # gradient arena (equal shards only), ordered on the step's stream
+            if any(wl.numels[i] % 64 for i in range(len(wl.numels))) or len(wl.numels) % world:
+                raise SystemExit("--dp nccl needs equal, unpadded shards")
+            nccl_pg = dist.new_group(backend="nccl") if world > 1 else None
+
+            class _Arena:
+                def __init__(self, ptr, n):
+                    self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i2", "data": (ptr, False),
+                                                     "version": 3}
+
+            arena = torch.as_tensor(_Arena(ctx.device_ptr(L.BUF_GRAD, owned[0]), nloc), device="cuda")
+            arena = arena.view(gdt)
+            rs_stream = torch.cuda.ExternalStream(ctx.stream_handle())
+
+            def rs_step():
+                with torch.cuda.stream(rs_stream):
+                    if world > 1:
+                        dist.reduce_scatter_tensor(arena, full, group=nccl_pg)
+                    else:
+                        arena.copy_(full)
+        torch.cuda.synchronize()
+
     def barrier():
         if world > 1:
             dist.barrier()
@@ -303,6 +350,8 @@ def main():
     t = 1
     w0 = time.perf_counter()
     for _ in range(args.warmup):
+        if rs_step:
+            rs_step()
         ctx.step(t)
         t += 1
     # every rank must run the same number of steps (each step has a
@@ -322,6 +371,8 @@ def main():
         ctx.set_timing(True)
         ctx.pass_times()
         for _ in range(n_clock_warm):
+            if rs_step:
+                rs_step()
             ctx.step_async(t)
             t += 1
             ctx.wait()
@@ -330,6 +381,8 @@ def main():
         barrier()
         ev0.record(stream)
         for _ in range(args.steps):
+            if rs_step:
+                rs_step()
             ctx.step_async(t)
             t += 1
         ev1.record(stream)
@@ -346,33 +399,43 @@ def main():
     value = TOTAL / (ms_step * 1e-3)
 
     # ---- end to end through the C ABI: pinned host gradients -> step -> result
-    pinned = [torch.empty(wl.numels[i] * gsz, dtype=torch.uint8, pin_memory=True) for i in owned]
-    for k, i in enumerate(owned):
-        pinned[k].copy_(torch.from_numpy(ctx.download(L.BUF_GRAD, i).view(np.uint8)))
-    lib = L.lib()
-    for _ in range(1):
-        for k, i in enumerate(owned):
-            L.check(lib.ody_upload_async(ctx._ctx, L.BUF_GRAD, i, pinned[k].data_ptr(), pinned[k].numel()), ctx._ctx)
+    # (data-parallel: this rank's full-model gradients; not measured for the
+    # NCCL comparison mode)
+    e2e_ms = wall = None
+    e2e_idx = owned if args.dp == "none" else list(range(len(wl.numels)))
+    e2e_buf = L.BUF_GRAD if args.dp == "none" else L.BUF_DP_GRAD
+    h2d_bytes = gsz * sum(wl.numels[i] for i in e2e_idx)
+    if args.dp != "nccl":
+        pinned = [torch.empty(wl.numels[i] * gsz, dtype=torch.uint8, pin_memory=True) for i in e2e_idx]
+        for k, i in enumerate(e2e_idx):
+            pinned[k].copy_(torch.from_numpy(ctx.download(e2e_buf, i).view(np.uint8)))
+        lib = L.lib()
+
+        def upload_all():
+            for k, i in enumerate(e2e_idx):
+                L.check(lib.ody_upload_async(ctx._ctx, e2e_buf, i, pinned[k].data_ptr(), pinned[k].numel()),
+                        ctx._ctx)
+
+        upload_all()
         ctx.step(t)
         t += 1
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    w0 = time.perf_counter()
-    e0.record(stream)
-    for _ in range(args.e2e_steps):
-        for k, i in enumerate(owned):
-            L.check(lib.ody_upload_async(ctx._ctx, L.BUF_GRAD, i, pinned[k].data_ptr(), pinned[k].numel()), ctx._ctx)
-        ctx.step(t)  # synchronous: includes the device->host read of the step result
-        t += 1
-    e1.record(stream)
-    e1.synchronize()
-    wall = time.perf_counter() - w0
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
-    if world > 1:
-        x = torch.tensor([e2e_ms], dtype=torch.float64)
-        dist.all_reduce(x, op=dist.ReduceOp.MAX)
-        e2e_ms = x.item()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            upload_all()
+            ctx.step(t)  # synchronous: includes the device->host read of the step result
+            t += 1
+        e1.record(stream)
+        e1.synchronize()
+        wall = time.perf_counter() - w0
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+        if world > 1:
+            x = torch.tensor([e2e_ms], dtype=torch.float64)
+            dist.all_reduce(x, op=dist.ReduceOp.MAX)
+            e2e_ms = x.item()
 
     # N > 1: the all-gather of the re-quantised model after the sharded step
     # (not part of the step; reported beside it)
@@ -413,11 +476,13 @@ def main():
                                      if WORKLOAD == "flat1b" and QUANT == "nvfp4_tensor" else None),
                          "traffic_source": ("ncu capture of an 8-tensor case scaled by params"
                                             if WORKLOAD == "flat1b" and QUANT == "nvfp4_tensor" else None)},
-            "e2e": {"value": TOTAL / (e2e_ms * 1e-3), "unit": "params/s", "ms_per_step": e2e_ms,
-                    "wall_ms_per_step": wall * 1e3 / args.e2e_steps,
-                    "h2d_bytes_per_step": gsz * nloc, "d2h_bytes_per_step": 80},
+            "e2e": None if e2e_ms is None else {
+                "value": TOTAL / (e2e_ms * 1e-3), "unit": "params/s", "ms_per_step": e2e_ms,
+                "wall_ms_per_step": wall * 1e3 / args.e2e_steps,
+                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": 80},
             "gpu_launches": args.steps * (2 if world == 1 else 3),
             "graph_mode": use_graph,
+            "dp_gradients": args.dp,
             "clocks": clk.summary(),
             "last_step": {k: res[k] for k in ("grad_norm", "clip_coef", "clipped", "skipped", "scale_used")},
         }

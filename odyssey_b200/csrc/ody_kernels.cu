@@ -491,47 +491,72 @@ __device__ __forceinline__ void st_raw8(void* g, int64_t e0, const Raw8& r) {
   }
 }
 
-template <int GDT>
-__device__ __forceinline__ Raw8 reduce8(const RsArgs& rs, int64_t e0) {
-  // ranks in batches of four: the batch's loads are in flight together, the
-  // adds stay in rank order
-  constexpr int kBatch = 4;
-  float acc[8];
+// G groups of 8 gradients from each of up to R ranks (R <= 4): all G*R loads
+// are issued before the first add, so that enough remote reads are in
+// flight to cover the NVLink latency; the adds stay in rank order.  With 8
+// ranks (G = 1) the ranks come in two batches of four.  Each reduced group
+// is stored and its statistics taken at once.
+template <int GDT, int R, int G>
+__device__ __forceinline__ void reduce_groups(const RsArgs& rs, int64_t e0, int64_t stride_el, bool use_scaler,
+                                              const Divisor& dv, double& acc_sq, long long& bad) {
+  constexpr int RB = R < 4 ? R : 4;  // ranks per batch
+  float acc[G][8];
 #pragma unroll
-  for (int k = 0; k < 8; k++) acc[k] = 0.0f;
+  for (int q0 = 0; q0 < R; q0 += RB) {
+    Raw8 raw[G][RB];
 #pragma unroll
-  for (int q0 = 0; q0 < 8; q0 += kBatch) {
-    if (q0 < rs.world) {
-      Raw8 raw[kBatch];
+    for (int q = 0; q < RB; q++)
 #pragma unroll
-      for (int j = 0; j < kBatch; j++)
-        if (q0 + j < rs.world) raw[j] = ld_raw8<GDT>(rs.peers[q0 + j], rs.shard_off + e0);
+      for (int u = 0; u < G; u++)
+        if (q0 + q < rs.world) raw[u][q] = ld_raw8<GDT>(rs.peers[q0 + q], rs.shard_off + e0 + u * stride_el);
 #pragma unroll
-      for (int j = 0; j < kBatch; j++) {
-        if (q0 + j < rs.world) {
+    for (int u = 0; u < G; u++) {
+#pragma unroll
+      for (int q = 0; q < RB; q++) {
+        if (q0 + q < rs.world) {
           float v[8];
-          unpack8<GDT>(raw[j], v);
+          unpack8<GDT>(raw[u][q], v);
 #pragma unroll
-          for (int k = 0; k < 8; k++) acc[k] = (q0 + j == 0) ? v[k] : __fadd_rn(acc[k], v[k]);
+          for (int k = 0; k < 8; k++) acc[u][k] = (q0 + q == 0) ? v[k] : __fadd_rn(acc[u][k], v[k]);
         }
       }
     }
   }
-  const Raw8 r = pack8<GDT>(acc);
-  st_raw8<GDT>(rs.out, e0, r);
-  return r;
+#pragma unroll
+  for (int u = 0; u < G; u++) {
+    const Raw8 r = pack8<GDT>(acc[u]);
+    st_raw8<GDT>(rs.out, e0 + u * stride_el, r);
+    stats_raw8<GDT>(r, use_scaler, dv, acc_sq, bad);
+  }
 }
 
-template <int GDT>
+// R: the rank count rounded up to a power of two (1, 2, 4, 8); G = 4 / R
+// groups per thread per round (at least 1): four raw loads in flight
+template <int GDT, int R>
 __global__ void __launch_bounds__(kThreads, 4) rs_stats_kernel(StatsArgs a, RsArgs rs) {
+  constexpr int G = R >= 4 ? 1 : 4 / R;
   const Divisor dv = make_divisor(unscale_divisor<GDT>(a.scaler->scale));
   double acc = 0.0;
   long long bad = 0;
   const int64_t ngroups = a.n / 8;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < ngroups; i += stride)
-    stats_raw8<GDT>(reduce8<GDT>(rs, i * 8), a.use_scaler, dv, acc, bad);
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + (G - 1) * stride < ngroups; i += G * stride)
+    reduce_groups<GDT, R, G>(rs, i * 8, stride * 8, a.use_scaler, dv, acc, bad);
+  for (; i < ngroups; i += stride) reduce_groups<GDT, R, 1>(rs, i * 8, stride * 8, a.use_scaler, dv, acc, bad);
   stats_finish(a, acc, bad);
+}
+
+template <int GDT>
+static void launch_rs_gdt(int world, int grid, const StatsArgs& a, const RsArgs& rs, cudaStream_t st) {
+  if (world <= 1)
+    rs_stats_kernel<GDT, 1><<<grid, kThreads, 0, st>>>(a, rs);
+  else if (world <= 2)
+    rs_stats_kernel<GDT, 2><<<grid, kThreads, 0, st>>>(a, rs);
+  else if (world <= 4)
+    rs_stats_kernel<GDT, 4><<<grid, kThreads, 0, st>>>(a, rs);
+  else
+    rs_stats_kernel<GDT, 8><<<grid, kThreads, 0, st>>>(a, rs);
 }
 
 cudaError_t launch_rs_stats(int gdt, const void* const* peers, int world, int64_t shard_off, void* grad, int64_t n,
@@ -543,11 +568,11 @@ cudaError_t launch_rs_stats(int gdt, const void* const* peers, int world, int64_
               amax_slots, sync, ntensors};
   RsArgs rs{peers, world, shard_off, grad};
   if (gdt == DT_F32)
-    rs_stats_kernel<DT_F32><<<grid, kThreads, 0, st>>>(a, rs);
+    launch_rs_gdt<DT_F32>(world, grid, a, rs, st);
   else if (gdt == DT_F16)
-    rs_stats_kernel<DT_F16><<<grid, kThreads, 0, st>>>(a, rs);
+    launch_rs_gdt<DT_F16>(world, grid, a, rs, st);
   else
-    rs_stats_kernel<DT_BF16><<<grid, kThreads, 0, st>>>(a, rs);
+    launch_rs_gdt<DT_BF16>(world, grid, a, rs, st);
   return cudaGetLastError();
 }
 

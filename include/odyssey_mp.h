@@ -42,10 +42,13 @@ extern "C" {
 #define ODY_F16 1
 #define ODY_BF16 2
 
-/* ---- optimizers (src/odyssey/training/optimizers/{sgd,adam,adamw}.mojo) -- */
-#define ODY_SGD 0
-#define ODY_ADAM 1
-#define ODY_ADAMW 2
+/* ---- optimizers (src/odyssey/training/optimizers/*.mojo) ------------------ */
+#define ODY_SGD 0      /* sgd.mojo */
+#define ODY_ADAM 1     /* adam.mojo */
+#define ODY_ADAMW 2    /* adamw.mojo */
+#define ODY_LION 3     /* lion.mojo: state m; beta1/beta2 as Lion's (0.9 / 0.99 there) */
+#define ODY_RMSPROP 4  /* rmsprop.mojo: state square_avg (+ buf with momentum > 0); alpha */
+#define ODY_ADAGRAD 5  /* adagrad.mojo: state accum; its default epsilon is 1e-10 */
 
 /* ---- re-quantisation targets of the updated master weights --------------- */
 #define ODY_Q_NONE 0
@@ -76,11 +79,11 @@ extern "C" {
  * (configs/lenet5/emnist/fp16.toml).
  */
 typedef struct ody_config {
-  int32_t optimizer;          /* ODY_SGD / ODY_ADAM / ODY_ADAMW */
+  int32_t optimizer;          /* ODY_SGD ... ODY_ADAGRAD */
   int32_t device;             /* CUDA device ordinal */
   double learning_rate;
-  double momentum;            /* SGD */
-  double beta1, beta2, epsilon; /* Adam / AdamW */
+  double momentum;            /* SGD, RMSprop */
+  double beta1, beta2, epsilon; /* Adam / AdamW / Lion (betas), RMSprop / Adagrad (epsilon) */
   double weight_decay;
   int32_t use_gradient_scaler;  /* PrecisionConfig.use_gradient_scaler */
   float initial_scale;          /* default 65536 */
@@ -92,7 +95,9 @@ typedef struct ody_config {
   int32_t clip_enabled;         /* clip_gradients_by_global_norm */
   float max_norm;
   int32_t comm_timeout_ms;      /* multi-GPU: bound on every collective wait */
-  int32_t reserved[7];
+  int32_t reserved0;
+  double alpha;                 /* RMSprop smoothing constant (default 0.99) */
+  int32_t reserved[4];
 } ody_config;
 
 /* What one step did (PrecisionConfig.step bookkeeping,
@@ -271,6 +276,19 @@ int ody_adam_step(const float* params, const float* grads, const float* m, const
 int ody_adamw_step(const float* params, const float* grads, const float* m, const float* v, int64_t n,
                    int64_t t, double learning_rate, double beta1, double beta2, double epsilon,
                    double weight_decay, float* out_params, float* out_m, float* out_v);
+/* lion_step (lion.mojo:36-104): returns params and momentum. */
+int ody_lion_step(const float* params, const float* grads, const float* m, int64_t n, double learning_rate,
+                  double beta1, double beta2, double weight_decay, float* out_params, float* out_m);
+/* rmsprop_step (rmsprop.mojo:30-175); buf / out_buf only with momentum > 0
+ * (buf NULL: a zero buffer, as the reference initialises it). */
+int ody_rmsprop_step(const float* params, const float* grads, const float* square_avg, const float* buf,
+                     int64_t n, int64_t t, double learning_rate, double alpha, double epsilon,
+                     double weight_decay, double momentum, float* out_params, float* out_square_avg,
+                     float* out_buf);
+/* adagrad_step (adagrad.mojo:30-120). */
+int ody_adagrad_step(const float* params, const float* grads, const float* accum, int64_t n,
+                     double learning_rate, double epsilon, double weight_decay, float* out_params,
+                     float* out_accum);
 /* AnyTensor.to_fp8/to_bf8/to_mxfp4/to_nvfp4 (+ per-tensor-scaled kinds,
  * + FP16/BF16 casts): src is float32 (src_dtype ODY_F32) or bfloat16
  * (ODY_BF16, upcast exactly first); out holds ody_quant_bytes(kind, n)

@@ -14,7 +14,7 @@ LIB_PATH = os.environ.get("ODYSSEY_MP_LIB") or os.path.join(_HERE, "libodyssey_m
 OK = 0
 ERR_ARG, ERR_SHAPE, ERR_DTYPE, ERR_CUDA, ERR_NCCL, ERR_COMM_TIMEOUT, ERR_DEVICE_BOUNDS, ERR_STATE = range(-1, -9, -1)
 F32, F16, BF16 = 0, 1, 2
-SGD, ADAM, ADAMW = 0, 1, 2
+SGD, ADAM, ADAMW, LION, RMSPROP, ADAGRAD = 0, 1, 2, 3, 4, 5
 (Q_NONE, Q_FP16, Q_BF16, Q_FP8_E4M3, Q_FP8_E5M2, Q_FP8_E4M3_TENSOR, Q_MXFP4, Q_NVFP4,
  Q_NVFP4_TENSOR) = range(9)
 BUF_MASTER, BUF_STATE1, BUF_STATE2, BUF_GRAD, BUF_DP_GRAD = range(5)
@@ -41,7 +41,8 @@ class Config(C.Structure):
         ("weight_decay", C.c_double), ("use_gradient_scaler", C.c_int32), ("initial_scale", C.c_float),
         ("growth_factor", C.c_float), ("backoff_factor", C.c_float), ("growth_interval", C.c_int64),
         ("min_scale", C.c_float), ("max_scale", C.c_float), ("clip_enabled", C.c_int32),
-        ("max_norm", C.c_float), ("comm_timeout_ms", C.c_int32), ("reserved", C.c_int32 * 7),
+        ("max_norm", C.c_float), ("comm_timeout_ms", C.c_int32), ("reserved0", C.c_int32),
+        ("alpha", C.c_double), ("reserved", C.c_int32 * 4),
     ]
 
 
@@ -100,6 +101,9 @@ _SIGS = {
     "ody_sgd_step": (C.c_int, [_p, _p, _p, _i64, C.c_double, C.c_double, C.c_double, _p, _p]),
     "ody_adam_step": (C.c_int, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p]),
     "ody_adamw_step": (C.c_int, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p]),
+    "ody_lion_step": (C.c_int, [_p, _p, _p, _i64] + [C.c_double] * 4 + [_p, _p]),
+    "ody_rmsprop_step": (C.c_int, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p]),
+    "ody_adagrad_step": (C.c_int, [_p, _p, _p, _i64] + [C.c_double] * 3 + [_p, _p]),
     "ody_quantize": (C.c_int, [_i32, _p, _i32, _i64, _p, _p]),
     "ody_dequantize": (C.c_int, [_i32, _p, _i64, C.c_float, _p]),
 }

@@ -212,7 +212,12 @@ extern "C" void ody_config_default(ody_config* c) {
   c->clip_enabled = 0;
   c->max_norm = 1.0f;
   c->comm_timeout_ms = 60000;
+  c->alpha = 0.99;
 }
+
+// optimizers whose step takes a timestep t >= 1 (adam.mojo:118,
+// adamw.mojo:118, rmsprop.mojo:125)
+static bool needs_timestep(int opt) { return opt == ODY_ADAM || opt == ODY_ADAMW || opt == ODY_RMSPROP; }
 
 extern "C" int64_t ody_quant_bytes(int32_t kind, int64_t n) {
   if (n < 0) return -1;
@@ -265,7 +270,7 @@ static int64_t quant_region(int kind, int64_t npad) {
 
 extern "C" int ody_ctx_create(ody_ctx** out, const ody_config* cfg) {
   if (!out || !cfg) return fail(ODY_ERR_ARG, "ody_ctx_create: null argument");
-  if (cfg->optimizer < ODY_SGD || cfg->optimizer > ODY_ADAMW)
+  if (cfg->optimizer < ODY_SGD || cfg->optimizer > ODY_ADAGRAD)
     return fail(ODY_ERR_ARG, "unknown optimizer " + std::to_string(cfg->optimizer));
   if (cfg->clip_enabled && !(cfg->max_norm > 0.0f))
     return fail(ODY_ERR_ARG, "max_norm must be positive, got: " + std::to_string(cfg->max_norm));
@@ -475,8 +480,9 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   ODY_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamDefault));
   ODY_CUDA(cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming));
   const size_t n = (size_t)(off > 0 ? off : kPad);
-  const bool need_s1 = c->cfg.optimizer != ODY_SGD || c->cfg.momentum > 0.0;
-  const bool need_s2 = c->cfg.optimizer != ODY_SGD;
+  const int opt = c->cfg.optimizer;
+  const bool need_s1 = opt != ODY_SGD || c->cfg.momentum > 0.0;
+  const bool need_s2 = opt == ODY_ADAM || opt == ODY_ADAMW || (opt == ODY_RMSPROP && c->cfg.momentum > 0.0);
   ODY_CUDA(dalloc(&c->master, n * 4));
   ODY_CUDA(cudaMemsetAsync(c->master, 0, n * 4, c->stream));
   if (need_s1) {
@@ -665,7 +671,11 @@ static OptConsts make_consts(const ody_config& cfg, int64_t t) {
   o.b2 = (float)cfg.beta2;
   o.omb2 = (float)(1.0 - cfg.beta2);
   o.eps = (float)cfg.epsilon;
-  if (t > 0) {
+  o.alpha = (float)cfg.alpha;
+  o.omalpha = (float)(1.0 - cfg.alpha);
+  o.wdlr = (float)(cfg.weight_decay * cfg.learning_rate);
+  o.use_wd_nz = cfg.weight_decay != 0.0;
+  if (t > 0 && (cfg.optimizer == ODY_ADAM || cfg.optimizer == ODY_ADAMW)) {
     o.bc1 = (float)(1.0 - pow(cfg.beta1, (double)t));
     o.bc2 = (float)(1.0 - pow(cfg.beta2, (double)t));
   }
@@ -855,7 +865,7 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   if (!c) return fail(ODY_ERR_ARG, "null context");
   if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
   if (c->broken) return ctx_fail(c, ODY_ERR_STATE, "context unusable after a communicator failure");
-  if (c->cfg.optimizer != ODY_SGD && t <= 0)
+  if (needs_timestep(c->cfg.optimizer) && t <= 0)
     return ctx_fail(c, ODY_ERR_ARG, "Timestep t must be positive (starts at 1)");
   ODY_CUDA(cudaSetDevice(c->cfg.device));
   const OptConsts oc = make_consts(c->cfg, t);
@@ -1412,19 +1422,33 @@ extern "C" int ody_global_norm_clip(float* const* grads, const int64_t* numels, 
 
 static int opt_common(int opt, const float* p, const float* g, const float* s1, const float* s2, int64_t n,
                       int64_t t, double lr, double mu, double b1, double b2, double eps, double wd, float* op,
-                      float* os1, float* os2) {
+                      float* os1, float* os2, double alpha = 0.99) {
   if (n <= 0) return fail(ODY_ERR_SHAPE, "Parameters and gradients must have the same shape");
   if (!p || !g || !op) return fail(ODY_ERR_ARG, "null pointer");
   if (opt == OPT_SGD) {
     if (mu > 0.0 && !s1)
       return fail(ODY_ERR_ARG, "Velocity buffer required when using momentum (use zeros_like(params))");
+  } else if (opt == OPT_LION) {
+    if (!s1 || !os1) return fail(ODY_ERR_ARG, "lion_step: params and momentum must have the same shape");
+  } else if (opt == OPT_RMSPROP) {
+    if (!s1 || !os1) return fail(ODY_ERR_ARG, "square_avg must be initialized (use zeros_like(params))");
+    if (t <= 0) return fail(ODY_ERR_ARG, "Timestep t must be positive (starts at 1)");
+    if (mu > 0.0 && !os2) return fail(ODY_ERR_ARG, "momentum > 0 needs an output momentum buffer");
+  } else if (opt == OPT_ADAGRAD) {
+    if (!s1 || !os1) return fail(ODY_ERR_ARG, "accumulator must be initialized (use zeros_like(params))");
   } else {
     if (!s1 || !s2 || !os1 || !os2)
       return fail(ODY_ERR_ARG, "Moment buffers (m and v) must be initialized (use zeros_like(params))");
     if (t <= 0) return fail(ODY_ERR_ARG, "Timestep t must be positive (starts at 1)");
   }
+  if (opt == OPT_RMSPROP && !(mu > 0.0)) {
+    s2 = nullptr;  // no momentum buffer is read or written
+    os2 = nullptr;
+  }
   ody_config cfg;
   ody_config_default(&cfg);
+  cfg.optimizer = opt;
+  cfg.alpha = alpha;
   cfg.learning_rate = lr;
   cfg.momentum = mu;
   cfg.beta1 = b1;
@@ -1468,6 +1492,22 @@ extern "C" int ody_adamw_step(const float* p, const float* g, const float* m, co
                               double lr, double b1, double b2, double eps, double wd, float* op, float* om,
                               float* ov) {
   return opt_common(OPT_ADAMW, p, g, m, v, n, t, lr, 0.0, b1, b2, eps, wd, op, om, ov);
+}
+
+extern "C" int ody_lion_step(const float* p, const float* g, const float* m, int64_t n, double lr, double b1,
+                             double b2, double wd, float* op, float* om) {
+  return opt_common(OPT_LION, p, g, m, nullptr, n, 0, lr, 0.0, b1, b2, 1e-8, wd, op, om, nullptr);
+}
+
+extern "C" int ody_rmsprop_step(const float* p, const float* g, const float* sq, const float* buf, int64_t n,
+                                int64_t t, double lr, double alpha, double eps, double wd, double mu, float* op,
+                                float* osq, float* obuf) {
+  return opt_common(OPT_RMSPROP, p, g, sq, buf, n, t, lr, mu, 0.9, 0.999, eps, wd, op, osq, obuf, alpha);
+}
+
+extern "C" int ody_adagrad_step(const float* p, const float* g, const float* acc, int64_t n, double lr, double eps,
+                                double wd, float* op, float* oacc) {
+  return opt_common(OPT_ADAGRAD, p, g, acc, nullptr, n, 0, lr, 0.0, 0.9, 0.999, eps, wd, op, oacc, nullptr);
 }
 
 extern "C" int ody_quantize(int32_t kind, const void* src, int32_t sdt, int64_t n, void* out, float* ts) {

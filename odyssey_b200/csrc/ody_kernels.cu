@@ -870,7 +870,7 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
         m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w;
         m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
       }
-      if (OPT != OPT_SGD) {
+      if (OPT == OPT_ADAM || OPT == OPT_ADAMW || (OPT == OPT_RMSPROP && oc.use_mu)) {
         const float4* vp = reinterpret_cast<const float4*>(a.s2 + e0);
         float4 v0 = __ldcs(vp), v1 = __ldcs(vp + 1);
         v[0] = v0.x; v[1] = v0.y; v[2] = v0.z; v[3] = v0.w;
@@ -884,8 +884,14 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
           sgd_elem(p[k], gk, m[k], oc);
         else if (OPT == OPT_ADAM)
           adam_elem<false>(p[k], gk, m[k], v[k], oc);
-        else
+        else if (OPT == OPT_ADAMW)
           adam_elem<true>(p[k], gk, m[k], v[k], oc);
+        else if (OPT == OPT_LION)
+          lion_elem(p[k], gk, m[k], oc);
+        else if (OPT == OPT_RMSPROP)
+          rmsprop_elem(p[k], gk, m[k], v[k], oc);
+        else
+          adagrad_elem(p[k], gk, m[k], oc);
       }
       float4* pw = reinterpret_cast<float4*>(a.master + e0);
       pw[0] = make_float4(p[0], p[1], p[2], p[3]);
@@ -895,7 +901,7 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
         __stcs(mw, make_float4(m[0], m[1], m[2], m[3]));
         __stcs(mw + 1, make_float4(m[4], m[5], m[6], m[7]));
       }
-      if (OPT != OPT_SGD) {
+      if (OPT == OPT_ADAM || OPT == OPT_ADAMW || (OPT == OPT_RMSPROP && oc.use_mu)) {
         float4* vw = reinterpret_cast<float4*>(a.s2 + e0);
         __stcs(vw, make_float4(v[0], v[1], v[2], v[3]));
         __stcs(vw + 1, make_float4(v[4], v[5], v[6], v[7]));
@@ -1077,8 +1083,11 @@ int apply_grid(int gdt, int opt, int device) {
 #define ODY_G(G, O) \
   if (gdt == G && opt == O) return grid_for_apply<G, O>(device);
   ODY_G(DT_F32, OPT_SGD) ODY_G(DT_F32, OPT_ADAM) ODY_G(DT_F32, OPT_ADAMW)
+  ODY_G(DT_F32, OPT_LION) ODY_G(DT_F32, OPT_RMSPROP) ODY_G(DT_F32, OPT_ADAGRAD)
   ODY_G(DT_F16, OPT_SGD) ODY_G(DT_F16, OPT_ADAM) ODY_G(DT_F16, OPT_ADAMW)
+  ODY_G(DT_F16, OPT_LION) ODY_G(DT_F16, OPT_RMSPROP) ODY_G(DT_F16, OPT_ADAGRAD)
   ODY_G(DT_BF16, OPT_SGD) ODY_G(DT_BF16, OPT_ADAM) ODY_G(DT_BF16, OPT_ADAMW)
+  ODY_G(DT_BF16, OPT_LION) ODY_G(DT_BF16, OPT_RMSPROP) ODY_G(DT_BF16, OPT_ADAGRAD)
 #undef ODY_G
   return 148;
 }
@@ -1106,8 +1115,11 @@ cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, 
     return cudaLaunchKernelEx(&cfg, apply_kernel<G, O>, a); \
   }
   ODY_L(DT_F32, OPT_SGD) ODY_L(DT_F32, OPT_ADAM) ODY_L(DT_F32, OPT_ADAMW)
+  ODY_L(DT_F32, OPT_LION) ODY_L(DT_F32, OPT_RMSPROP) ODY_L(DT_F32, OPT_ADAGRAD)
   ODY_L(DT_F16, OPT_SGD) ODY_L(DT_F16, OPT_ADAM) ODY_L(DT_F16, OPT_ADAMW)
+  ODY_L(DT_F16, OPT_LION) ODY_L(DT_F16, OPT_RMSPROP) ODY_L(DT_F16, OPT_ADAGRAD)
   ODY_L(DT_BF16, OPT_SGD) ODY_L(DT_BF16, OPT_ADAM) ODY_L(DT_BF16, OPT_ADAMW)
+  ODY_L(DT_BF16, OPT_LION) ODY_L(DT_BF16, OPT_RMSPROP) ODY_L(DT_BF16, OPT_ADAGRAD)
 #undef ODY_L
   return cudaErrorInvalidValue;
 }
@@ -1116,8 +1128,11 @@ const void* apply_kernel_fn(int gdt, int opt) {
 #define ODY_F(G, O) \
   if (gdt == G && opt == O) return reinterpret_cast<const void*>(&apply_kernel<G, O>);
   ODY_F(DT_F32, OPT_SGD) ODY_F(DT_F32, OPT_ADAM) ODY_F(DT_F32, OPT_ADAMW)
+  ODY_F(DT_F32, OPT_LION) ODY_F(DT_F32, OPT_RMSPROP) ODY_F(DT_F32, OPT_ADAGRAD)
   ODY_F(DT_F16, OPT_SGD) ODY_F(DT_F16, OPT_ADAM) ODY_F(DT_F16, OPT_ADAMW)
+  ODY_F(DT_F16, OPT_LION) ODY_F(DT_F16, OPT_RMSPROP) ODY_F(DT_F16, OPT_ADAGRAD)
   ODY_F(DT_BF16, OPT_SGD) ODY_F(DT_BF16, OPT_ADAM) ODY_F(DT_BF16, OPT_ADAMW)
+  ODY_F(DT_BF16, OPT_LION) ODY_F(DT_BF16, OPT_RMSPROP) ODY_F(DT_BF16, OPT_ADAGRAD)
 #undef ODY_F
   return nullptr;
 }
@@ -1499,6 +1514,18 @@ __global__ void opt_kernel(OptConsts oc, const float* p, const float* g, const f
       float vel = s1 ? s1[i] : 0.0f;
       sgd_elem(pp, g[i], vel, oc);
       if (os1) os1[i] = vel;
+    } else if (OPT == OPT_LION || OPT == OPT_ADAGRAD) {
+      float st = s1[i];
+      if (OPT == OPT_LION)
+        lion_elem(pp, g[i], st, oc);
+      else
+        adagrad_elem(pp, g[i], st, oc);
+      os1[i] = st;
+    } else if (OPT == OPT_RMSPROP) {
+      float sq = s1[i], buf = s2 ? s2[i] : 0.0f;
+      rmsprop_elem(pp, g[i], sq, buf, oc);
+      os1[i] = sq;
+      if (os2) os2[i] = buf;
     } else {
       float m = s1[i], v = s2[i];
       adam_elem<OPT == OPT_ADAMW>(pp, g[i], m, v, oc);
@@ -1515,8 +1542,14 @@ cudaError_t launch_opt_step(int opt, const OptConsts& oc, const float* p, const 
     opt_kernel<OPT_SGD><<<grid_for(n), kThreads, 0, st>>>(oc, p, g, s1, s2, n, op, os1, os2);
   else if (opt == OPT_ADAM)
     opt_kernel<OPT_ADAM><<<grid_for(n), kThreads, 0, st>>>(oc, p, g, s1, s2, n, op, os1, os2);
-  else
+  else if (opt == OPT_ADAMW)
     opt_kernel<OPT_ADAMW><<<grid_for(n), kThreads, 0, st>>>(oc, p, g, s1, s2, n, op, os1, os2);
+  else if (opt == OPT_LION)
+    opt_kernel<OPT_LION><<<grid_for(n), kThreads, 0, st>>>(oc, p, g, s1, s2, n, op, os1, os2);
+  else if (opt == OPT_RMSPROP)
+    opt_kernel<OPT_RMSPROP><<<grid_for(n), kThreads, 0, st>>>(oc, p, g, s1, s2, n, op, os1, os2);
+  else
+    opt_kernel<OPT_ADAGRAD><<<grid_for(n), kThreads, 0, st>>>(oc, p, g, s1, s2, n, op, os1, os2);
   return cudaGetLastError();
 }
 

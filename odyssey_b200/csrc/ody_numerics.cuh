@@ -16,7 +16,7 @@
 namespace ody {
 
 enum : int { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2 };
-enum : int { OPT_SGD = 0, OPT_ADAM = 1, OPT_ADAMW = 2 };
+enum : int { OPT_SGD = 0, OPT_ADAM = 1, OPT_ADAMW = 2, OPT_LION = 3, OPT_RMSPROP = 4, OPT_ADAGRAD = 5 };
 enum : int {
   Q_NONE = 0,
   Q_FP16 = 1,
@@ -35,7 +35,10 @@ struct OptConsts {
   float lr, mu, wd;          // sgd.mojo:27-121
   float b1, omb1, b2, omb2;  // adam.mojo:123-140
   float bc1, bc2, eps;       // adam.mojo:142-163
+  float alpha, omalpha;      // rmsprop.mojo:144-152
+  float wdlr;                // lion.mojo:100-103: Float64(wd * lr) rounded once
   int use_wd, use_mu;
+  int use_wd_nz;             // lion.mojo:100: weight_decay != 0
 };
 
 // sgd.mojo:89-118: e = g + wd*p; v' = mu*v + e; p' = p - lr*v'
@@ -62,6 +65,47 @@ __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
   float np = __fsub_rn(p, __fmul_rn(c.lr, __fdiv_rn(mh, den)));
   if (DECOUPLED && c.use_wd) np = __fsub_rn(np, __fmul_rn(c.wd, np));
   p = np;
+}
+
+// lion.mojo:76-104: m' = b2*m + (1-b2)*g; step = sign(b1*m + (1-b1)*g) of
+// the old m (sign: 1 / -1 / 0, NaN -> 0, elementwise.mojo:148-155);
+// p' = p - lr*step - (wd*lr)*p with the old p
+__device__ __forceinline__ void lion_elem(float& p, float g, float& m, const OptConsts& c) {
+  const float nm = __fadd_rn(__fmul_rn(c.b2, m), __fmul_rn(c.omb2, g));
+  const float x = __fadd_rn(__fmul_rn(c.b1, m), __fmul_rn(c.omb1, g));
+  const float u = x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f);
+  float np = __fsub_rn(p, __fmul_rn(c.lr, u));
+  if (c.use_wd_nz) np = __fsub_rn(np, __fmul_rn(c.wdlr, p));
+  p = np;
+  m = nm;
+}
+
+// rmsprop.mojo:128-175: e = g + wd*p (wd > 0); sq' = alpha*sq + (1-alpha)*e^2
+// (pow(e, 2.0) as the correctly rounded e*e); n = e / (sqrt(sq') + eps);
+// with momentum buf' = mu*buf + n is the update; p' = p - lr*update
+__device__ __forceinline__ void rmsprop_elem(float& p, float g, float& sq, float& buf, const OptConsts& c) {
+  float e = g;
+  if (c.use_wd) e = __fadd_rn(g, __fmul_rn(c.wd, p));
+  const float nsq = __fadd_rn(__fmul_rn(c.alpha, sq), __fmul_rn(c.omalpha, __fmul_rn(e, e)));
+  const float den = __fadd_rn(__fsqrt_rn(nsq), c.eps);
+  float upd = __fdiv_rn(e, den);
+  if (c.use_mu) {
+    buf = __fadd_rn(__fmul_rn(c.mu, buf), upd);
+    upd = buf;
+  }
+  p = __fsub_rn(p, __fmul_rn(c.lr, upd));
+  sq = nsq;
+}
+
+// adagrad.mojo:93-118: acc' = acc + g*g; update = lr * g / (sqrt(acc') + eps)
+// (+ wd*p outside the adaptive scaling when wd > 0); p' = p - update
+__device__ __forceinline__ void adagrad_elem(float& p, float g, float& acc, const OptConsts& c) {
+  const float na = __fadd_rn(acc, __fmul_rn(g, g));
+  const float den = __fadd_rn(__fsqrt_rn(na), c.eps);
+  float upd = __fmul_rn(c.lr, __fdiv_rn(g, den));
+  if (c.use_wd) upd = __fadd_rn(upd, __fmul_rn(c.wd, p));
+  p = __fsub_rn(p, upd);
+  acc = na;
 }
 
 // ---- low-precision element casts (IEEE round-to-nearest-even) -------------

@@ -16,7 +16,8 @@ import numpy as np
 from . import _lib as L
 from .quant import QuantizedTensor
 
-_OPT = {"sgd": L.SGD, "adam": L.ADAM, "adamw": L.ADAMW}
+_OPT = {"sgd": L.SGD, "adam": L.ADAM, "adamw": L.ADAMW, "lion": L.LION, "rmsprop": L.RMSPROP,
+        "adagrad": L.ADAGRAD}
 _GDT = {"float32": L.F32, "float16": L.F16, "bfloat16": L.BF16}
 
 
@@ -39,7 +40,7 @@ class MixedPrecisionStep:
                  momentum=0.0, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.0,
                  use_gradient_scaler=True, initial_scale=65536.0, growth_factor=2.0, backoff_factor=0.5,
                  growth_interval=2000, min_scale=1.0, max_scale=65536.0, clip_max_norm=None, device=0,
-                 world_size=1, rank=0, unique_id=None, comm_timeout_ms=60000):
+                 world_size=1, rank=0, unique_id=None, comm_timeout_ms=60000, alpha=0.99):
         cfg = L.default_config()
         cfg.optimizer = _OPT[optimizer] if isinstance(optimizer, str) else int(optimizer)
         cfg.device = int(device)
@@ -51,6 +52,7 @@ class MixedPrecisionStep:
         cfg.clip_enabled = int(clip_max_norm is not None)
         cfg.max_norm = float(clip_max_norm) if clip_max_norm is not None else 1.0
         cfg.comm_timeout_ms = int(comm_timeout_ms)
+        cfg.alpha = float(alpha)
         self.cfg = cfg
         self.numels = [int(n) for n in numels]
         self.grad_dtype = _GDT[grad_dtype] if isinstance(grad_dtype, str) else int(grad_dtype)

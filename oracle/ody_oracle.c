@@ -692,6 +692,105 @@ DEFINE_ADAM(ora_adam_step_f64, double, sqrt, 0)
 DEFINE_ADAM(ora_adamw_step_f32, float, sqrtf, 1)
 DEFINE_ADAM(ora_adamw_step_f64, double, sqrt, 1)
 
+/* lion.mojo:76-104: the momentum EMA uses beta2; the sign of the beta1
+ * interpolation of the OLD momentum is the step; decoupled weight decay
+ * lr*wd (one Float64 product rounded once) times the OLD params, applied
+ * when wd != 0.  sign(x) is 1 for x > 0, -1 for x < 0, else 0
+ * (elementwise.mojo:148-155, so NaN gives 0). */
+#define DEFINE_LION(SUF, T)                                                     \
+  void ora_lion_step_##SUF(const T* p, const T* g, const T* m, int64_t n,       \
+                           double lr, double b1, double b2, double wd,          \
+                           T* out_p, T* out_m) {                                \
+    const T b2_t = (T)b2, omb2 = (T)(1.0 - b2), b1_t = (T)b1,                   \
+            omb1 = (T)(1.0 - b1), lr_t = (T)lr, wdlr = (T)(wd * lr);            \
+    const int use_wd = wd != 0.0;                                              \
+    _Pragma("omp parallel for num_threads(ORA_NT) schedule(static)")            \
+    for (int64_t i = 0; i < n; i++) {                                           \
+      T a = b2_t * m[i];                                                        \
+      T c = omb2 * g[i];                                                        \
+      T nm = a + c;                                                             \
+      T x1 = b1_t * m[i];                                                       \
+      T x2 = omb1 * g[i];                                                       \
+      T x = x1 + x2;                                                            \
+      T u = x > (T)0 ? (T)1 : (x < (T)0 ? (T)-1 : (T)0);                        \
+      T lu = lr_t * u;                                                          \
+      T np = p[i] - lu;                                                         \
+      if (use_wd) {                                                             \
+        T d = wdlr * p[i];                                                      \
+        np = np - d;                                                            \
+      }                                                                         \
+      out_p[i] = np;                                                            \
+      out_m[i] = nm;                                                            \
+    }                                                                           \
+  }
+DEFINE_LION(f32, float)
+DEFINE_LION(f64, double)
+
+/* rmsprop.mojo:128-175: coupled weight decay (wd > 0) into the gradient,
+ * square_avg EMA, eps outside the sqrt, optional momentum buffer (a zero
+ * buffer when none is given), p - lr*update. */
+#define DEFINE_RMSPROP(SUF, T, SQRT)                                            \
+  void ora_rmsprop_step_##SUF(const T* p, const T* g, const T* sq,              \
+                              const T* buf, int64_t n, double lr, double alpha, \
+                              double eps, double wd, double momentum, T* out_p, \
+                              T* out_sq, T* out_buf) {                          \
+    const T al = (T)alpha, oma = (T)(1.0 - alpha), eps_t = (T)eps,              \
+            lr_t = (T)lr, wd_t = (T)wd, mu_t = (T)momentum;                     \
+    const int use_wd = wd > 0.0, use_mu = momentum > 0.0;                      \
+    _Pragma("omp parallel for num_threads(ORA_NT) schedule(static)")            \
+    for (int64_t i = 0; i < n; i++) {                                           \
+      T e = g[i];                                                               \
+      if (use_wd) {                                                             \
+        T d = wd_t * p[i];                                                      \
+        e = g[i] + d;                                                           \
+      }                                                                         \
+      T g2 = e * e;                                                             \
+      T a1 = al * sq[i];                                                        \
+      T a2 = oma * g2;                                                          \
+      T nsq = a1 + a2;                                                          \
+      T den = SQRT(nsq) + eps_t;                                                \
+      T ng = e / den;                                                           \
+      T upd = ng;                                                               \
+      if (use_mu) {                                                             \
+        T b = buf ? buf[i] : (T)0;                                              \
+        T bt = mu_t * b;                                                        \
+        upd = bt + ng;                                                          \
+        if (out_buf) out_buf[i] = upd;                                          \
+      }                                                                         \
+      T pu = lr_t * upd;                                                        \
+      out_p[i] = p[i] - pu;                                                     \
+      out_sq[i] = nsq;                                                          \
+    }                                                                           \
+  }
+DEFINE_RMSPROP(f32, float, sqrtf)
+DEFINE_RMSPROP(f64, double, sqrt)
+
+/* adagrad.mojo:93-118: accum + g*g (no weight decay fold), eps outside the
+ * sqrt, lr*g/den, plus wd*p outside the adaptive scaling when wd > 0. */
+#define DEFINE_ADAGRAD(SUF, T, SQRT)                                            \
+  void ora_adagrad_step_##SUF(const T* p, const T* g, const T* acc, int64_t n,  \
+                              double lr, double eps, double wd, T* out_p,       \
+                              T* out_acc) {                                     \
+    const T eps_t = (T)eps, lr_t = (T)lr, wd_t = (T)wd;                         \
+    const int use_wd = wd > 0.0;                                               \
+    _Pragma("omp parallel for num_threads(ORA_NT) schedule(static)")            \
+    for (int64_t i = 0; i < n; i++) {                                           \
+      T g2 = g[i] * g[i];                                                       \
+      T na = acc[i] + g2;                                                       \
+      T den = SQRT(na) + eps_t;                                                 \
+      T ag = g[i] / den;                                                        \
+      T upd = lr_t * ag;                                                        \
+      if (use_wd) {                                                             \
+        T d = wd_t * p[i];                                                      \
+        upd = upd + d;                                                          \
+      }                                                                         \
+      out_p[i] = p[i] - upd;                                                    \
+      out_acc[i] = na;                                                          \
+    }                                                                           \
+  }
+DEFINE_ADAGRAD(f32, float, sqrtf)
+DEFINE_ADAGRAD(f64, double, sqrt)
+
 /* ------------------------------------------------------------------------ */
 /* The fused step, in the order of examples/mixed_precision_training.mojo:  */
 /* 132-216 and examples/lenet_emnist/run_train.mojo:219-306:                 */
@@ -703,7 +802,8 @@ int ora_fused_step(ora_tensor* ts, int nt, const ora_cfg* cfg, ora_scaler* sc,
                    int64_t* step_count, int64_t* overflow_count, int64_t t,
                    ora_result* res) {
   memset(res, 0, sizeof(*res));
-  if (cfg->optimizer != ORA_SGD && t <= 0) return -1;
+  if ((cfg->optimizer == ORA_ADAM || cfg->optimizer == ORA_ADAMW || cfg->optimizer == ORA_RMSPROP) && t <= 0)
+    return -1;
   res->scale_used = sc->scale;
   int64_t total = 0;
   for (int i = 0; i < nt; i++) total += ts[i].numel;
@@ -755,6 +855,18 @@ int ora_fused_step(ora_tensor* ts, int nt, const ora_cfg* cfg, ora_scaler* sc,
         case ORA_SGD:
           ora_sgd_step_f32(T->master, g, T->s1, n, cfg->lr, cfg->momentum,
                            cfg->weight_decay, T->master, T->s1);
+          break;
+        case ORA_LION:
+          ora_lion_step_f32(T->master, g, T->s1, n, cfg->lr, cfg->beta1, cfg->beta2, cfg->weight_decay,
+                            T->master, T->s1);
+          break;
+        case ORA_RMSPROP:
+          ora_rmsprop_step_f32(T->master, g, T->s1, T->s2, n, cfg->lr, cfg->alpha, cfg->epsilon,
+                               cfg->weight_decay, cfg->momentum, T->master, T->s1, T->s2);
+          break;
+        case ORA_ADAGRAD:
+          ora_adagrad_step_f32(T->master, g, T->s1, n, cfg->lr, cfg->epsilon, cfg->weight_decay, T->master,
+                               T->s1);
           break;
         case ORA_ADAM:
           ora_adam_step_f32(T->master, g, T->s1, T->s2, n, t, cfg->lr, cfg->beta1,

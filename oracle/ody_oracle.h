@@ -11,8 +11,9 @@
  * the reference; the citations are paths inside that project.
  *
  * Pinning: the optimizer formulas are pinned by the reference's own golden
- * vectors (tests/odyssey/training/optimizers/test_{sgd,adam,adamw}.mojo,
- * float64, tol 1e-9); the scaler by tests/odyssey/training/
+ * vectors (tests/odyssey/training/optimizers/test_{sgd,adam,adamw,lion,
+ * rmsprop}.mojo, float64, tol 1e-9; Adagrad has no reference fixture and is
+ * pinned by this restatement of adagrad.mojo only); the scaler by tests/odyssey/training/
  * test_mixed_precision.mojo; the FP4 block formats only by the reference's
  * tolerance tests (tests/core/types/test_{mx,nv}fp4_block.mojo) -- the bit
  * patterns of FP4 codes and scales are pinned by this restatement of
@@ -33,7 +34,7 @@ extern "C" {
 /* element dtypes (same codes as include/odyssey_mp.h) */
 enum { ORA_F32 = 0, ORA_F16 = 1, ORA_BF16 = 2 };
 /* optimizers */
-enum { ORA_SGD = 0, ORA_ADAM = 1, ORA_ADAMW = 2 };
+enum { ORA_SGD = 0, ORA_ADAM = 1, ORA_ADAMW = 2, ORA_LION = 3, ORA_RMSPROP = 4, ORA_ADAGRAD = 5 };
 /* re-quantisation targets (same codes as include/odyssey_mp.h) */
 enum {
   ORA_Q_NONE = 0,
@@ -120,14 +121,32 @@ void ora_adamw_step_f64(const double* p, const double* g, const double* m,
                         double b1, double b2, double eps, double wd,
                         double* out_p, double* out_m, double* out_v);
 
+/* lion.mojo:36-104, rmsprop.mojo:30-175 (pow(e, 2.0) restated as the
+ * correctly rounded e*e), adagrad.mojo:30-120 */
+void ora_lion_step_f32(const float* p, const float* g, const float* m, int64_t n, double lr, double b1,
+                       double b2, double wd, float* out_p, float* out_m);
+void ora_lion_step_f64(const double* p, const double* g, const double* m, int64_t n, double lr, double b1,
+                       double b2, double wd, double* out_p, double* out_m);
+void ora_rmsprop_step_f32(const float* p, const float* g, const float* sq, const float* buf, int64_t n,
+                          double lr, double alpha, double eps, double wd, double momentum, float* out_p,
+                          float* out_sq, float* out_buf);
+void ora_rmsprop_step_f64(const double* p, const double* g, const double* sq, const double* buf, int64_t n,
+                          double lr, double alpha, double eps, double wd, double momentum, double* out_p,
+                          double* out_sq, double* out_buf);
+void ora_adagrad_step_f32(const float* p, const float* g, const float* acc, int64_t n, double lr, double eps,
+                          double wd, float* out_p, float* out_acc);
+void ora_adagrad_step_f64(const double* p, const double* g, const double* acc, int64_t n, double lr,
+                          double eps, double wd, double* out_p, double* out_acc);
+
 /* ---- the fused step (call stack B of the reference) --------------------- */
 typedef struct {
   int64_t numel;
   int32_t grad_dtype;
   int32_t quant;
   float* master; /* in/out */
-  float* s1;     /* velocity (SGD) or m (Adam/AdamW); may be NULL for SGD mu=0 */
-  float* s2;     /* v (Adam/AdamW) */
+  float* s1;     /* velocity (SGD), m (Adam/AdamW/Lion), square_avg (RMSprop),
+                    accumulator (Adagrad); may be NULL for SGD mu=0 */
+  float* s2;     /* v (Adam/AdamW), momentum buffer (RMSprop with momentum) */
   const void* grad;
   uint8_t* qout;  /* ora_quant_bytes(quant, numel) bytes, or NULL */
   float* qscale;  /* per-tensor scale out, or NULL */
@@ -139,6 +158,7 @@ typedef struct {
   int32_t use_scaler;
   int32_t clip_enabled;
   float max_norm;
+  double alpha; /* RMSprop smoothing constant */
 } ora_cfg;
 
 typedef struct {

@@ -16,7 +16,7 @@ _LIB_PATH = os.path.join(_HERE, "libody_oracle.so")
 _lib = None
 
 F32, F16, BF16 = 0, 1, 2
-SGD, ADAM, ADAMW = 0, 1, 2
+SGD, ADAM, ADAMW, LION, RMSPROP, ADAGRAD = 0, 1, 2, 3, 4, 5
 Q_NONE, Q_FP16, Q_BF16, Q_FP8_E4M3, Q_FP8_E5M2, Q_FP8_E4M3_TENSOR, Q_MXFP4, Q_NVFP4, Q_NVFP4_TENSOR = range(9)
 
 _p = C.c_void_p
@@ -38,7 +38,7 @@ class Cfg(C.Structure):
     _fields_ = [("optimizer", C.c_int32), ("lr", C.c_double), ("momentum", C.c_double),
                 ("beta1", C.c_double), ("beta2", C.c_double), ("epsilon", C.c_double),
                 ("weight_decay", C.c_double), ("use_scaler", C.c_int32), ("clip_enabled", C.c_int32),
-                ("max_norm", C.c_float)]
+                ("max_norm", C.c_float), ("alpha", C.c_double)]
 
 
 class Result(C.Structure):
@@ -87,6 +87,9 @@ def lib():
             sig[f"ora_sgd_step_{t}"] = (None, [_p, _p, _p, _i64, C.c_double, C.c_double, C.c_double, _p, _p])
             for o in ("adam", "adamw"):
                 sig[f"ora_{o}_step_{t}"] = (None, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p])
+            sig[f"ora_lion_step_{t}"] = (None, [_p, _p, _p, _i64] + [C.c_double] * 4 + [_p, _p])
+            sig[f"ora_rmsprop_step_{t}"] = (None, [_p, _p, _p, _p, _i64] + [C.c_double] * 5 + [_p, _p, _p])
+            sig[f"ora_adagrad_step_{t}"] = (None, [_p, _p, _p, _i64] + [C.c_double] * 3 + [_p, _p])
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
             fn.restype = res
@@ -275,6 +278,36 @@ def adamw_step(p, g, m, v, t, lr, b1=0.9, b2=0.999, eps=1e-8, wd=0.0, f64=False)
     return _adam("adamw", p, g, m, v, t, lr, b1, b2, eps, wd, f64)
 
 
+def lion_step(p, g, m, lr, b1=0.9, b2=0.99, wd=0.0, f64=False):
+    dt = np.float64 if f64 else np.float32
+    p, g, m = (np.ascontiguousarray(a, dt) for a in (p, g, m))
+    op, om = np.empty_like(p), np.empty_like(m)
+    getattr(lib(), f"ora_lion_step_{'f64' if f64 else 'f32'}")(
+        _ptr(p), _ptr(g), _ptr(m), p.size, lr, b1, b2, wd, _ptr(op), _ptr(om))
+    return op, om
+
+
+def rmsprop_step(p, g, sq, lr, alpha=0.99, eps=1e-8, wd=0.0, momentum=0.0, buf=None, f64=False):
+    dt = np.float64 if f64 else np.float32
+    p, g, sq = (np.ascontiguousarray(a, dt) for a in (p, g, sq))
+    bufa = np.ascontiguousarray(buf, dt) if buf is not None else None
+    op, osq = np.empty_like(p), np.empty_like(sq)
+    ob = np.zeros_like(p) if momentum > 0.0 else None
+    getattr(lib(), f"ora_rmsprop_step_{'f64' if f64 else 'f32'}")(
+        _ptr(p), _ptr(g), _ptr(sq), _ptr(bufa) if bufa is not None else None, p.size, lr, alpha, eps, wd,
+        momentum, _ptr(op), _ptr(osq), _ptr(ob) if ob is not None else None)
+    return op, osq, ob
+
+
+def adagrad_step(p, g, acc, lr, eps=1e-10, wd=0.0, f64=False):
+    dt = np.float64 if f64 else np.float32
+    p, g, acc = (np.ascontiguousarray(a, dt) for a in (p, g, acc))
+    op, oa = np.empty_like(p), np.empty_like(acc)
+    getattr(lib(), f"ora_adagrad_step_{'f64' if f64 else 'f32'}")(
+        _ptr(p), _ptr(g), _ptr(acc), p.size, lr, eps, wd, _ptr(op), _ptr(oa))
+    return op, oa
+
+
 # ---- fused step over a model ----
 class Model:
     """Host-side state of a whole model for ora_fused_step.
@@ -284,10 +317,10 @@ class Model:
 
     def __init__(self, specs, optimizer, lr, momentum=0.0, beta1=0.9, beta2=0.999, epsilon=1e-8,
                  weight_decay=0.0, use_scaler=True, clip_enabled=False, max_norm=1.0,
-                 scaler_kwargs=None):
+                 scaler_kwargs=None, alpha=0.99):
         self.specs = specs
         self.cfg = Cfg(optimizer, lr, momentum, beta1, beta2, epsilon, weight_decay, int(use_scaler),
-                       int(clip_enabled), max_norm)
+                       int(clip_enabled), max_norm, alpha)
         self.scaler = scaler(**(scaler_kwargs or {}))
         self.step_count = C.c_int64(0)
         self.overflow_count = C.c_int64(0)

@@ -5,9 +5,9 @@ Run in a container where the reference checkout is present:
     python tests/golden/make_golden.py /path/to/Odyssey
 
 It (1) runs the reference's own numpy/torch parity generators
-``tests/odyssey/training/optimizers/parity_refs/{sgd,adam,adamw}_parity_reference.py``
+``tests/odyssey/training/optimizers/parity_refs/{sgd,adam,adamw,lion,rmsprop}_parity_reference.py``
 and (2) reads the values the reference's Mojo tests transcribed from them
-(``test_{sgd,adam,adamw}.mojo`` ``test_parity_with_reference``), checks that
+(``test_{sgd,adam,adamw,lion,rmsprop}.mojo`` ``test_parity_with_reference``), checks that
 both agree, and writes ``optimizer_parity.json``.  The scaler and clip cases
 (``scaler_cases.json``, ``clip_cases.json``) are the assertions of
 ``tests/odyssey/training/test_mixed_precision.mojo``,
@@ -38,7 +38,7 @@ def _mojo_lists(root, name):
     body = src[src.index("def test_parity_with_reference"):]
     body = body[: body.index("print(\"test_parity_with_reference PASSED\")")]
     lists = {}
-    for var, val in re.findall(r"\b(r[pmv])\.append\(([-0-9.e+]+)\)", body):
+    for var, val in re.findall(r"\b(r[a-z]+)\.append\(([-0-9.e+]+)\)", body):
         lists.setdefault(var, []).append(float(val))
     call = re.search(rf"{name}_step\(([^)]*)\)", body).group(1)
     line = src[: src.index("def test_parity_with_reference")].count("\n") + 1
@@ -47,7 +47,7 @@ def _mojo_lists(root, name):
 
 def optimizer_parity(root):
     out = {}
-    for name in ("sgd", "adam", "adamw"):
+    for name in ("sgd", "adam", "adamw", "lion", "rmsprop"):
         ref = _run_ref(root, name)
         lists, call, line = _mojo_lists(root, name)
         new_p = ref["new_params"]
@@ -60,7 +60,16 @@ def optimizer_parity(root):
             "grad": ref["grad"],
             "new_params": new_p,
         }
-        if name == "sgd":
+        if name == "lion":
+            case.update(lr=ref["lr"], beta1=ref["beta1"], beta2=ref["beta2"], weight_decay=ref["weight_decay"],
+                        m=ref["momentum_in"], new_m=ref["new_momentum"])
+            assert max(abs(a - b) for a, b in zip(ref["new_momentum"], lists["rm"])) < 1e-12
+        elif name == "rmsprop":
+            case.update(lr=ref["lr"], alpha=ref["alpha"], epsilon=ref["epsilon"], weight_decay=ref["weight_decay"],
+                        t=1, square_avg=ref["square_avg_in"], new_square_avg=ref["new_square_avg"],
+                        generator=ref["source"])
+            assert max(abs(a - b) for a, b in zip(ref["new_square_avg"], lists["rsq"])) < 1e-12
+        elif name == "sgd":
             case.update(lr=ref["lr"], momentum=ref["momentum"], weight_decay=ref["weight_decay"],
                         velocity=ref.get("velocity_in", ref.get("velocity")),
                         new_velocity=ref["new_velocity"])

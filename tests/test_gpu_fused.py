@@ -10,7 +10,7 @@ from odyssey_b200 import workloads as W
 pytestmark = pytest.mark.gpu
 
 GDT = {"float32": 0, "float16": 1, "bfloat16": 2}
-OPT = {"sgd": 0, "adam": 1, "adamw": 2}
+OPT = {"sgd": 0, "adam": 1, "adamw": 2, "lion": 3, "rmsprop": 4, "adagrad": 5}
 QK = {"none": 0, "fp16": 1, "bf16": 2, "fp8": 3, "bf8": 4, "fp8_tensor": 5, "mxfp4": 6, "nvfp4": 7,
       "nvfp4_tensor": 8}
 
@@ -39,7 +39,7 @@ def run_pair(oracle, wl, nsteps, numels=None, quants=None, seed=0, t0=1, check_e
     model = oracle.Model(specs, OPT[wl.optimizer], hy["learning_rate"], momentum=hy.get("momentum", 0.0),
                          beta1=hy.get("beta1", 0.9), beta2=hy.get("beta2", 0.999), epsilon=hy.get("epsilon", 1e-8),
                          weight_decay=hy.get("weight_decay", 0.0), clip_enabled=wl.clip is not None,
-                         max_norm=wl.clip or 1.0, scaler_kwargs=sk)
+                         max_norm=wl.clip or 1.0, scaler_kwargs=sk, alpha=hy.get("alpha", 0.99))
     master = wl.master(seed, numels)
     for i, m in enumerate(master):
         ctx.set_master(i, m)
@@ -63,7 +63,7 @@ def run_pair(oracle, wl, nsteps, numels=None, quants=None, seed=0, t0=1, check_e
             assert r["grad_norm"] == ro.norm and r["clip_coef"] == ro.coef, s
         else:
             assert not np.isfinite(r["sumsq"]), s
-        if not r["skipped"] and wl.optimizer != "sgd":
+        if not r["skipped"] and wl.optimizer in ("adam", "adamw", "rmsprop"):
             t += 1
         if (s + 1) % check_every == 0 or s == nsteps - 1:
             compare_state(ctx, model, numels, qlist, wl.optimizer)
@@ -76,7 +76,7 @@ def compare_state(ctx, model, numels, qlist, optimizer):
         assert d.max() <= 2, (i, d.max())
         if optimizer != "sgd" or model.cfg.momentum > 0:
             assert ulp_diff(ctx.state(i, 0), model.s1[i]).max() <= 2, i
-        if optimizer != "sgd":
+        if optimizer in ("adam", "adamw") or (optimizer == "rmsprop" and model.cfg.momentum > 0):
             assert ulp_diff(ctx.state(i, 1), model.s2[i]).max() <= 2, i
         if QK[qlist[i]] != 0:
             q = ctx.get_quant(i)
@@ -118,17 +118,32 @@ def test_flat_adamw_clip_nvfp4_tensor_small(oracle):
     ctx.close()
 
 
-@pytest.mark.parametrize("opt", ["sgd", "adam", "adamw"])
+HYPER = {
+    "sgd": dict(learning_rate=1e-2, momentum=0.9, weight_decay=0.01),
+    "adam": dict(learning_rate=1e-3, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.01),
+    "adamw": dict(learning_rate=1e-3, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.01),
+    "lion": dict(learning_rate=1e-4, beta1=0.9, beta2=0.99, weight_decay=0.01),
+    "rmsprop": dict(learning_rate=1e-2, alpha=0.9, epsilon=1e-8, weight_decay=0.01, momentum=0.9),
+    "adagrad": dict(learning_rate=1e-2, epsilon=1e-10, weight_decay=0.01),
+}
+
+
+@pytest.mark.parametrize("opt", ["sgd", "adam", "adamw", "lion", "rmsprop", "adagrad"])
 @pytest.mark.parametrize("gdt", ["float32", "float16", "bfloat16"])
 def test_all_kinds_all_optimizers(oracle, opt, gdt):
     """Every re-quantisation kind in one model, ragged tensor sizes."""
     wl = W.Workload("mix", [(1,), (15,), (33,), (2049,), (5000,), (16384 + 64,), (40000,), (7,), (100,)],
-                    gdt, "none", opt,
-                    dict(learning_rate=1e-2, momentum=0.9, weight_decay=0.01) if opt == "sgd" else
-                    dict(learning_rate=1e-3, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.01),
-                    0.05, 1e-3, 256.0, clip=0.05)
+                    gdt, "none", opt, HYPER[opt], 0.05, 1e-3, 256.0, clip=0.05)
     quants = ["fp16", "bf16", "fp8", "bf8", "fp8_tensor", "mxfp4", "nvfp4", "nvfp4_tensor", "none"]
     ctx, model, res = run_pair(oracle, wl, 3, quants=quants)
+    ctx.close()
+
+
+def test_rmsprop_without_momentum_fused(oracle):
+    """RMSprop without momentum keeps a single state buffer."""
+    wl = W.Workload("rms", [(3000,), (70,)], "bfloat16", "nvfp4_tensor", "rmsprop",
+                    dict(learning_rate=1e-3, alpha=0.99, epsilon=1e-8), 0.05, 1e-3, 1024.0)
+    ctx, model, res = run_pair(oracle, wl, 3)
     ctx.close()
 
 

@@ -1,6 +1,6 @@
 """GPU parity of the single-op entry points (unscale, finite check, global-
-norm clip, SGD / Adam / AdamW) against the oracle and the reference's golden
-vectors."""
+norm clip, SGD / Adam / AdamW / Lion / RMSprop / Adagrad) against the oracle
+and the reference's golden vectors."""
 import numpy as np
 import pytest
 
@@ -56,6 +56,45 @@ def test_optimizers_bit_exact(ody, oracle, n, wd):
             np.testing.assert_array_equal(x.view(np.uint32), y.view(np.uint32))
 
 
+@pytest.mark.parametrize("n", [1, 7, 1000, 65537])
+@pytest.mark.parametrize("wd", [0.0, 0.01])
+def test_lion_rmsprop_adagrad_bit_exact(ody, oracle, n, wd):
+    """lion.mojo / rmsprop.mojo / adagrad.mojo through the CUDA single ops,
+    bit for bit against the oracle's float32 restatement; zeros in the
+    gradient and momentum exercise Lion's sign(0) = 0."""
+    p, g, m = _rand(n, 1, 0.05), _rand(n, 2, 1e-3), _rand(n, 3, 1e-3)
+    g[::5] = 0.0
+    m[::5] = 0.0
+    sq = np.abs(_rand(n, 4, 1e-6))
+    same = lambda a, b: [np.testing.assert_array_equal(x.view(np.uint32), y.view(np.uint32))  # noqa: E731
+                         for x, y in zip(a, b)]
+    same(ody.lion_step(p, g, m, 1e-4, 0.9, 0.99, wd), oracle.lion_step(p, g, m, 1e-4, 0.9, 0.99, wd))
+    same(ody.adagrad_step(p, g, sq, 1e-2, 1e-10, wd), oracle.adagrad_step(p, g, sq, 1e-2, 1e-10, wd))
+    a = ody.rmsprop_step(p, g, sq, 1, 1e-2, 0.99, 1e-8, wd)
+    b = oracle.rmsprop_step(p, g, sq, 1e-2, 0.99, 1e-8, wd)
+    same(a[:2], b[:2])
+    buf = _rand(n, 5, 1e-2)
+    a = ody.rmsprop_step(p, g, sq, 3, 1e-2, 0.9, 1e-8, wd, momentum=0.9, buf=buf)
+    b = oracle.rmsprop_step(p, g, sq, 1e-2, 0.9, 1e-8, wd, momentum=0.9, buf=buf)
+    same(a, b)
+
+
+@pytest.mark.parametrize("name", ["lion", "rmsprop"])
+def test_lion_rmsprop_golden_f32(ody, golden, name):
+    """The reference's float64 golden vectors (test_lion.mojo,
+    test_rmsprop.mojo) through the float32 kernels."""
+    c = golden["optimizer_parity"][name]
+    f = lambda k: np.array(c[k], np.float32)  # noqa: E731
+    if name == "lion":
+        p, m = ody.lion_step(f("params"), f("grad"), f("m"), c["lr"], c["beta1"], c["beta2"], c["weight_decay"])
+        np.testing.assert_allclose(m, c["new_m"], rtol=2e-6, atol=1e-9)
+    else:
+        p, sq, _ = ody.rmsprop_step(f("params"), f("grad"), f("square_avg"), 1, c["lr"], c["alpha"],
+                                    c["epsilon"], c["weight_decay"])
+        np.testing.assert_allclose(sq, c["new_square_avg"], rtol=2e-6, atol=1e-12)
+    np.testing.assert_allclose(p, c["new_params"], rtol=2e-6, atol=1e-7)
+
+
 def test_optimizer_errors(ody):
     z = np.zeros(4, np.float32)
     with pytest.raises(ody.OdysseyError, match="Timestep t must be positive"):
@@ -64,6 +103,14 @@ def test_optimizer_errors(ody):
         ody.sgd_step(z, z, None, 0.1, momentum=0.9)
     with pytest.raises(ody.OdysseyError, match="same shape"):
         ody.sgd_step(z, np.zeros(5, np.float32), z, 0.1)
+    with pytest.raises(ody.OdysseyError, match="lion_step: params and momentum must have the same shape"):
+        ody.lion_step(z, z, np.zeros(5, np.float32), 1e-4)
+    with pytest.raises(ody.OdysseyError, match="square_avg must be initialized"):
+        ody.rmsprop_step(z, z, np.zeros(0, np.float32), 1, 1e-2)
+    with pytest.raises(ody.OdysseyError, match="Timestep t must be positive"):
+        ody.rmsprop_step(z, z, z, 0, 1e-2)
+    with pytest.raises(ody.OdysseyError, match="accumulator must be initialized"):
+        ody.adagrad_step(z, z, np.zeros(0, np.float32), 1e-2)
 
 
 @pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])

@@ -276,6 +276,16 @@ int ody_adam_step(const float* params, const float* grads, const float* m, const
 int ody_adamw_step(const float* params, const float* grads, const float* m, const float* v, int64_t n,
                    int64_t t, double learning_rate, double beta1, double beta2, double epsilon,
                    double weight_decay, float* out_params, float* out_m, float* out_v);
+/* FP4 singles: each value with its own power-of-two scale (MXFP4 /
+ * NVFP4.from_float32, mxfp4.mojo:303-342, nvfp4.mojo:290-328; with seeds,
+ * from_float32_stochastic, mxfp4.mojo:344-396 + 398-483).  kind is
+ * ODY_Q_MXFP4 (E8M0 scale bytes) or ODY_Q_NVFP4 (E4M3 scale bytes); values
+ * receive the 4-bit E2M1 codes, one per byte.  seeds: NULL for round to
+ * nearest, else one seed per value. */
+int ody_fp4_single_encode(int32_t kind, const float* x, int64_t n, const uint64_t* seeds, uint8_t* values,
+                          uint8_t* scales);
+/* MXFP4 / NVFP4.to_float32 (mxfp4.mojo:484-491, nvfp4.mojo:474-481). */
+int ody_fp4_single_decode(int32_t kind, const uint8_t* values, const uint8_t* scales, int64_t n, float* out);
 /* lion_step (lion.mojo:36-104): returns params and momentum. */
 int ody_lion_step(const float* params, const float* grads, const float* m, int64_t n, double learning_rate,
                   double beta1, double beta2, double weight_decay, float* out_params, float* out_m);

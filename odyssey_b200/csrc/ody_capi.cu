@@ -1555,6 +1555,44 @@ extern "C" int ody_dequantize(int32_t kind, const void* q, int64_t n, float ts, 
   return ODY_OK;
 }
 
+extern "C" int ody_fp4_single_encode(int32_t kind, const float* x, int64_t n, const uint64_t* seeds,
+                                     uint8_t* values, uint8_t* scales) {
+  if (kind != ODY_Q_MXFP4 && kind != ODY_Q_NVFP4)
+    return fail(ODY_ERR_ARG, "FP4 singles are ODY_Q_MXFP4 or ODY_Q_NVFP4, not " + std::to_string(kind));
+  if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot convert an empty tensor");
+  if (!x || !values || !scales) return fail(ODY_ERR_ARG, "null pointer");
+  Scope S;
+  void *dx, *dseeds = nullptr, *dv, *ds;
+  ODY_STAGE(S, x, (size_t)n * 4, true, &dx);
+  if (seeds) ODY_STAGE(S, seeds, (size_t)n * 8, true, &dseeds);
+  ODY_STAGE(S, values, (size_t)n, false, &dv);
+  ODY_STAGE(S, scales, (size_t)n, false, &ds);
+  ODY_CUDA(launch_fp4_single_encode(kind == ODY_Q_MXFP4, (const float*)dx, n, (const uint64_t*)dseeds,
+                                    (uint8_t*)dv, (uint8_t*)ds, S.st));
+  ODY_CUDA(S.copy_out(values));
+  ODY_CUDA(S.copy_out(scales));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  return ODY_OK;
+}
+
+extern "C" int ody_fp4_single_decode(int32_t kind, const uint8_t* values, const uint8_t* scales, int64_t n,
+                                     float* out) {
+  if (kind != ODY_Q_MXFP4 && kind != ODY_Q_NVFP4)
+    return fail(ODY_ERR_ARG, "FP4 singles are ODY_Q_MXFP4 or ODY_Q_NVFP4, not " + std::to_string(kind));
+  if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot convert an empty tensor");
+  if (!values || !scales || !out) return fail(ODY_ERR_ARG, "null pointer");
+  Scope S;
+  void *dv, *ds, *dout;
+  ODY_STAGE(S, values, (size_t)n, true, &dv);
+  ODY_STAGE(S, scales, (size_t)n, true, &ds);
+  ODY_STAGE(S, out, (size_t)n * 4, false, &dout);
+  ODY_CUDA(launch_fp4_single_decode(kind == ODY_Q_MXFP4, (const uint8_t*)dv, (const uint8_t*)ds, n,
+                                    (float*)dout, S.st));
+  ODY_CUDA(S.copy_out(out));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  return ODY_OK;
+}
+
 // Test hook (not part of include/odyssey_mp.h): the exact-division shortcut
 // used by the per-tensor-scaled requant against IEEE division, on device
 // arrays of n (x, s) pairs.

@@ -106,6 +106,10 @@ cudaError_t launch_rs_stats(int gdt, const void* const* peers, int world, int64_
                             int use_scaler, DevScaler* scaler, StatsPartial* partials, int grid, unsigned* ticket,
                             int world_mode, double* local_stats, const DecideParams& dp, Decision* dec,
                             uint32_t* amax_slots, uint32_t* sync, int ntensors, cudaStream_t st);
+cudaError_t launch_fp4_single_encode(int mx, const float* x, int64_t n, const uint64_t* seeds, uint8_t* vals,
+                                     uint8_t* scs, cudaStream_t st);
+cudaError_t launch_fp4_single_decode(int mx, const uint8_t* vals, const uint8_t* scs, int64_t n, float* out,
+                                     cudaStream_t st);
 int apply_grid(int gdt, int opt, int device);
 // the apply kernel instance for (gdt, opt), and an update of its node in an
 // instantiated graph with new launch arguments

@@ -1504,6 +1504,103 @@ cudaError_t launch_scale_inplace(float* g, int64_t n, const float* coef, cudaStr
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// FP4 singles: one value with its own power-of-two scale
+// (MXFP4/NVFP4.from_float32 / from_float32_stochastic / to_float32,
+// src/odyssey/core/types/mxfp4.mojo:303-491, nvfp4.mojo:290-481).
+// ---------------------------------------------------------------------------
+// _fp4_from_float32 (mxfp4.mojo:144-224) on RN(x / scale)
+__device__ __forceinline__ uint8_t fp4_ladder_code(float x, float scale) {
+  if (x != x) return 0x7;
+  if (fabsf(x) == __uint_as_float(0x7f800000u)) return x > 0.0f ? 0x7 : 0xf;
+  const float q = __fdiv_rn(x, scale);
+  if (q == 0.0f) return 0;
+  const uint8_t sign = q < 0.0f;
+  const float a = fabsf(q);
+  if (a >= 6.0f) return (uint8_t)((sign << 3) | 0x7);
+  if (a < 0.5f) return (uint8_t)(sign << 3);
+  const uint8_t code = a < 1.25f ? 0x2 : a < 1.75f ? 0x3 : a < 2.5f ? 0x4 : a < 3.5f ? 0x5 : a < 5.0f ? 0x6 : 0x7;
+  return (uint8_t)((sign << 3) | code);
+}
+
+// _fp4_stochastic_round (mxfp4.mojo:398-483): the E2M1 bucket of |x/scale|,
+// P(upper) = (|x/scale| - lower) / (upper - lower), one 32-bit LCG step of
+// the seed, (state >> 8) / 2^24 < P picks the upper value
+__device__ __forceinline__ uint8_t fp4_stochastic_code(float x, float scale, uint64_t seed) {
+  const float q = __fdiv_rn(x, scale);
+  const uint8_t sign = q < 0.0f;
+  const float a = sign ? -q : q;
+  float lo, hi;
+  uint8_t lb, ub;
+  if (a < 0.5f) return (uint8_t)(sign << 3);
+  if (a < 1.0f) { lo = 0.0f; hi = 1.0f; lb = 0x0; ub = 0x2; }
+  else if (a < 1.5f) { lo = 1.0f; hi = 1.5f; lb = 0x2; ub = 0x3; }
+  else if (a < 2.0f) { lo = 1.5f; hi = 2.0f; lb = 0x3; ub = 0x4; }
+  else if (a < 3.0f) { lo = 2.0f; hi = 3.0f; lb = 0x4; ub = 0x5; }
+  else if (a < 4.0f) { lo = 3.0f; hi = 4.0f; lb = 0x5; ub = 0x6; }
+  else if (a < 6.0f) { lo = 4.0f; hi = 6.0f; lb = 0x6; ub = 0x7; }
+  else return (uint8_t)((sign << 3) | 0x7);
+  const float p_up = __fdiv_rn(__fsub_rn(a, lo), __fsub_rn(hi, lo));
+  const uint32_t st = 1103515245u * (uint32_t)seed + 12345u;
+  const float r = __fdiv_rn((float)(st >> 8), 16777216.0f);
+  return (uint8_t)((sign << 3) | (r < p_up ? ub : lb));
+}
+
+__global__ void fp4_single_encode_kernel(int mx, const float* x, int64_t n, const uint64_t* seeds, uint8_t* vals,
+                                         uint8_t* scs) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float v = x[i];
+    const uint8_t unit = mx ? 127 : 0x3C;
+    if (v != v || fabsf(v) == __uint_as_float(0x7f800000u)) {
+      vals[i] = fp4_ladder_code(v, 1.0f);
+      scs[i] = unit;
+      continue;
+    }
+    if (v == 0.0f) {
+      vals[i] = 0;
+      scs[i] = unit;
+      continue;
+    }
+    const float ax = v > 0.0f ? v : -v;
+    float sv = 1.0f;
+    int ev = 0;
+    // at most 128 doublings (sv reaches Inf, the quotient 0) and 127 halvings
+    while (__fdiv_rn(ax, sv) > 6.0f) {
+      sv = __fmul_rn(sv, 2.0f);
+      ev++;
+    }
+    while (__fdiv_rn(ax, sv) < 0.5f && ev > (mx ? -127 : -7)) {
+      sv = __fdiv_rn(sv, 2.0f);
+      ev--;
+    }
+    const uint8_t e = mx ? e8m0_from_f32(sv) : e4m3_scale_from_f32(sv);
+    const float sf = mx ? e8m0_to_f32(e) : e4m3_to_f32(e);
+    scs[i] = e;
+    vals[i] = seeds ? fp4_stochastic_code(v, sf, seeds[i]) : fp4_ladder_code(v, sf);
+  }
+}
+
+__global__ void fp4_single_decode_kernel(int mx, const uint8_t* vals, const uint8_t* scs, int64_t n, float* out) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float sf = mx ? e8m0_to_f32(scs[i]) : e4m3_to_f32(scs[i]);
+    out[i] = fp4_decode(vals[i] & 0xfu, sf);
+  }
+}
+
+cudaError_t launch_fp4_single_encode(int mx, const float* x, int64_t n, const uint64_t* seeds, uint8_t* vals,
+                                     uint8_t* scs, cudaStream_t st) {
+  fp4_single_encode_kernel<<<grid_for(n), kThreads, 0, st>>>(mx, x, n, seeds, vals, scs);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fp4_single_decode(int mx, const uint8_t* vals, const uint8_t* scs, int64_t n, float* out,
+                                     cudaStream_t st) {
+  fp4_single_decode_kernel<<<grid_for(n), kThreads, 0, st>>>(mx, vals, scs, n, out);
+  return cudaGetLastError();
+}
+
 template <int OPT>
 __global__ void opt_kernel(OptConsts oc, const float* p, const float* g, const float* s1, const float* s2,
                            int64_t n, float* op, float* os1, float* os2) {

@@ -103,3 +103,58 @@ def from_mxfp4(q):
 def from_nvfp4(q):
     """tensor_dtype_conv.mojo:433-494."""
     return _from(q, L.Q_NVFP4, 9, "NVFP4")
+
+
+class _FP4Single:
+    """FP4 singles: one E2M1 code per value, each with its own power-of-two
+    scale byte (MXFP4 / NVFP4 scalar types, src/odyssey/core/types/
+    mxfp4.mojo:279-491 and nvfp4.mojo:265-481), over arrays of values."""
+
+    kind = None
+
+    @classmethod
+    def _encode(cls, x, seeds):
+        src = L.contiguous(x)
+        n = L.numel(src)
+        if n == 0:
+            raise L.OdysseyError("cannot convert an empty tensor", L.ERR_SHAPE)
+        if L.dtype_code(src) != L.F32:
+            raise L.OdysseyError("FP4 singles convert float32 values", L.ERR_DTYPE)
+        sd = None
+        if seeds is not None:
+            sd = np.ascontiguousarray(seeds, np.uint64) if not L.is_torch(seeds) else seeds.contiguous()
+            if L.numel(sd) != n:
+                raise L.OdysseyError("one seed per value", L.ERR_SHAPE)
+        vals, scs = L.empty_like(src, "uint8", n), L.empty_like(src, "uint8", n)
+        L.check(L.lib().ody_fp4_single_encode(cls.kind, L.ptr(src), n, L.ptr(sd), L.ptr(vals), L.ptr(scs)))
+        return vals, scs
+
+    @classmethod
+    def from_float32(cls, x):
+        """from_float32 per value -> (codes, scale bytes)."""
+        return cls._encode(x, None)
+
+    @classmethod
+    def from_float32_stochastic(cls, x, seeds):
+        """from_float32_stochastic per value with its seed -> (codes, scale bytes)."""
+        return cls._encode(x, seeds)
+
+    @classmethod
+    def to_float32(cls, values, scales):
+        v, s = L.contiguous(values), L.contiguous(scales)
+        n = L.numel(v)
+        if n == 0 or L.numel(s) != n:
+            raise L.OdysseyError("values and scales must be non-empty and of one length", L.ERR_SHAPE)
+        out = L.empty_like(v, "float32", n)
+        L.check(L.lib().ody_fp4_single_decode(cls.kind, L.ptr(v), L.ptr(s), n, L.ptr(out)))
+        return out
+
+
+class MXFP4(_FP4Single):
+    """MXFP4 singles (E8M0 scale bytes)."""
+    kind = L.QUANT_NAMES["mxfp4"]
+
+
+class NVFP4(_FP4Single):
+    """NVFP4 singles (E4M3 scale bytes)."""
+    kind = L.QUANT_NAMES["nvfp4"]

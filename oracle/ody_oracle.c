@@ -232,6 +232,78 @@ uint8_t ora_fp4_from_f32(float x, float scale) {
   return (uint8_t)((sign << 3) | (e << 1) | m);
 }
 
+/* MXFP4._fp4_stochastic_round (mxfp4.mojo:398-483; the NVFP4 copy,
+ * nvfp4.mojo:386-471, is identical): bucket of |x/scale| between two E2M1
+ * values (0 and 1.0 adjacent: 0.5 is never produced), probability of the
+ * upper one (|x/scale| - lower) / (upper - lower), one LCG step on the low
+ * 32 bits of the seed, its top 24 bits / 2^24 compared with it. */
+static uint8_t fp4_stochastic_round(float x, float scale, uint64_t seed) {
+  float scaled = x / scale;
+  uint8_t sign = 0;
+  float a = scaled;
+  if (scaled < 0) {
+    sign = 1;
+    a = -scaled;
+  }
+  float lower, upper;
+  uint8_t lb, ub;
+  if (a < 0.5f) return (uint8_t)(sign << 3);
+  else if (a < 1.0f) { lower = 0.0f; upper = 1.0f; lb = 0x0; ub = 0x2; }
+  else if (a < 1.5f) { lower = 1.0f; upper = 1.5f; lb = 0x2; ub = 0x3; }
+  else if (a < 2.0f) { lower = 1.5f; upper = 2.0f; lb = 0x3; ub = 0x4; }
+  else if (a < 3.0f) { lower = 2.0f; upper = 3.0f; lb = 0x4; ub = 0x5; }
+  else if (a < 4.0f) { lower = 3.0f; upper = 4.0f; lb = 0x5; ub = 0x6; }
+  else if (a < 6.0f) { lower = 4.0f; upper = 6.0f; lb = 0x6; ub = 0x7; }
+  else return (uint8_t)((sign << 3) | 0x7);
+  float dist = a - lower;
+  float range = upper - lower;
+  float prob_up = dist / range;
+  uint32_t st = (uint32_t)seed;
+  st = 1103515245u * st + 12345u;
+  float rv = (float)(st >> 8) / 16777216.0f;
+  return (uint8_t)((sign << 3) | (rv < prob_up ? ub : lb));
+}
+
+/* MXFP4/NVFP4.from_float32 and from_float32_stochastic (mxfp4.mojo:303-396,
+ * nvfp4.mojo:290-384): NaN/Inf encode against scale 1 with the unit scale
+ * byte (E8M0 127 / E4M3 0x3C), zero is code 0 with the unit scale; else the
+ * power-of-two scale found by doubling while |x|/scale > 6 and halving
+ * while |x|/scale < 0.5 (down to 2^-127 / 2^-7), stored as E8M0 / E4M3. */
+void ora_fp4_single_encode(int kind, float x, int stochastic, uint64_t seed, uint8_t* value, uint8_t* scale) {
+  const int mx = kind == ORA_Q_MXFP4;
+  const uint8_t unit = mx ? 127 : 0x3C;
+  if (isnan(x) || isinf(x)) {
+    *value = (uint8_t)(ora_fp4_from_f32(x, 1.0f) & 0xf);
+    *scale = unit;
+    return;
+  }
+  if (x == 0.0f) {
+    *value = 0;
+    *scale = unit;
+    return;
+  }
+  float ax = x > 0 ? x : -x;
+  float sv = 1.0f;
+  int ev = 0;
+  while (ax / sv > 6.0f) {
+    sv *= 2.0f;
+    ev++;
+  }
+  while (ax / sv < 0.5f && ev > (mx ? -127 : -7)) {
+    sv /= 2.0f;
+    ev--;
+  }
+  const uint8_t e = mx ? ora_e8m0_from_f32(sv) : ora_e4m3_scale_from_f32(sv);
+  const float sf = mx ? ora_e8m0_to_f32(e) : ora_e4m3_to_f32(e);
+  *scale = e;
+  *value = stochastic ? fp4_stochastic_round(x, sf, seed) : (uint8_t)(ora_fp4_from_f32(x, sf) & 0xf);
+}
+
+float ora_fp4_single_decode(int kind, uint8_t value, uint8_t scale) {
+  const float sf = kind == ORA_Q_MXFP4 ? ora_e8m0_to_f32(scale) : ora_e4m3_to_f32(scale);
+  return ora_fp4_to_f32((uint8_t)(value & 0xf), sf);
+}
+
 /* mxfp4.mojo:227-268 (_fp4_to_float32) */
 float ora_fp4_to_f32(uint8_t code, float scale) {
   int sign = (code >> 3) & 1, e = (code >> 1) & 3, m = code & 1;

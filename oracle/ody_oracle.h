@@ -138,6 +138,13 @@ void ora_adagrad_step_f32(const float* p, const float* g, const float* acc, int6
 void ora_adagrad_step_f64(const double* p, const double* g, const double* acc, int64_t n, double lr,
                           double eps, double wd, double* out_p, double* out_acc);
 
+/* ---- FP4 singles: one value with its own scale (MXFP4/NVFP4.from_float32,
+ * from_float32_stochastic, to_float32; mxfp4.mojo:303-491, nvfp4.mojo:
+ * 290-481).  kind ORA_Q_MXFP4 or ORA_Q_NVFP4; stochastic 0 gives
+ * from_float32, else from_float32_stochastic with the given seed. */
+void ora_fp4_single_encode(int kind, float x, int stochastic, uint64_t seed, uint8_t* value, uint8_t* scale);
+float ora_fp4_single_decode(int kind, uint8_t value, uint8_t scale);
+
 /* ---- the fused step (call stack B of the reference) --------------------- */
 typedef struct {
   int64_t numel;

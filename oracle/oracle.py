@@ -82,6 +82,8 @@ def lib():
             "ora_global_norm_clip": (C.c_float, [_p, _p, C.c_int, C.c_float]),
             "ora_fused_step": (C.c_int, [_p, C.c_int, _p, _p, _p, _p, _i64, _p]),
             "ora_set_threads": (None, [C.c_int]), "ora_get_threads": (C.c_int, []),
+            "ora_fp4_single_encode": (None, [C.c_int, C.c_float, C.c_int, C.c_uint64, _p, _p]),
+            "ora_fp4_single_decode": (C.c_float, [C.c_int, C.c_uint8, C.c_uint8]),
         }
         for t in ("f32", "f64"):
             sig[f"ora_sgd_step_{t}"] = (None, [_p, _p, _p, _i64, C.c_double, C.c_double, C.c_double, _p, _p])
@@ -306,6 +308,24 @@ def adagrad_step(p, g, acc, lr, eps=1e-10, wd=0.0, f64=False):
     getattr(lib(), f"ora_adagrad_step_{'f64' if f64 else 'f32'}")(
         _ptr(p), _ptr(g), _ptr(acc), p.size, lr, eps, wd, _ptr(op), _ptr(oa))
     return op, oa
+
+
+def fp4_single_encode(kind, x, seeds=None):
+    """(values, scales) of MXFP4/NVFP4.from_float32[_stochastic] per element."""
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    vals, scs = np.zeros(x.size, np.uint8), np.zeros(x.size, np.uint8)
+    v, sc = C.c_uint8(), C.c_uint8()
+    f = lib().ora_fp4_single_encode
+    for i in range(x.size):
+        f(kind, float(x[i]), 0 if seeds is None else 1, 0 if seeds is None else int(seeds[i]), C.byref(v),
+          C.byref(sc))
+        vals[i], scs[i] = v.value, sc.value
+    return vals, scs
+
+
+def fp4_single_decode(kind, values, scales):
+    f = lib().ora_fp4_single_decode
+    return np.array([f(kind, int(a), int(b)) for a, b in zip(values, scales)], np.float32)
 
 
 # ---- fused step over a model ----

@@ -212,3 +212,39 @@ def test_exact_division_shortcut(ody):
             i = bad[:5].tolist()
             pytest.fail(f"{bad.numel()} mismatches, e.g. x={x[i].tolist()} s={s[i].tolist()} "
                         f"fast={fast[i].tolist()} ieee={ieee[i].tolist()}")
+
+
+@pytest.mark.parametrize("fmt", ["mxfp4", "nvfp4"])
+def test_fp4_singles_bit_exact(ody, oracle, fmt):
+    """MXFP4/NVFP4.from_float32, from_float32_stochastic and to_float32 per
+    value (mxfp4.mojo:303-491, nvfp4.mojo:290-481) against the oracle: codes
+    and scale bytes bit for bit over magnitudes from subnormal to the float
+    maximum, zeros of both signs, NaN and Inf, and seeds over the full 64
+    bits (the LCG uses their low 32)."""
+    rng = np.random.default_rng(11)
+    n = 20000
+    x = (np.exp2(rng.uniform(-149, 127.9, n)) * rng.choice([-1.0, 1.0], n)).astype(np.float32)
+    x[:2000] = (rng.standard_normal(2000) * 3).astype(np.float32)
+    x[2000:2010] = [0.0, -0.0, np.nan, np.inf, -np.inf, 1.25, -1.25, 6.0, 0.5, 3.4e38]
+    seeds = rng.integers(0, 2**63, n, dtype=np.int64).astype(np.uint64) * np.uint64(2) + np.uint64(1)
+    kind = ody.MXFP4.kind if fmt == "mxfp4" else ody.NVFP4.kind
+    cls = ody.MXFP4 if fmt == "mxfp4" else ody.NVFP4
+    for sd in (None, seeds):
+        v, s = cls.from_float32(x) if sd is None else cls.from_float32_stochastic(x, sd)
+        ov, os_ = oracle.fp4_single_encode(kind, x, sd)
+        np.testing.assert_array_equal(v, ov)
+        np.testing.assert_array_equal(s, os_)
+        d = cls.to_float32(v, s)
+        od = oracle.fp4_single_decode(kind, v, s)
+        np.testing.assert_array_equal(d.view(np.uint32), od.view(np.uint32))
+
+
+def test_fp4_single_stochastic_is_unbiased(ody):
+    """from_float32_stochastic: 1.25 between 1.0 and 1.5 rounds up about half
+    the time over many seeds (mxfp4.mojo:361-366)."""
+    n = 100000
+    seeds = np.arange(n, dtype=np.uint64) * np.uint64(2654435761)
+    v, s = ody.MXFP4.from_float32_stochastic(np.full(n, 1.25, np.float32), seeds)
+    d = ody.MXFP4.to_float32(v, s)
+    assert set(np.unique(d).tolist()) <= {1.0, 1.5}
+    assert abs(d.mean() - 1.25) < 0.01

@@ -362,3 +362,35 @@ def test_dp_single_rank_matches_plain(oracle, graph):
         np.testing.assert_array_equal(a.get_quant(i).data, b.get_quant(i).data)
     a.close()
     b.close()
+
+
+def test_reference_checkpoint_layout_resume(oracle, tmp_path):
+    """Save a running context in the reference's checkpoint layout, load it
+    into a fresh context, and continue: identical to the uninterrupted run."""
+    from odyssey_b200 import MixedPrecisionStep
+    from odyssey_b200 import checkpoint as ck
+    wl = W.resnet18()
+    kw = wl.step_kwargs()
+    names = [f"p{i}" for i in range(len(wl.numels))]
+    a = MixedPrecisionStep(wl.numels, **kw)
+    for i, m in enumerate(wl.master(0)):
+        a.set_master(i, m)
+
+    def run(ctx, steps, t0):
+        for s in steps:
+            for i, g in enumerate(wl.grads(s)):
+                ctx.set_grad(i, g)
+            ctx.step(t0 + s)
+
+    run(a, range(2), 1)
+    ck.save_checkpoint(a, str(tmp_path), names, wl.shapes, epoch=1, step=2)
+    b = MixedPrecisionStep(wl.numels, **kw)
+    assert ck.load_checkpoint(b, str(tmp_path), names) == (1, 2)
+    assert b.scaler_state == a.scaler_state
+    run(a, range(2, 4), 1)
+    run(b, range(2, 4), 1)
+    for i in range(len(wl.numels)):
+        np.testing.assert_array_equal(a.master(i), b.master(i))
+        np.testing.assert_array_equal(a.get_quant(i).data, b.get_quant(i).data)
+    a.close()
+    b.close()

@@ -776,6 +776,19 @@ static int step_graph(ody_ctx* c, const OptConsts& oc, const DecideParams& dp) {
   return ODY_OK;
 }
 
+// the data-parallel buffers and peer mappings (also after a failed attach)
+static void dp_release(ody_ctx* c) {
+  for (void* p : c->dp_opened) cudaIpcCloseMemHandle(p);
+  c->dp_opened.clear();
+  void* dpb[] = {c->dp_buf, (void*)c->d_peers, c->bar_send, c->bar_recv};
+  for (void* b : dpb)
+    if (b) cudaFree(b);
+  c->dp_buf = nullptr;
+  c->d_peers = nullptr;
+  c->bar_send = c->bar_recv = nullptr;
+  c->dp_on = false;
+}
+
 extern "C" int ody_ctx_dp_attach(ody_ctx* c) {
   if (!c) return fail(ODY_ERR_ARG, "null context");
   if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
@@ -783,6 +796,7 @@ extern "C" int ody_ctx_dp_attach(ody_ctx* c) {
   if (c->dp_on) return ctx_fail(c, ODY_ERR_STATE, "data-parallel gradients already attached");
   if (c->world > 8) return ctx_fail(c, ODY_ERR_ARG, "data-parallel gradients support at most 8 ranks");
   ODY_CUDA(cudaSetDevice(c->cfg.device));
+  dp_release(c);  // what a failed earlier attempt left
   const int nt = (int)c->specs.size();
   const size_t esz = dtype_size(c->gdt);
   c->dp_off.assign(nt, 0);
@@ -1238,10 +1252,7 @@ extern "C" void ody_ctx_destroy(ody_ctx* c) {
     if (b) cudaFree(b);
   for (auto& e : c->tev) cudaEventDestroy(e);
   drop_graph(c);
-  for (void* p : c->dp_opened) cudaIpcCloseMemHandle(p);
-  void* dpb[] = {c->dp_buf, (void*)c->d_peers, c->bar_send, c->bar_recv};
-  for (void* b : dpb)
-    if (b) cudaFree(b);
+  dp_release(c);
   if (c->h_dec) cudaFreeHost(c->h_dec);
   if (c->done) cudaEventDestroy(c->done);
   if (c->stream) cudaStreamDestroy(c->stream);

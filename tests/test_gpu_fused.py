@@ -394,3 +394,19 @@ def test_reference_checkpoint_layout_resume(oracle, tmp_path):
         np.testing.assert_array_equal(a.get_quant(i).data, b.get_quant(i).data)
     a.close()
     b.close()
+
+
+def test_dp_attach_errors():
+    """Data-parallel gradients: a second attach is refused, and the buffer
+    kind is refused before an attach."""
+    from odyssey_b200 import MixedPrecisionStep, OdysseyError
+    from odyssey_b200 import _lib as L
+    ctx = MixedPrecisionStep([100, 37], grad_dtype="bfloat16", optimizer="adamw")
+    with pytest.raises(OdysseyError, match="not attached"):
+        ctx.set_dp_grad(0, np.zeros(100, np.uint16))
+    ctx.dp_attach()
+    with pytest.raises(OdysseyError, match="already attached"):
+        ctx.dp_attach()
+    ctx.set_dp_grad(1, np.ones(37, np.uint16))
+    np.testing.assert_array_equal(ctx.download(L.BUF_DP_GRAD, 1), np.ones(37, np.uint16))
+    ctx.close()

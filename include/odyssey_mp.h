@@ -309,6 +309,21 @@ int ody_quantize(int32_t kind, const void* src, int32_t src_dtype, int64_t n, vo
  * 69-92,211-235,369-494): n float32 values out. */
 int ody_dequantize(int32_t kind, const void* q, int64_t n, float tensor_scale, float* out);
 
+/* Per-format entry points of the two calls above (same arguments without
+ * the kind; the per-tensor-scaled kinds keep the generic calls). */
+int ody_quant_mxfp4(const void* src, int32_t src_dtype, int64_t n, void* out);   /* AnyTensor.to_mxfp4 (any_tensor.mojo:2237-2302) */
+int ody_quant_nvfp4(const void* src, int32_t src_dtype, int64_t n, void* out);   /* AnyTensor.to_nvfp4 (any_tensor.mojo:2329-2401) */
+int ody_quant_fp8_e4m3(const void* src, int32_t src_dtype, int64_t n, void* out);   /* AnyTensor.to_fp8 (any_tensor.mojo:1946) */
+int ody_quant_fp8_e5m2(const void* src, int32_t src_dtype, int64_t n, void* out);   /* AnyTensor.to_bf8 (any_tensor.mojo:2165) */
+int ody_quant_fp16(const void* src, int32_t src_dtype, int64_t n, void* out);   /* update_model_from_master to FP16 (mixed_precision.mojo:299-354) */
+int ody_quant_bf16(const void* src, int32_t src_dtype, int64_t n, void* out);   /* update_model_from_master to BF16 */
+int ody_dequant_mxfp4(const void* q, int64_t n, float* out);   /* from_mxfp4 (tensor_dtype_conv.mojo:369-430) */
+int ody_dequant_nvfp4(const void* q, int64_t n, float* out);   /* from_nvfp4 (tensor_dtype_conv.mojo:433-494) */
+int ody_dequant_fp8_e4m3(const void* q, int64_t n, float* out);   /* from_fp8 (tensor_dtype_conv.mojo:69-92) */
+int ody_dequant_fp8_e5m2(const void* q, int64_t n, float* out);   /* from_bf8 (tensor_dtype_conv.mojo:211-235) */
+int ody_dequant_fp16(const void* q, int64_t n, float* out);   /* the exact FP16 -> float32 upcast */
+int ody_dequant_bf16(const void* q, int64_t n, float* out);   /* the exact BF16 -> float32 upcast */
+
 #ifdef __cplusplus
 }
 #endif

@@ -103,6 +103,18 @@ _SIGS = {
     "ody_adamw_step": (C.c_int, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p]),
     "ody_lion_step": (C.c_int, [_p, _p, _p, _i64] + [C.c_double] * 4 + [_p, _p]),
     "ody_fp4_single_encode": (C.c_int, [_i32, _p, _i64, _p, _p, _p]),
+    "ody_quant_mxfp4": (C.c_int, [_p, _i32, _i64, _p]),
+    "ody_dequant_mxfp4": (C.c_int, [_p, _i64, _p]),
+    "ody_quant_nvfp4": (C.c_int, [_p, _i32, _i64, _p]),
+    "ody_dequant_nvfp4": (C.c_int, [_p, _i64, _p]),
+    "ody_quant_fp8_e4m3": (C.c_int, [_p, _i32, _i64, _p]),
+    "ody_dequant_fp8_e4m3": (C.c_int, [_p, _i64, _p]),
+    "ody_quant_fp8_e5m2": (C.c_int, [_p, _i32, _i64, _p]),
+    "ody_dequant_fp8_e5m2": (C.c_int, [_p, _i64, _p]),
+    "ody_quant_fp16": (C.c_int, [_p, _i32, _i64, _p]),
+    "ody_dequant_fp16": (C.c_int, [_p, _i64, _p]),
+    "ody_quant_bf16": (C.c_int, [_p, _i32, _i64, _p]),
+    "ody_dequant_bf16": (C.c_int, [_p, _i64, _p]),
     "ody_fp4_single_decode": (C.c_int, [_i32, _p, _p, _i64, _p]),
     "ody_rmsprop_step": (C.c_int, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p]),
     "ody_adagrad_step": (C.c_int, [_p, _p, _p, _i64] + [C.c_double] * 3 + [_p, _p]),

@@ -1604,6 +1604,44 @@ extern "C" int ody_fp4_single_decode(int32_t kind, const uint8_t* values, const 
   return ODY_OK;
 }
 
+// per-format entry points over ody_quantize / ody_dequantize
+extern "C" int ody_quant_mxfp4(const void* src, int32_t sdt, int64_t n, void* out) {
+  return ody_quantize(ODY_Q_MXFP4, src, sdt, n, out, nullptr);
+}
+extern "C" int ody_dequant_mxfp4(const void* q, int64_t n, float* out) {
+  return ody_dequantize(ODY_Q_MXFP4, q, n, 1.0f, out);
+}
+extern "C" int ody_quant_nvfp4(const void* src, int32_t sdt, int64_t n, void* out) {
+  return ody_quantize(ODY_Q_NVFP4, src, sdt, n, out, nullptr);
+}
+extern "C" int ody_dequant_nvfp4(const void* q, int64_t n, float* out) {
+  return ody_dequantize(ODY_Q_NVFP4, q, n, 1.0f, out);
+}
+extern "C" int ody_quant_fp8_e4m3(const void* src, int32_t sdt, int64_t n, void* out) {
+  return ody_quantize(ODY_Q_FP8_E4M3, src, sdt, n, out, nullptr);
+}
+extern "C" int ody_dequant_fp8_e4m3(const void* q, int64_t n, float* out) {
+  return ody_dequantize(ODY_Q_FP8_E4M3, q, n, 1.0f, out);
+}
+extern "C" int ody_quant_fp8_e5m2(const void* src, int32_t sdt, int64_t n, void* out) {
+  return ody_quantize(ODY_Q_FP8_E5M2, src, sdt, n, out, nullptr);
+}
+extern "C" int ody_dequant_fp8_e5m2(const void* q, int64_t n, float* out) {
+  return ody_dequantize(ODY_Q_FP8_E5M2, q, n, 1.0f, out);
+}
+extern "C" int ody_quant_fp16(const void* src, int32_t sdt, int64_t n, void* out) {
+  return ody_quantize(ODY_Q_FP16, src, sdt, n, out, nullptr);
+}
+extern "C" int ody_dequant_fp16(const void* q, int64_t n, float* out) {
+  return ody_dequantize(ODY_Q_FP16, q, n, 1.0f, out);
+}
+extern "C" int ody_quant_bf16(const void* src, int32_t sdt, int64_t n, void* out) {
+  return ody_quantize(ODY_Q_BF16, src, sdt, n, out, nullptr);
+}
+extern "C" int ody_dequant_bf16(const void* q, int64_t n, float* out) {
+  return ody_dequantize(ODY_Q_BF16, q, n, 1.0f, out);
+}
+
 // Test hook (not part of include/odyssey_mp.h): the exact-division shortcut
 // used by the per-tensor-scaled requant against IEEE division, on device
 // arrays of n (x, s) pairs.

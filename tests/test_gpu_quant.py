@@ -248,3 +248,23 @@ def test_fp4_single_stochastic_is_unbiased(ody):
     d = ody.MXFP4.to_float32(v, s)
     assert set(np.unique(d).tolist()) <= {1.0, 1.5}
     assert abs(d.mean() - 1.25) < 0.01
+
+
+@pytest.mark.parametrize("fmt,kind", [("mxfp4", 6), ("nvfp4", 7), ("fp8_e4m3", 3), ("fp8_e5m2", 4), ("fp16", 1),
+                                      ("bf16", 2)])
+def test_per_format_entry_points(ody, oracle, fmt, kind):
+    """ody_quant_<fmt> / ody_dequant_<fmt> equal the generic calls and the oracle."""
+    x = _mixed(5000, 21)
+    lib = ody.lib()
+    out = np.zeros(ody._lib.quant_bytes(kind, x.size), np.uint8)
+    ody._lib.check(getattr(lib, f"ody_quant_{fmt}")(x.ctypes.data, 0, x.size, out.ctypes.data))
+    ref, _ = _gpu_quant(ody, kind, x)
+    np.testing.assert_array_equal(out, ref)
+    ora = np.zeros(oracle.quant_bytes(kind, x.size), np.uint8)
+    oracle.lib().ora_quantize(kind, x.ctypes.data, x.size, ora.ctypes.data)
+    np.testing.assert_array_equal(out, ora[: out.size])
+    back = np.zeros(x.size, np.float32)
+    ody._lib.check(getattr(lib, f"ody_dequant_{fmt}")(out.ctypes.data, x.size, back.ctypes.data))
+    oback = np.zeros(x.size, np.float32)
+    oracle.lib().ora_dequantize(kind, ora.ctypes.data, x.size, 1.0, oback.ctypes.data)
+    np.testing.assert_array_equal(back.view(np.uint32), oback.view(np.uint32))

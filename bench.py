@@ -64,6 +64,8 @@ def make_workload(name, ntensors):
     wl = W.lenet() if name == "lenet" else W.resnet18()
     wl.inf_every = 0
     return wl
+
+
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes per param of one apply_kernel launch, measured with ncu
 # (dram__bytes_read.sum + dram__bytes_write.sum of the 8-tensor case
@@ -206,6 +208,178 @@ def run_reference(args, rank, world):
     return 0
 
 
+# ---- the standalone quantiser -------------------
+# name: (kind, side, source dtype, bytes read+written per element by the
+# quantiser's kernels: source read (twice with the amax pre-pass of the
+# per-tensor scale) + codes written)
+QUANT_WORKLOADS = {
+    "mxfp4": dict(kind=6, side=4096, sdt="float32", bytes_per_elem=4 + 17 / 32,
+                  name="mxfp4_4096x4096_f32_outliers (configs[1])"),
+    "nvfp4": dict(kind=8, side=8192, sdt="bfloat16", bytes_per_elem=2 + 2 + 9 / 16,
+                  name="nvfp4_tensor_scaled_8192x8192_bf16_outliers (configs[2])"),
+}
+QUANT_METRIC = "standalone quantiser: elements/s & HBM GB/s (% of peak)"
+
+
+def _quant_input(spec, seed, device):
+    """N(0,1) with 0.1 % of positions x100; bfloat16 N(0, 0.02^2)
+    with 0.05 % x50; positions drawn without replacement."""
+    import torch
+    n = spec["side"] ** 2
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    if spec["kind"] == 6:
+        x = torch.randn(n, device=device, generator=g)
+        idx = torch.randperm(n, device=device, generator=g)[: n // 1000]
+        x[idx] *= 100.0
+        return x
+    x = torch.randn(n, device=device, generator=g) * 0.02
+    idx = torch.randperm(n, device=device, generator=g)[: n * 5 // 10000]
+    x[idx] *= 50.0
+    return x.to(torch.bfloat16)
+
+
+def _quant_cpu_sample(spec, x_host, seconds):
+    """The oracle's quantiser (all host threads) over the same tensor."""
+    from oracle import oracle as O
+    O.build()
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    if spec["sdt"] == "bfloat16":
+        x32 = (x_host.view(np.uint16).astype(np.uint32) << np.uint32(16)).view(np.float32)
+    else:
+        x32 = x_host
+    out = np.zeros(O.quant_bytes(spec["kind"], x32.size), np.uint8)
+    O.lib().ora_quantize(spec["kind"], x32.ctypes.data, x32.size, out.ctypes.data)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        O.lib().ora_quantize(spec["kind"], x32.ctypes.data, x32.size, out.ctypes.data)
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {"value": x32.size / sec, "unit": "elems/s", "cores": threads, "kind": "port",
+            "sample": f"the whole tensor ({x32.size} elements), {len(times)} runs, median {sec * 1e3:.1f} ms, "
+                      f"{threads} OpenMP threads on {cpu_info()[0]}"}
+
+
+def run_quant(args):
+    """the standalone quantiser on one GPU per rank
+    (replicas: each rank quantises its own copy; no collective)."""
+    spec = QUANT_WORKLOADS[args.workload]
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    n = spec["side"] ** 2
+    config = {"workload": spec["name"], "elements": n, "source_dtype": GDT_SHORT[spec["sdt"]],
+              "kind": args.workload + ("_tensor" if spec["kind"] == 8 else ""),
+              "parallelism": f"replicas x{world}",
+              "l2": "L2 flushed (256 MB write) before every timed launch, outside its events"}
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        import torch
+        x = _quant_input(spec, 7, "cpu")
+        xh = (x.view(torch.int16).numpy().view(np.uint16) if spec["sdt"] == "bfloat16" else x.numpy())
+        cb = _quant_cpu_sample(spec, xh, max(3.0, min(30.0, 2.0 * args.steps)))
+        print(json.dumps({"metric": QUANT_METRIC, "impl": "reference", "value": cb["value"], "unit": "elems/s",
+                          "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": n / cb["value"] * 1e3, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                          "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "elems/s",
+                                                      "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return 0
+    import torch
+    import torch.distributed as dist
+    from odyssey_b200 import _lib as L
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("gloo")
+    kind = spec["kind"]
+    x = _quant_input(spec, 7 + rank, "cuda")
+    qb = L.quant_bytes(kind, n)
+    out = torch.empty(qb, dtype=torch.uint8, device="cuda")
+    ts = torch.zeros(1, dtype=torch.float32, device="cuda")
+    scratch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    sdt = L.F32 if spec["sdt"] == "float32" else L.BF16
+    lib = L.lib()
+    scaled = kind == 8
+
+    def launch():
+        L.check(lib.ody_quantize_on_stream(kind, x.data_ptr(), sdt, n, out.data_ptr(),
+                                           ts.data_ptr() if scaled else None,
+                                           scratch.data_ptr() if scaled else None, stream.cuda_stream))
+
+    for _ in range(max(args.warmup, 3)):
+        launch()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        for _ in range(20):  # load while the clock sampler starts
+            launch()
+        for e0, e1 in evs:
+            flush.fill_(1)
+            e0.record(stream)
+            launch()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    # end to end through the public API: pinned host source -> device ->
+    # quantise -> codes back to pinned host memory, on one stream
+    esz = 4 if sdt == L.F32 else 2
+    hx = torch.empty(n * esz, dtype=torch.uint8, pin_memory=True)
+    hx.copy_(x.view(torch.uint8).cpu())
+    hout = torch.empty(qb, dtype=torch.uint8, pin_memory=True)
+    xb = x.view(torch.uint8)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for it in range(4):
+        if it == 1:
+            e0.record(stream)
+        xb.copy_(hx, non_blocking=True)
+        launch()
+        hout.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / 3
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        xh = hx.numpy().view(np.float32 if sdt == L.F32 else np.uint16)
+        cb = _quant_cpu_sample(spec, xh, 12.0)
+    if rank == 0:
+        peak, peak_kind = peaks()
+        gbs = spec["bytes_per_elem"] * n / (ms * 1e-3) / 1e9
+        line = {"metric": QUANT_METRIC, "value": world * n / (ms * 1e-3), "unit": "elems/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "roofline": {"kernel": "quantize_kernel" + (" + amax_kernel" if scaled else ""), "bound": "hbm",
+                             "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                             "peak_source": peak_kind, "alg_bytes_per_launch": spec["bytes_per_elem"] * n,
+                             "traffic": None},
+                "e2e": {"value": world * n / (e2e_ms * 1e-3), "unit": "elems/s", "ms_per_step": e2e_ms,
+                        "h2d_bytes_per_step": n * esz, "d2h_bytes_per_step": qb},
+                "gpu_launches": args.steps * (2 if scaled else 1), "clocks": clk.summary()}
+        if cb:
+            line["cpu_baseline"] = cb
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 GDT_SHORT = {"float32": "f32", "float16": "f16", "bfloat16": "bf16"}
 QUANT = "nvfp4_tensor"
 
@@ -246,9 +420,12 @@ def main():
                     help="data-parallel gradients: every rank holds full-model gradients and each step first "
                          "reduce-scatters them, fused with pass 1 (fused) or by ncclReduceScatter (nccl, "
                          "for comparison); none = gradients already reduced (the headline)")
-    ap.add_argument("--workload", default="flat1b", choices=["flat1b", "resnet18", "lenet"],
-                    help="flat1b = the headline 1B model; resnet18 / lenet = secondary lines")
+    ap.add_argument("--workload", default="flat1b", choices=["flat1b", "resnet18", "lenet", "mxfp4", "nvfp4"],
+                    help="flat1b = the headline 1B model; resnet18 / lenet = secondary step lines; mxfp4 / "
+                         "nvfp4 = the standalone quantiser on configs[1] / configs[2]")
     args = ap.parse_args()
+    if args.workload in QUANT_WORKLOADS:
+        return run_quant(args)
     global NT, TOTAL, WORKLOAD, QUANT, ALG_BYTES_STEP, ALG_BYTES_UPDATE
     WORKLOAD, NT = args.workload, args.tensors
     wl = make_workload(WORKLOAD, NT)

@@ -309,6 +309,15 @@ int ody_quantize(int32_t kind, const void* src, int32_t src_dtype, int64_t n, vo
  * 69-92,211-235,369-494): n float32 values out. */
 int ody_dequantize(int32_t kind, const void* q, int64_t n, float tensor_scale, float* out);
 
+/* The same two operations stream-ordered on device memory only: no staging,
+ * no synchronisation (for quantising inside a CUDA pipeline).  For the
+ * per-tensor-scaled kinds, tensor_scale (device float, written) and
+ * amax_scratch (device, 4 bytes, reset by the call) are required; else both
+ * may be NULL.  stream NULL is the legacy default stream. */
+int ody_quantize_on_stream(int32_t kind, const void* src, int32_t src_dtype, int64_t n, void* out,
+                           float* tensor_scale, uint32_t* amax_scratch, void* stream);
+int ody_dequantize_on_stream(int32_t kind, const void* q, int64_t n, const float* tensor_scale, float* out,
+                             void* stream);
 /* Per-format entry points of the two calls above (same arguments without
  * the kind; the per-tensor-scaled kinds keep the generic calls). */
 int ody_quant_mxfp4(const void* src, int32_t src_dtype, int64_t n, void* out);   /* AnyTensor.to_mxfp4 (any_tensor.mojo:2237-2302) */

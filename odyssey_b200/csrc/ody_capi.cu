@@ -1548,6 +1548,42 @@ extern "C" int ody_quantize(int32_t kind, const void* src, int32_t sdt, int64_t 
   return ODY_OK;
 }
 
+extern "C" int ody_quantize_on_stream(int32_t kind, const void* src, int32_t sdt, int64_t n, void* out,
+                                      float* tensor_scale, uint32_t* amax_scratch, void* stream) {
+  if (kind <= ODY_Q_NONE || kind > ODY_Q_NVFP4_TENSOR)
+    return fail(ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(kind));
+  if (sdt != DT_F32 && sdt != DT_BF16) return fail(ODY_ERR_DTYPE, "quantize source must be float32 or bfloat16");
+  if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot quantize an empty tensor");
+  if (!src || !out) return fail(ODY_ERR_ARG, "null pointer");
+  const bool scaled = kind == ODY_Q_NVFP4_TENSOR || kind == ODY_Q_FP8_E4M3_TENSOR;
+  if (scaled && (!tensor_scale || !amax_scratch))
+    return fail(ODY_ERR_ARG, "per-tensor-scaled kinds need tensor_scale and amax_scratch");
+  if (!is_device_ptr(src) || !is_device_ptr(out) || (tensor_scale && !is_device_ptr(tensor_scale)) ||
+      (amax_scratch && !is_device_ptr(amax_scratch)))
+    return fail(ODY_ERR_ARG, "ody_quantize_on_stream takes device memory only");
+  current_device_tables();
+  cudaStream_t st = (cudaStream_t)stream;
+  if (scaled) {
+    ODY_CUDA(cudaMemsetAsync(amax_scratch, 0, 4, st));
+    ODY_CUDA(launch_amax(sdt, src, n, amax_scratch, st));
+  }
+  ODY_CUDA(launch_quantize(kind, sdt, src, n, (uint8_t*)out, scaled ? amax_scratch : nullptr,
+                           scaled ? tensor_scale : nullptr, st));
+  return ODY_OK;
+}
+
+extern "C" int ody_dequantize_on_stream(int32_t kind, const void* q, int64_t n, const float* tensor_scale,
+                                        float* out, void* stream) {
+  if (kind <= ODY_Q_NONE || kind > ODY_Q_NVFP4_TENSOR)
+    return fail(ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(kind));
+  if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot dequantize an empty tensor");
+  if (!q || !out) return fail(ODY_ERR_ARG, "null pointer");
+  if (!is_device_ptr(q) || !is_device_ptr(out) || (tensor_scale && !is_device_ptr(tensor_scale)))
+    return fail(ODY_ERR_ARG, "ody_dequantize_on_stream takes device memory only");
+  ODY_CUDA(launch_dequantize(kind, (const uint8_t*)q, n, tensor_scale, out, (cudaStream_t)stream));
+  return ODY_OK;
+}
+
 extern "C" int ody_dequantize(int32_t kind, const void* q, int64_t n, float ts, float* out) {
   if (kind <= ODY_Q_NONE || kind > ODY_Q_NVFP4_TENSOR)
     return fail(ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(kind));

@@ -268,3 +268,31 @@ def test_per_format_entry_points(ody, oracle, fmt, kind):
     oback = np.zeros(x.size, np.float32)
     oracle.lib().ora_dequantize(kind, ora.ctypes.data, x.size, 1.0, oback.ctypes.data)
     np.testing.assert_array_equal(back.view(np.uint32), oback.view(np.uint32))
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_quantize_on_stream_matches(ody, kind):
+    """ody_quantize_on_stream / ody_dequantize_on_stream (device memory,
+    stream-ordered) equal the synchronous calls."""
+    import torch
+    x = _mixed(70001, 31)
+    ref, ts_ref = _gpu_quant(ody, kind, x)
+    dx = torch.from_numpy(x).cuda()
+    out = torch.zeros(ref.size, dtype=torch.uint8, device="cuda")
+    ts = torch.zeros(1, dtype=torch.float32, device="cuda")
+    scratch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    ody._lib.check(ody.lib().ody_quantize_on_stream(kind, dx.data_ptr(), 0, x.size, out.data_ptr(), ts.data_ptr(),
+                                                     scratch.data_ptr(), st))
+    back = torch.zeros(x.size, dtype=torch.float32, device="cuda")
+    ody._lib.check(ody.lib().ody_dequantize_on_stream(kind, out.data_ptr(), x.size, ts.data_ptr(), back.data_ptr(),
+                                                       st))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+    assert ts.item() == np.float32(ts_ref) or kind not in (5, 8)
+    hb = np.zeros(x.size, np.float32)
+    ody._lib.check(ody.lib().ody_dequantize(kind, ref.ctypes.data, x.size, ts_ref, hb.ctypes.data))
+    np.testing.assert_array_equal(back.cpu().numpy().view(np.uint32), hb.view(np.uint32))
+    with pytest.raises(ody.OdysseyError, match="device memory only"):
+        ody._lib.check(ody.lib().ody_quantize_on_stream(kind, x.ctypes.data, 0, x.size, out.data_ptr(),
+                                                         ts.data_ptr(), scratch.data_ptr(), st))

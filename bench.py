@@ -321,8 +321,13 @@ def run_quant(args):
         dist.barrier()
     torch.cuda.synchronize()
     with Clocks(local) as clk:
-        for _ in range(20):  # load while the clock sampler starts
-            launch()
+        # about a second of back-to-back launches while the clock sampler
+        # (200 ms period) starts, then the timed launches
+        w0 = time.perf_counter()
+        while time.perf_counter() - w0 < 1.0:
+            for _ in range(50):
+                launch()
+            torch.cuda.synchronize()
         for e0, e1 in evs:
             flush.fill_(1)
             e0.record(stream)

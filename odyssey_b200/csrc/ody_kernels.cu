@@ -1196,7 +1196,18 @@ __device__ __forceinline__ void load_src8(int sdt, const void* x, int64_t n, int
 __global__ void amax_kernel(int sdt, const void* x, int64_t n, uint32_t* out) {
   float am = 0.0f;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x * 8;
-  for (int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; e0 < n; e0 += stride) {
+  int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  // four groups of 8 in flight per thread
+  for (; e0 + 3 * stride < n; e0 += 4 * stride) {
+    float v[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; u++) load_src8(sdt, x, n, e0 + u * stride, v[u]);
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int k = 0; k < 8; k++) am = amax_acc(am, v[u][k]);
+  }
+  for (; e0 < n; e0 += stride) {
     float v[8];
     load_src8(sdt, x, n, e0, v);
 #pragma unroll
@@ -1227,19 +1238,43 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, int sdt, c
                                                             const uint32_t* amax, float* tscale) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
+  __shared__ Fp4Thr s_cx[kCxCount];
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
-  load_thr_smem(s_mx, s_nv);
+  // only the table this format reads
+  if (kind == Q_MXFP4) {
+    float* d = reinterpret_cast<float*>(s_mx);
+    const float* g = reinterpret_cast<const float*>(g_thr_mx);
+    for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) d[i] = g[i];
+  } else if (kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
+    float* d = reinterpret_cast<float*>(s_nv);
+    const float* g = reinterpret_cast<const float*>(g_thr_nv);
+    for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x) d[i] = g[i];
+  }
   __syncthreads();
   const bool scaled = (kind == Q_NVFP4_TENSOR || kind == Q_FP8_E4M3_TENSOR);
   const float s = scaled ? tensor_scale_from_amax(kind, *amax) : 1.0f;
   const float r = __frcp_rn(s);
   if (blockIdx.x == 0 && threadIdx.x == 0 && tscale) *tscale = s;
+  if (kind == Q_NVFP4_TENSOR) {
+    // composite thresholds for s (see stage_nvfp4_tensor): compares of the
+    // raw values, one division per block
+    float* cx = reinterpret_cast<float*>(s_cx);
+    const float* q = reinterpret_cast<const float*>(s_nv);
+    for (int i = threadIdx.x; i < kCxCount * 8; i += blockDim.x)
+      cx[i] = (i & 7) == 7 ? 0.0f : composite_threshold(q[kCxFirst * 8 + i], s);
+    __syncthreads();
+  }
   const int64_t ntiles = (n + kTile - 1) / kTile;
+  // the next tile's values are loaded before this tile is encoded
+  float nx[8];
+  if ((int64_t)blockIdx.x < ntiles) load_src8(sdt, x, n, (int64_t)blockIdx.x * kTile + (int64_t)threadIdx.x * kVec, nx);
   for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
     const int64_t e0 = t * kTile + (int64_t)threadIdx.x * kVec;
     float v[8];
-    load_src8(sdt, x, n, e0, v);
-    if (scaled) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) v[k] = nx[k];
+    if (t + gridDim.x < ntiles) load_src8(sdt, x, n, e0 + (int64_t)gridDim.x * kTile, nx);
+    if (kind == Q_FP8_E4M3_TENSOR) {
 #pragma unroll
       for (int k = 0; k < 8; k++) v[k] = div_by(v[k], s, r);
     }
@@ -1252,7 +1287,10 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, int sdt, c
         const int64_t off = t * kMxTileBytes + w * kMxWarpBytes;
         flush_warp<true>(ws, out + off, out_bytes - off);
       } else {
-        stage_fp4<false>(v, ws, s_nv);
+        if (kind == Q_NVFP4_TENSOR)
+          stage_nvfp4_tensor(v, ws, s_nv, s_cx, s);
+        else
+          stage_fp4<false>(v, ws, s_nv);
         __syncwarp();
         const int64_t off = t * kNvTileBytes + w * kNvWarpBytes;
         flush_warp<false>(ws, out + off, out_bytes - off);
@@ -1299,7 +1337,7 @@ static int64_t quant_bytes_dev(int kind, int64_t n) {
 cudaError_t launch_quantize(int kind, int sdt, const void* x, int64_t n, uint8_t* out,
                             const uint32_t* amax, float* tscale, cudaStream_t st) {
   int64_t ntiles = (n + kTile - 1) / kTile;
-  int64_t cap = (int64_t)sm_count() * 6;
+  int64_t cap = (int64_t)sm_count() * 8;
   int grid = (int)(ntiles < cap ? ntiles : cap);
   if (grid < 1) grid = 1;
   quantize_kernel<<<grid, kThreads, 0, st>>>(kind, sdt, x, n, out, quant_bytes_dev(kind, n), amax,

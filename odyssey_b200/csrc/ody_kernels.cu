@@ -1227,23 +1227,15 @@ static int sm_count() {
 cudaError_t launch_amax(int sdt, const void* x, int64_t n, uint32_t* amax, cudaStream_t st) {
   int64_t groups = (n + 7) / 8;
   int64_t want = (groups + kThreads - 1) / kThreads;
-  int per = 1;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, amax_kernel, kThreads, 0);
-  const int64_t cap = (int64_t)sm_count() * (per > 0 ? per : 1);  // one wave
-  int grid = (int)(want < cap ? want : cap);
+  int grid = (int)(want < (int64_t)sm_count() * 8 ? want : (int64_t)sm_count() * 8);
   if (grid < 1) grid = 1;
   amax_kernel<<<grid, kThreads, 0, st>>>(sdt, x, n, amax);
   return cudaGetLastError();
 }
 
-// SDT: the source dtype (float32 or bfloat16).  G tiles' raw loads (64 bytes
-// per thread) are issued before the first of them is encoded.
-template <int SDT>
-__global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, const void* x, int64_t n, uint8_t* out,
-                                                            int64_t out_bytes, const uint32_t* amax,
-                                                            float* tscale) {
-  constexpr int sdt = SDT;
-  constexpr int G = SDT == DT_F32 ? 2 : 4;
+__global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, int sdt, const void* x, int64_t n,
+                                                            uint8_t* out, int64_t out_bytes,
+                                                            const uint32_t* amax, float* tscale) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
   __shared__ Fp4Thr s_cx[kCxCount];
@@ -1273,75 +1265,50 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, const void
     __syncthreads();
   }
   const int64_t ntiles = (n + kTile - 1) / kTile;
-  const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
-  for (int64_t t0 = blockIdx.x; t0 < ntiles; t0 += (int64_t)G * gridDim.x) {
-    uint4 raw[G][2];  // the second half only for float32
+  // the next tile's values are loaded before this tile is encoded
+  float nx[8];
+  if ((int64_t)blockIdx.x < ntiles) load_src8(sdt, x, n, (int64_t)blockIdx.x * kTile + (int64_t)threadIdx.x * kVec, nx);
+  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int64_t e0 = t * kTile + (int64_t)threadIdx.x * kVec;
+    float v[8];
 #pragma unroll
-    for (int u = 0; u < G; u++) {
-      const int64_t e0 = (t0 + (int64_t)u * gridDim.x) * kTile + (int64_t)threadIdx.x * kVec;
-      if (aligned && e0 + 8 <= n) {
-        const uint4* p = SDT == DT_F32 ? reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(x) + e0)
-                                       : reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + e0);
-        raw[u][0] = __ldcs(p);
-        if (SDT == DT_F32) raw[u][1] = __ldcs(p + 1);
-      }
+    for (int k = 0; k < 8; k++) v[k] = nx[k];
+    if (t + gridDim.x < ntiles) load_src8(sdt, x, n, e0 + (int64_t)gridDim.x * kTile, nx);
+    if (kind == Q_FP8_E4M3_TENSOR) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) v[k] = div_by(v[k], s, r);
     }
-#pragma unroll
-    for (int u = 0; u < G; u++) {
-      const int64_t t = t0 + (int64_t)u * gridDim.x;
-      if (t >= ntiles) break;
-      const int64_t e0 = t * kTile + (int64_t)threadIdx.x * kVec;
-      float v[8];
-      if (aligned && e0 + 8 <= n) {
-        if (SDT == DT_F32) {
-          const uint4 a = raw[u][0], b = raw[u][1];
-          v[0] = __uint_as_float(a.x); v[1] = __uint_as_float(a.y); v[2] = __uint_as_float(a.z);
-          v[3] = __uint_as_float(a.w); v[4] = __uint_as_float(b.x); v[5] = __uint_as_float(b.y);
-          v[6] = __uint_as_float(b.z); v[7] = __uint_as_float(b.w);
-        } else {
-          const uint32_t w[4] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w};
-#pragma unroll
-          for (int k = 0; k < 8; k++) v[k] = bf16_bits_to_f32((uint16_t)(w[k >> 1] >> ((k & 1) * 16)));
-        }
-      } else {
-        load_src8(sdt, x, n, e0, v);
-      }
-      if (kind == Q_FP8_E4M3_TENSOR) {
-#pragma unroll
-        for (int k = 0; k < 8; k++) v[k] = div_by(v[k], s, r);
-      }
-      if (kind == Q_MXFP4 || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
-        const int w = threadIdx.x >> 5;
-        uint8_t* ws = stage + w * kWarpStage;
-        if (kind == Q_MXFP4) {
-          stage_fp4<true>(v, ws, s_mx);
-          __syncwarp();
-          const int64_t off = t * kMxTileBytes + w * kMxWarpBytes;
-          flush_warp<true>(ws, out + off, out_bytes - off);
-        } else {
-          if (kind == Q_NVFP4_TENSOR)
-            stage_nvfp4_tensor(v, ws, s_nv, s_cx, s);
-          else
-            stage_fp4<false>(v, ws, s_nv);
-          __syncwarp();
-          const int64_t off = t * kNvTileBytes + w * kNvWarpBytes;
-          flush_warp<false>(ws, out + off, out_bytes - off);
-        }
+    if (kind == Q_MXFP4 || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
+      const int w = threadIdx.x >> 5;
+      uint8_t* ws = stage + w * kWarpStage;
+      if (kind == Q_MXFP4) {
+        stage_fp4<true>(v, ws, s_mx);
         __syncwarp();
+        const int64_t off = t * kMxTileBytes + w * kMxWarpBytes;
+        flush_warp<true>(ws, out + off, out_bytes - off);
       } else {
-        const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
-        const int qk = kind == Q_FP8_E4M3_TENSOR ? Q_FP8_E4M3 : kind;
-        uint8_t* dst = out + e0 * esz;
-        if (e0 + 8 <= n && (reinterpret_cast<uintptr_t>(dst) & (esz == 2 ? 15u : 7u)) == 0) {
-          store_elem8(qk, v, dst);
-        } else {
-          for (int k = 0; k < 8 && e0 + k < n; k++) {
-            if (esz == 2) {
-              uint16_t h = qk == Q_FP16 ? f32_to_f16_bits(v[k]) : f32_to_bf16_bits(v[k]);
-              reinterpret_cast<uint16_t*>(out)[e0 + k] = h;
-            } else {
-              out[e0 + k] = qk == Q_FP8_E5M2 ? f32_to_e5m2(v[k]) : f32_to_e4m3(v[k]);
-            }
+        if (kind == Q_NVFP4_TENSOR)
+          stage_nvfp4_tensor(v, ws, s_nv, s_cx, s);
+        else
+          stage_fp4<false>(v, ws, s_nv);
+        __syncwarp();
+        const int64_t off = t * kNvTileBytes + w * kNvWarpBytes;
+        flush_warp<false>(ws, out + off, out_bytes - off);
+      }
+      __syncwarp();
+    } else {
+      const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
+      const int qk = kind == Q_FP8_E4M3_TENSOR ? Q_FP8_E4M3 : kind;
+      uint8_t* dst = out + e0 * esz;
+      if (e0 + 8 <= n && (reinterpret_cast<uintptr_t>(dst) & (esz == 2 ? 15u : 7u)) == 0) {
+        store_elem8(qk, v, dst);
+      } else {
+        for (int k = 0; k < 8 && e0 + k < n; k++) {
+          if (esz == 2) {
+            uint16_t h = qk == Q_FP16 ? f32_to_f16_bits(v[k]) : f32_to_bf16_bits(v[k]);
+            reinterpret_cast<uint16_t*>(out)[e0 + k] = h;
+          } else {
+            out[e0 + k] = qk == Q_FP8_E5M2 ? f32_to_e5m2(v[k]) : f32_to_e4m3(v[k]);
           }
         }
       }
@@ -1369,20 +1336,12 @@ static int64_t quant_bytes_dev(int kind, int64_t n) {
 
 cudaError_t launch_quantize(int kind, int sdt, const void* x, int64_t n, uint8_t* out,
                             const uint32_t* amax, float* tscale, cudaStream_t st) {
-  // one wave of resident CTAs
   int64_t ntiles = (n + kTile - 1) / kTile;
-  int per = 1;
-  if (sdt == DT_F32)
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, quantize_kernel<DT_F32>, kThreads, 0);
-  else
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, quantize_kernel<DT_BF16>, kThreads, 0);
-  int64_t cap = (int64_t)sm_count() * (per > 0 ? per : 1);
+  int64_t cap = (int64_t)sm_count() * 8;
   int grid = (int)(ntiles < cap ? ntiles : cap);
   if (grid < 1) grid = 1;
-  if (sdt == DT_F32)
-    quantize_kernel<DT_F32><<<grid, kThreads, 0, st>>>(kind, x, n, out, quant_bytes_dev(kind, n), amax, tscale);
-  else
-    quantize_kernel<DT_BF16><<<grid, kThreads, 0, st>>>(kind, x, n, out, quant_bytes_dev(kind, n), amax, tscale);
+  quantize_kernel<<<grid, kThreads, 0, st>>>(kind, sdt, x, n, out, quant_bytes_dev(kind, n), amax,
+                                             tscale);
   return cudaGetLastError();
 }
 

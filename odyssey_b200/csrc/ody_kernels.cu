@@ -639,7 +639,8 @@ __device__ __forceinline__ void stage_fp4(const float v[8], uint8_t* ws, const F
   am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
   if (MX) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
   const uint8_t e = MX ? e8m0_from_f32(block_scale_value(am)) : e4m3_scale_from_f32(block_scale_value(am));
-  const float* t = thr[e].t;
+  float t[8];
+  thr_load(&thr[e], t);
   const bool z = !MX && e == 0;
   const bool special = z || (MX && e == 255) || any_nonfinite8(v);
   const int lane = threadIdx.x & 31;
@@ -770,12 +771,14 @@ __device__ __forceinline__ void stage_nvfp4_tensor(const float x[8], uint8_t* ws
   const int lane = threadIdx.x & 31;
   uint8_t* dst = ws + (lane >> 1) * 9 + 4 * (lane & 1);
   if (!special) {
-    const float* t = thr_x[e - kCxFirst].t;
+    float t[8];
+    thr_load(&thr_x[e - kCxFirst], t);
 #pragma unroll
     for (int i = 0; i < 4; i++)
       dst[i] = (uint8_t)((fp4_encode_plain(x[2 * i], t) << 4) | fp4_encode_plain(x[2 * i + 1], t));
   } else {
-    const float* t = thr_q[e].t;
+    float t[8];
+    thr_load(&thr_q[e], t);
 #pragma unroll
     for (int i = 0; i < 4; i++)
       dst[i] = (uint8_t)((fp4_encode(__fdiv_rn(x[2 * i], st), t, z) << 4) |

@@ -187,9 +187,18 @@ __device__ __forceinline__ float amax_acc(float acc, float x) { return fmaxf(acc
 // thr[0] = least |x| with RN(|x|/s) > 0 (decides the sign bit of tiny
 // negatives), thr[1..6] = X_T for T = 0.5, 1.25, 1.75, 2.5, 3.5, 5.0.
 // A threshold of NaN means "never" (scale = +inf).
-struct Fp4Thr {
+struct __align__(16) Fp4Thr {
   float t[8];
 };
+
+// one table entry into registers with two 128-bit loads (scalar loads of
+// entries e*8 + k from shared memory hit only 4 bank groups across a warp)
+__device__ __forceinline__ void thr_load(const Fp4Thr* p, float t[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p->t)[0];
+  const float4 b = reinterpret_cast<const float4*>(p->t)[1];
+  t[0] = a.x; t[1] = a.y; t[2] = a.z; t[3] = a.w;
+  t[4] = b.x; t[5] = b.y; t[6] = b.z; t[7] = b.w;
+}
 
 __device__ __forceinline__ uint32_t fp4_encode(float x, const float* thr, bool scale_zero) {
   const float a = fabsf(x);

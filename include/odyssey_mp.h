@@ -42,7 +42,7 @@ extern "C" {
 #define ODY_F16 1
 #define ODY_BF16 2
 
-/* ---- optimizers (src/odyssey/training/optimizers/*.mojo) ------------------ */
+/* ---- optimizers (src/odyssey/training/optimizers/<name>.mojo) ------------- */
 #define ODY_SGD 0      /* sgd.mojo */
 #define ODY_ADAM 1     /* adam.mojo */
 #define ODY_ADAMW 2    /* adamw.mojo */

@@ -135,14 +135,15 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
         _lib.lib()
 
 
-def test_c_caller(L, tmp_path):
-    """tests/abi_check.c: the header and library used from plain C (gcc),
-    host-only entry points and error paths."""
+@pytest.mark.parametrize("compiler", [["gcc", "-std=c11"], ["g++", "-x", "c++", "-std=c++17"]])
+def test_c_caller(L, tmp_path, compiler):
+    """tests/abi_check.c: the header and library used from plain C (gcc) and
+    C++ (g++), host-only entry points and error paths."""
     exe = tmp_path / "abi_check"
     libdir = os.path.dirname(L.LIB_PATH)
-    cc = subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
-                         os.path.join(ROOT, "tests", "abi_check.c"), "-o", str(exe), "-L", libdir,
-                         "-l:" + os.path.basename(L.LIB_PATH), f"-Wl,-rpath,{libdir}"],
+    cc = subprocess.run(compiler + ["-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                                    os.path.join(ROOT, "tests", "abi_check.c"), "-o", str(exe), "-L", libdir,
+                                    "-l:" + os.path.basename(L.LIB_PATH), f"-Wl,-rpath,{libdir}"],
                         capture_output=True, text=True)
     assert cc.returncode == 0, cc.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)

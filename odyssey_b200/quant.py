@@ -53,27 +53,58 @@ def dequantize(q):
     return out
 
 
+def _reference_source(x, dtype, method):
+    """The source checks of AnyTensor.to_fp8/to_bf8/to_mxfp4/to_nvfp4
+    (tensor_dtype_conv.mojo:21-36 and 259-279): bfloat16 is rejected,
+    float16/float32/float64 are accepted (float64 rounded to float32 as the
+    reference's .cast[DType.float32] does), anything else is rejected."""
+    bf16 = dtype in ("bfloat16", L.BF16)
+    name = None
+    if L.is_torch(x):
+        name = str(x.dtype).replace("torch.", "")
+        bf16 = bf16 or name == "bfloat16"
+    else:
+        name = np.asarray(x).dtype.name
+    if bf16:
+        raise L.OdysseyError(f"{method} does not support bfloat16: the bfloat16 conversion path does not correctly "
+                             "round-trip through the Float32 intermediate representation", L.ERR_DTYPE)
+    if dtype is None and name == "float64":
+        return x.float() if L.is_torch(x) else np.asarray(x, np.float32)
+    if dtype is None and name not in ("float16", "float32"):
+        raise L.OdysseyError(f"{method} requires a floating-point tensor", L.ERR_DTYPE)
+    return x
+
+
 def to_fp8(x, dtype=None):
-    return quantize(x, L.Q_FP8_E4M3, dtype)
+    """AnyTensor.to_fp8 (any_tensor.mojo:1946-2002): float16/32/64 sources."""
+    return quantize(_reference_source(x, dtype, "to_fp8()"), L.Q_FP8_E4M3, dtype)
 
 
 def to_bf8(x, dtype=None):
-    return quantize(x, L.Q_FP8_E5M2, dtype)
+    """AnyTensor.to_bf8 (any_tensor.mojo:2165-2220): float16/32/64 sources."""
+    return quantize(_reference_source(x, dtype, "to_bf8()"), L.Q_FP8_E5M2, dtype)
 
 
 def to_fp8_tensor_scaled(x, dtype=None):
+    """Extension: FP8 E4M3 with a per-tensor scale; bfloat16 sources are
+    accepted (upcast exactly)."""
     return quantize(x, L.Q_FP8_E4M3_TENSOR, dtype)
 
 
 def to_mxfp4(x, dtype=None):
-    return quantize(x, L.Q_MXFP4, dtype)
+    """AnyTensor.to_mxfp4 (any_tensor.mojo:2237-2302): float16/32/64 sources."""
+    return quantize(_reference_source(x, dtype, "to_mxfp4()"), L.Q_MXFP4, dtype)
 
 
 def to_nvfp4(x, dtype=None):
-    return quantize(x, L.Q_NVFP4, dtype)
+    """AnyTensor.to_nvfp4 (any_tensor.mojo:2329-2401): float16/32/64 sources;
+    bfloat16 through quantize() or to_nvfp4_tensor_scaled (extensions)."""
+    return quantize(_reference_source(x, dtype, "to_nvfp4()"), L.Q_NVFP4, dtype)
 
 
 def to_nvfp4_tensor_scaled(x, dtype=None):
+    """Extension: NVFP4 with a per-tensor scale; bfloat16 sources are
+    accepted (upcast exactly)."""
     return quantize(x, L.Q_NVFP4_TENSOR, dtype)
 
 

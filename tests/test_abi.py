@@ -148,3 +148,21 @@ def test_c_caller(L, tmp_path, compiler):
     assert cc.returncode == 0, cc.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and run.stdout.strip() == "ok", run.stdout + run.stderr
+
+
+def test_reference_source_checks_of_to_family():
+    """AnyTensor.to_fp8/to_bf8/to_mxfp4/to_nvfp4 reject bfloat16 and
+    non-float sources with the reference's messages
+    (tests/odyssey/tensor/test_fp8_bf8_conversion.mojo:18-116,
+    tensor_dtype_conv.mojo:21-36,259-279); checked before any device work."""
+    import torch
+    from odyssey_b200 import OdysseyError, to_bf8, to_fp8, to_mxfp4, to_nvfp4
+    for fn, name in ((to_fp8, "to_fp8()"), (to_bf8, "to_bf8()"), (to_mxfp4, "to_mxfp4()"),
+                     (to_nvfp4, "to_nvfp4()")):
+        with pytest.raises(OdysseyError, match=re.escape(f"{name} does not support bfloat16: the bfloat16 "
+                                                         "conversion path does not correctly round-trip")):
+            fn(torch.zeros(2, 3, dtype=torch.bfloat16))
+        with pytest.raises(OdysseyError, match="does not support bfloat16"):
+            fn(np.zeros(6, np.uint16), dtype="bfloat16")
+        with pytest.raises(OdysseyError, match=re.escape(f"{name} requires a floating-point tensor")):
+            fn(np.zeros(6, np.int32))

@@ -296,3 +296,14 @@ def test_quantize_on_stream_matches(ody, kind):
     with pytest.raises(ody.OdysseyError, match="device memory only"):
         ody._lib.check(ody.lib().ody_quantize_on_stream(kind, x.ctypes.data, 0, x.size, out.data_ptr(),
                                                          ts.data_ptr(), scratch.data_ptr(), st))
+
+
+def test_to_family_float64_and_float16_sources(ody, oracle):
+    """to_fp8/to_mxfp4 accept float64 (rounded to float32, the reference's
+    .cast[DType.float32]) and float16 (exact upcast) sources."""
+    x64 = np.random.default_rng(4).standard_normal(5000) * 3.0
+    x32 = x64.astype(np.float32)
+    np.testing.assert_array_equal(ody.to_fp8(x64).data, ody.to_fp8(x32).data)
+    np.testing.assert_array_equal(ody.to_mxfp4(x64).data, oracle.quantize(6, x32)[0])
+    x16 = x32.astype(np.float16)
+    np.testing.assert_array_equal(ody.to_bf8(x16).data, oracle.quantize(4, x16.astype(np.float32))[0])

@@ -111,6 +111,10 @@ def to_nvfp4_tensor_scaled(x, dtype=None):
 def _from(q, kind, block, what):
     if isinstance(q, QuantizedTensor):
         return dequantize(q)
+    # tensor_dtype_conv.mojo:78-79, 227-228, 380-385, 444-449
+    is_u8 = str(q.dtype) == "torch.uint8" if L.is_torch(q) else np.asarray(q).dtype == np.uint8
+    if not is_u8:
+        raise L.OdysseyError(f"from_{what.lower()}() requires a uint8 tensor ({what}-encoded)", L.ERR_DTYPE)
     nbytes = L.numel(q)
     if block and nbytes % block:
         raise L.OdysseyError(f"{what} tensor size must be multiple of {block} bytes", L.ERR_SHAPE)

@@ -166,3 +166,17 @@ def test_reference_source_checks_of_to_family():
             fn(np.zeros(6, np.uint16), dtype="bfloat16")
         with pytest.raises(OdysseyError, match=re.escape(f"{name} requires a floating-point tensor")):
             fn(np.zeros(6, np.int32))
+
+
+def test_reference_checks_of_from_family():
+    """from_fp8/from_bf8/from_mxfp4/from_nvfp4 source checks
+    (tensor_dtype_conv.mojo:78-79,227-228,380-385,444-449)."""
+    from odyssey_b200 import OdysseyError, from_bf8, from_fp8, from_mxfp4, from_nvfp4
+    for fn, what in ((from_fp8, "FP8"), (from_bf8, "BF8"), (from_mxfp4, "MXFP4"), (from_nvfp4, "NVFP4")):
+        with pytest.raises(OdysseyError, match=re.escape(f"from_{what.lower()}() requires a uint8 tensor "
+                                                         f"({what}-encoded)")):
+            fn(np.zeros(18, np.float32))
+    with pytest.raises(OdysseyError, match="MXFP4 tensor size must be multiple of 17 bytes"):
+        from_mxfp4(np.zeros(18, np.uint8))
+    with pytest.raises(OdysseyError, match="NVFP4 tensor size must be multiple of 9 bytes"):
+        from_nvfp4(np.zeros(10, np.uint8))

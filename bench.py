@@ -152,13 +152,14 @@ def cpu_info():
     return model, os.cpu_count()
 
 
-def cpu_reference_sample(seconds=12.0, ntensors=1, quant="nvfp4_tensor"):
+def cpu_reference_sample(seconds=12.0, ntensors=1, quant="nvfp4_tensor", threads=None):
     """The oracle (CPU restatement of the reference path) on the host cores:
     the workload's step (for the 1B model over `ntensors` of its 4096x4096
-    tensors; the smaller models whole), repeated for about `seconds`."""
+    tensors; the smaller models whole), repeated for about `seconds`, on all
+    host threads or on `threads`."""
     from oracle import oracle as O
     O.build()
-    threads = os.cpu_count() or 1
+    threads = threads or os.cpu_count() or 1
     O.set_threads(threads)
     wl = make_workload(WORKLOAD, ntensors)
     gdt = {"float32": O.F32, "float16": O.F16, "bfloat16": O.BF16}[wl.grad_dtype]
@@ -194,10 +195,19 @@ def cpu_reference_sample(seconds=12.0, ntensors=1, quant="nvfp4_tensor"):
                       f"median {sec * 1e3:.3f} ms/step, {threads} OpenMP threads on {cpu_info()[0]}"}
 
 
+def with_single_thread(cb, sample):
+    """Adds the one-thread figure (the reference's path is single-threaded)
+    to an all-threads CPU baseline."""
+    cb["single_thread"] = {"value": sample["value"], "unit": sample["unit"], "cores": 1,
+                           "sample": sample["sample"]}
+    return cb
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
     cb = cpu_reference_sample(seconds=max(3.0, min(30.0, 2.0 * args.steps)), quant=QUANT)
+    with_single_thread(cb, cpu_reference_sample(seconds=8.0, quant=QUANT, threads=1))
     line = {"metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "params/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": TOTAL / cb["value"] * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
@@ -239,11 +249,12 @@ def _quant_input(spec, seed, device):
     return x.to(torch.bfloat16)
 
 
-def _quant_cpu_sample(spec, x_host, seconds):
-    """The oracle's quantiser (all host threads) over the same tensor."""
+def _quant_cpu_sample(spec, x_host, seconds, threads=None):
+    """The oracle's quantiser (all host threads, or `threads`) over the same
+    tensor."""
     from oracle import oracle as O
     O.build()
-    threads = os.cpu_count() or 1
+    threads = threads or os.cpu_count() or 1
     O.set_threads(threads)
     if spec["sdt"] == "bfloat16":
         x32 = (x_host.view(np.uint16).astype(np.uint32) << np.uint32(16)).view(np.float32)
@@ -281,7 +292,8 @@ def run_quant(args):
         import torch
         x = _quant_input(spec, 7, "cpu")
         xh = (x.view(torch.int16).numpy().view(np.uint16) if spec["sdt"] == "bfloat16" else x.numpy())
-        cb = _quant_cpu_sample(spec, xh, max(3.0, min(30.0, 2.0 * args.steps)))
+        cb = with_single_thread(_quant_cpu_sample(spec, xh, max(3.0, min(30.0, 2.0 * args.steps))),
+                                _quant_cpu_sample(spec, xh, 5.0, threads=1))
         print(json.dumps({"metric": QUANT_METRIC, "impl": "reference", "value": cb["value"], "unit": "elems/s",
                           "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                           "ms_per_step": n / cb["value"] * 1e3, "higher_is_better": True, "scaling": "weak",
@@ -365,7 +377,7 @@ def run_quant(args):
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         xh = hx.numpy().view(np.float32 if sdt == L.F32 else np.uint16)
-        cb = _quant_cpu_sample(spec, xh, 12.0)
+        cb = with_single_thread(_quant_cpu_sample(spec, xh, 12.0), _quant_cpu_sample(spec, xh, 5.0, threads=1))
     if rank == 0:
         peak, peak_kind = peaks()
         gbs = spec["bytes_per_elem"] * n / (ms * 1e-3) / 1e9
@@ -645,7 +657,8 @@ def main():
         step_gbs_gpu = ALG_BYTES_STEP * nloc / (ms_step * 1e-3) / 1e9
         cb = None
         if world == 1 and not args.no_cpu_baseline:
-            cb = cpu_reference_sample(quant=QUANT)
+            cb = with_single_thread(cpu_reference_sample(quant=QUANT),
+                                    cpu_reference_sample(seconds=8.0, quant=QUANT, threads=1))
         line = {
             "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",

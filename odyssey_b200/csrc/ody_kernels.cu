@@ -624,10 +624,41 @@ __device__ __forceinline__ bool any_nonfinite8(const float v[8]) {
   return z != z;
 }
 
+// Exact division x / s with s's reciprocal r = RN(1/s) precomputed: the
+// product estimate is corrected once with the exactly computed remainder
+// (Markstein's correction: q0 = x*r is within one ulp, x - q0*s is exact by
+// FMA, and q0 + rem*r rounded once is the correctly rounded quotient when r
+// is the correctly rounded reciprocal, provided nothing under- or overflows:
+// the remainder is a multiple of about ulp(x) * 2^-24, exact only while |x|
+// stays above 2^-100).  Zero, non-finite and extreme magnitudes take the
+// IEEE division.
+__device__ __forceinline__ float div_by(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float q = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
+  const float aq = fabsf(q0), ax = fabsf(x);
+  return (aq >= 0x1p-125f && aq <= 0x1p+125f && ax >= 0x1p-100f && ax <= 0x1p+125f) ? q : __fdiv_rn(x, s);
+}
+
+// Block scale value amax / 6 (block_scale_value) through the exact
+// reciprocal division.
+__device__ __forceinline__ float block_scale_value_fast(float amax) {
+  float v = div_by(amax, 6.0f, __frcp_rn(6.0f));
+  if (v < 1e-10f) v = 1.0f;
+  return v;
+}
+
 // the threshold ladder without special cases (finite x, positive finite scale)
+// t[1..6] are sorted (a "never" threshold is NaN and sits at the top, where
+// a >= NaN is false as for +Inf), so the count of t[1..6] at or below |x| is
+// found with three compares: t[3], then t[5] or t[2], then t[6], t[4] or t[1].
+// The magnitude code counts t[1] twice (code 1 is never produced).
 __device__ __forceinline__ uint32_t fp4_encode_plain(float x, const float* t) {
   const float a = fabsf(x);
-  const uint32_t mag = 2u * (a >= t[1]) + (a >= t[2]) + (a >= t[3]) + (a >= t[4]) + (a >= t[5]) + (a >= t[6]);
+  const bool s1 = a >= t[3];
+  const bool s2 = a >= (s1 ? t[5] : t[2]);
+  const uint32_t base = s1 ? (s2 ? 5u : 3u) : (s2 ? 1u : 0u);
+  const uint32_t c = base + (a >= (s1 ? (s2 ? t[6] : t[4]) : t[1]));
+  const uint32_t mag = c + (c != 0u);
   return ((uint32_t)((x < 0.0f) && (a >= t[0])) << 3) | mag;
 }
 
@@ -638,7 +669,7 @@ __device__ __forceinline__ void stage_fp4(const float v[8], uint8_t* ws, const F
   for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
   am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
   if (MX) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-  const uint8_t e = MX ? e8m0_from_f32(block_scale_value(am)) : e4m3_scale_from_f32(block_scale_value(am));
+  const uint8_t e = MX ? e8m0_from_f32(block_scale_value_fast(am)) : e4m3_scale_from_f32(block_scale_value_fast(am));
   float t[8];
   thr_load(&thr[e], t);
   const bool z = !MX && e == 0;
@@ -677,21 +708,6 @@ __device__ __forceinline__ void flush_warp(const uint8_t* ws, uint8_t* dst, int6
     const int m = (int)(limit < nbytes ? (limit > 0 ? limit : 0) : nbytes);
     for (int i = lane; i < m; i += 32) dst[i] = ws[i];
   }
-}
-
-// Exact division x / s with s's reciprocal r = RN(1/s) precomputed: the
-// product estimate is corrected once with the exactly computed remainder
-// (Markstein's correction: q0 = x*r is within one ulp, x - q0*s is exact by
-// FMA, and q0 + rem*r rounded once is the correctly rounded quotient when r
-// is the correctly rounded reciprocal, provided nothing under- or overflows:
-// the remainder is a multiple of about ulp(x) * 2^-24, exact only while |x|
-// stays above 2^-100).  Zero, non-finite and extreme magnitudes take the
-// IEEE division.
-__device__ __forceinline__ float div_by(float x, float s, float r) {
-  const float q0 = __fmul_rn(x, r);
-  const float q = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
-  const float aq = fabsf(q0), ax = fabsf(x);
-  return (aq >= 0x1p-125f && aq <= 0x1p+125f && ax >= 0x1p-100f && ax <= 0x1p+125f) ? q : __fdiv_rn(x, s);
 }
 
 __device__ __forceinline__ void store_elem8(int kind, const float v[8], uint8_t* dst) {
@@ -759,13 +775,13 @@ __device__ __forceinline__ float composite_threshold(float Q, float s) {
 // values x (s_t > 0 finite); blocks with a non-finite element, an infinite
 // q amax or a zero block scale divide element by element as the reference does
 __device__ __forceinline__ void stage_nvfp4_tensor(const float x[8], uint8_t* ws, const Fp4Thr* thr_q,
-                                                   const Fp4Thr* thr_x, float st) {
+                                                   const Fp4Thr* thr_x, float st, float rst) {
   float am = 0.0f;
 #pragma unroll
   for (int k = 0; k < 8; k++) am = amax_acc(am, x[k]);
   am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-  const float amq = __fdiv_rn(am, st);
-  const uint8_t e = e4m3_scale_from_f32(block_scale_value(amq));
+  const float amq = div_by(am, st, rst);
+  const uint8_t e = e4m3_scale_from_f32(block_scale_value_fast(amq));
   const bool z = e == 0;
   const bool special = e < kCxFirst || amq == __uint_as_float(0x7f800000u) || any_nonfinite8(x);
   const int lane = threadIdx.x & 31;
@@ -1023,7 +1039,7 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
         const int64_t tile_in_tensor = (tb - td.off) / kTile;
         const int w = threadIdx.x >> 5;
         uint8_t* ws = stage + w * kWarpStage;
-        stage_nvfp4_tensor(x, ws, s_nv, s_cx, s);
+        stage_nvfp4_tensor(x, ws, s_nv, s_cx, s, r);
         __syncwarp();
         flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
         __syncwarp();
@@ -1291,7 +1307,7 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, int sdt, c
         flush_warp<true>(ws, out + off, out_bytes - off);
       } else {
         if (kind == Q_NVFP4_TENSOR)
-          stage_nvfp4_tensor(v, ws, s_nv, s_cx, s);
+          stage_nvfp4_tensor(v, ws, s_nv, s_cx, s, r);
         else
           stage_fp4<false>(v, ws, s_nv);
         __syncwarp();

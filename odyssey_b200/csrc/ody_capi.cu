@@ -411,7 +411,7 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   for (int i = 0; i < nt; i++) numels[i] = c->specs[i].numel;
   ody_plan_shards(numels.data(), nt, world, c->owner.data());
   c->local_of.assign(nt, -1);
-  // chunk length: 8 tiles, halved while the model would give fewer than four
+  // chunk length: 32 tiles, halved while the model would give fewer than four
   // chunks per resident apply CTA (small models spread over more CTAs
   // instead of walking long chunks tile by tile)
   int64_t chunk = kChunk;

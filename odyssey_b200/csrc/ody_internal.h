@@ -17,7 +17,7 @@ namespace ody {
 constexpr int kThreads = 256;
 constexpr int kVec = 8;
 constexpr int kTile = kThreads * kVec;  // 2048 elements
-constexpr int kChunk = 8 * kTile;       // 16384 elements per chunk-table entry
+constexpr int kChunk = 32 * kTile;      // 65536 elements per chunk-table entry (at most)
 constexpr int kPad = 64;                // arena alignment of every tensor (elements)
 constexpr int kMxTileBytes = (kTile / 32) * 17;  // 1088
 constexpr int kNvTileBytes = (kTile / 16) * 9;   // 1152

@@ -97,7 +97,9 @@ typedef struct ody_config {
   int32_t comm_timeout_ms;      /* multi-GPU: bound on every collective wait */
   int32_t reserved0;
   double alpha;                 /* RMSprop smoothing constant (default 0.99) */
-  int32_t reserved[4];
+  int32_t chunk_elems;          /* apply-job chunk length in elements, a multiple of 2048 up to
+                                   65536; 0 (default): chosen from the model size */
+  int32_t reserved[3];
 } ody_config;
 
 /* What one step did (PrecisionConfig.step bookkeeping,

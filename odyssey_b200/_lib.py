@@ -42,7 +42,7 @@ class Config(C.Structure):
         ("growth_factor", C.c_float), ("backoff_factor", C.c_float), ("growth_interval", C.c_int64),
         ("min_scale", C.c_float), ("max_scale", C.c_float), ("clip_enabled", C.c_int32),
         ("max_norm", C.c_float), ("comm_timeout_ms", C.c_int32), ("reserved0", C.c_int32),
-        ("alpha", C.c_double), ("reserved", C.c_int32 * 4),
+        ("alpha", C.c_double), ("chunk_elems", C.c_int32), ("reserved", C.c_int32 * 3),
     ]
 
 

@@ -276,6 +276,9 @@ extern "C" int ody_ctx_create(ody_ctx** out, const ody_config* cfg) {
     return fail(ODY_ERR_ARG, "max_norm must be positive, got: " + std::to_string(cfg->max_norm));
   if (cfg->use_gradient_scaler && cfg->initial_scale == 0.0f)
     return fail(ODY_ERR_ARG, "Cannot unscale with zero scale factor");
+  if (cfg->chunk_elems < 0 || cfg->chunk_elems % kTile != 0 || cfg->chunk_elems > kChunk)
+    return fail(ODY_ERR_ARG, "chunk_elems must be 0 or a multiple of " + std::to_string(kTile) + " up to " +
+                                 std::to_string(kChunk));
   ody_ctx* c = new ody_ctx();
   c->cfg = *cfg;
   if (c->cfg.comm_timeout_ms <= 0) c->cfg.comm_timeout_ms = 60000;
@@ -421,6 +424,7 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
       if (c->owner[i] == rank) nloc += (c->specs[i].numel + kPad - 1) / kPad * kPad;
     const int64_t full = apply_grid(c->gdt, c->cfg.optimizer, c->cfg.device);
     while (chunk > kTile && nloc / chunk < 4 * full) chunk /= 2;
+    if (c->cfg.chunk_elems > 0) chunk = c->cfg.chunk_elems;  // validated at create
   }
   int64_t off = 0, qoff = 0;
   for (int i = 0; i < nt; i++) {

@@ -40,7 +40,7 @@ class MixedPrecisionStep:
                  momentum=0.0, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.0,
                  use_gradient_scaler=True, initial_scale=65536.0, growth_factor=2.0, backoff_factor=0.5,
                  growth_interval=2000, min_scale=1.0, max_scale=65536.0, clip_max_norm=None, device=0,
-                 world_size=1, rank=0, unique_id=None, comm_timeout_ms=60000, alpha=0.99):
+                 world_size=1, rank=0, unique_id=None, comm_timeout_ms=60000, alpha=0.99, chunk_elems=0):
         cfg = L.default_config()
         cfg.optimizer = _OPT[optimizer] if isinstance(optimizer, str) else int(optimizer)
         cfg.device = int(device)
@@ -53,6 +53,7 @@ class MixedPrecisionStep:
         cfg.max_norm = float(clip_max_norm) if clip_max_norm is not None else 1.0
         cfg.comm_timeout_ms = int(comm_timeout_ms)
         cfg.alpha = float(alpha)
+        cfg.chunk_elems = int(chunk_elems)
         self.cfg = cfg
         self.numels = [int(n) for n in numels]
         self.grad_dtype = _GDT[grad_dtype] if isinstance(grad_dtype, str) else int(grad_dtype)

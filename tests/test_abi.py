@@ -180,3 +180,15 @@ def test_reference_checks_of_from_family():
         from_mxfp4(np.zeros(18, np.uint8))
     with pytest.raises(OdysseyError, match="NVFP4 tensor size must be multiple of 9 bytes"):
         from_nvfp4(np.zeros(10, np.uint8))
+
+
+def test_chunk_elems_validation(L):
+    import ctypes as C
+    cfg = L.default_config()
+    ctx = C.c_void_p()
+    for bad in (-2048, 1000, 131072):
+        cfg.chunk_elems = bad
+        assert L.lib().ody_ctx_create(C.byref(ctx), C.byref(cfg)) == L.ERR_ARG
+    cfg.chunk_elems = 4096
+    assert L.lib().ody_ctx_create(C.byref(ctx), C.byref(cfg)) == 0
+    L.lib().ody_ctx_destroy(ctx)

@@ -23,7 +23,7 @@ def ulp_diff(a, b):
     return np.abs(ai - bi)
 
 
-def run_pair(oracle, wl, nsteps, numels=None, quants=None, seed=0, t0=1, check_every=1):
+def run_pair(oracle, wl, nsteps, numels=None, quants=None, seed=0, t0=1, check_every=1, ctx_kwargs=None):
     """Run the same workload through the GPU context and the oracle."""
     from odyssey_b200 import MixedPrecisionStep
     numels = numels or wl.numels
@@ -31,7 +31,7 @@ def run_pair(oracle, wl, nsteps, numels=None, quants=None, seed=0, t0=1, check_e
     if quants is not None:
         kw["quant"] = quants
     qlist = kw["quant"] if isinstance(kw["quant"], list) else [kw["quant"]] * len(numels)
-    ctx = MixedPrecisionStep(numels, **kw)
+    ctx = MixedPrecisionStep(numels, **kw, **(ctx_kwargs or {}))
     specs = [{"numel": n, "grad_dtype": GDT[wl.grad_dtype], "quant": QK[q]} for n, q in zip(numels, qlist)]
     hy = wl.hyper
     sk = {k: kw[k] for k in ("initial_scale", "growth_factor", "backoff_factor", "growth_interval", "min_scale",
@@ -409,4 +409,17 @@ def test_dp_attach_errors():
         ctx.dp_attach()
     ctx.set_dp_grad(1, np.ones(37, np.uint16))
     np.testing.assert_array_equal(ctx.download(L.BUF_DP_GRAD, 1), np.ones(37, np.uint16))
+    ctx.close()
+
+
+@pytest.mark.parametrize("chunk", [65536, 8192])
+def test_long_chunks(oracle, chunk):
+    """Apply jobs of the longest chunk length the 1B model uses (65,536
+    elements; the size rule gives test-sized models short chunks), with a
+    ragged last chunk, against the oracle."""
+    wl = W.Workload("long", [(200000,), (65536 * 2,), (70000,)], "bfloat16", "nvfp4_tensor", "adamw",
+                    dict(learning_rate=1e-3, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.01),
+                    0.02, 1e-3, 4096.0, clip=1.0)
+    ctx, model, res = run_pair(oracle, wl, 3, quants=["nvfp4_tensor", "mxfp4", "fp8_tensor"],
+                               ctx_kwargs={"chunk_elems": chunk})
     ctx.close()

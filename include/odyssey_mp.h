@@ -266,6 +266,18 @@ int ody_global_norm_clip(float* const* grads, const int64_t* numels, int32_t nte
  * the calling thread's default stream and returns after it completes. */
 int ody_global_norm_clip_noalloc(float* const* grads, const int64_t* numels, int32_t ntensors,
                                  float max_norm, float* total_norm);
+/* The two other global-norm clips of the reference, in place on float32
+ * tensors, returning the float64 norm before clipping:
+ *   mode 0: clip_grad_global_norm_ (core/numerical_safety.mojo:760-815):
+ *           float32 squares, no +1e-6, factor max_norm/norm as float32;
+ *   mode 1: clip_global_norm (training/optimizers/optimizer_utils.mojo:
+ *           303-348): float64 squares, each value scaled in float64 and
+ *           rounded to float32.
+ * Both clip only when norm > max_norm and norm > 0; max_norm 0 is allowed.
+ * The float64 sums run in a different order than the reference's serial
+ * loops (same value to ~1e-15 relative). */
+int ody_clip_global_norm_variant(float* const* grads, const int64_t* numels, int32_t ntensors,
+                                 double max_norm, int32_t mode, double* total_norm);
 /* sgd_step (sgd.mojo:27-121); velocity/out_velocity may be NULL when momentum == 0. */
 int ody_sgd_step(const float* params, const float* grads, const float* velocity, int64_t n,
                  double learning_rate, double momentum, double weight_decay, float* out_params,

@@ -10,7 +10,8 @@ to_/from_{fp8,bf8,mxfp4,nvfp4}, plus the fused MixedPrecisionStep.
 """
 from ._lib import LIB_PATH, OdysseyError, lib  # noqa: F401
 from .fused import MixedPrecisionStep, nccl_unique_id, plan_shards  # noqa: F401
-from .gradient_clipping import clip_gradients_by_global_norm, compute_gradient_norm_list  # noqa: F401
+from .gradient_clipping import (clip_global_norm, clip_grad_global_norm_,  # noqa: F401
+                                clip_gradients_by_global_norm, compute_gradient_norm_list)
 from .mixed_precision import (GradientScaler, check_gradients_finite, clip_gradients_by_norm,  # noqa: F401
                               convert_to_fp32_master, update_model_from_master)
 from .optimizers import (adagrad_step, adagrad_step_simple, adam_step, adamw_step,  # noqa: F401

@@ -102,6 +102,7 @@ _SIGS = {
     "ody_adam_step": (C.c_int, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p]),
     "ody_adamw_step": (C.c_int, [_p, _p, _p, _p, _i64, _i64] + [C.c_double] * 5 + [_p, _p, _p]),
     "ody_lion_step": (C.c_int, [_p, _p, _p, _i64] + [C.c_double] * 4 + [_p, _p]),
+    "ody_clip_global_norm_variant": (C.c_int, [_p, _p, _i32, C.c_double, _i32, _p]),
     "ody_fp4_single_encode": (C.c_int, [_i32, _p, _i64, _p, _p, _p]),
     "ody_quantize_on_stream": (C.c_int, [_i32, _p, _i32, _i64, _p, _p, _p, _p]),
     "ody_dequantize_on_stream": (C.c_int, [_i32, _p, _i64, _p, _p, _p]),

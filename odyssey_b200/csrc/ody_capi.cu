@@ -1435,6 +1435,54 @@ extern "C" int ody_global_norm_clip(float* const* grads, const int64_t* numels, 
   return ODY_OK;
 }
 
+extern "C" int ody_clip_global_norm_variant(float* const* grads, const int64_t* numels, int32_t nt,
+                                            double max_norm, int32_t mode, double* total_norm) {
+  if (mode != 0 && mode != 1) return fail(ODY_ERR_ARG, "mode must be 0 or 1");
+  if (max_norm < 0.0) {
+    char buf[64];
+    snprintf(buf, sizeof(buf), "%g", max_norm);
+    return fail(ODY_ERR_ARG, std::string("max_norm must be non-negative, got: ") + buf);
+  }
+  if (nt <= 0) return fail(ODY_ERR_ARG, mode == 0 ? "grads list cannot be empty" : "tensors list cannot be empty");
+  if (!grads || !numels) return fail(ODY_ERR_ARG, "bad argument");
+  Scope S;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int grid = stats_grid(dev);
+  void *part, *ticket, *tot;
+  ODY_CUDA(cudaMallocAsync(&part, sizeof(StatsPartial) * grid, S.st));
+  S.bufs.push_back({nullptr, part, 0, true});
+  ODY_CUDA(cudaMallocAsync(&ticket, 4, S.st));
+  S.bufs.push_back({nullptr, ticket, 0, true});
+  ODY_CUDA(cudaMallocAsync(&tot, 32, S.st));  // total, norm, coef[2]
+  S.bufs.push_back({nullptr, tot, 0, true});
+  double* dtot = (double*)tot;
+  ODY_CUDA(cudaMemsetAsync(ticket, 0, 4, S.st));
+  ODY_CUDA(cudaMemsetAsync(tot, 0, 32, S.st));
+  std::vector<void*> dptr(nt);
+  for (int i = 0; i < nt; i++) {
+    if (numels[i] < 0 || (numels[i] > 0 && !grads[i])) return fail(ODY_ERR_ARG, "bad tensor");
+    ODY_STAGE(S, grads[i], (size_t)numels[i] * 4, true, &dptr[i]);
+    if (numels[i] > 0) {
+      if (mode == 0)
+        ODY_CUDA(launch_sumsq((const float*)dptr[i], numels[i], (StatsPartial*)part, grid, (unsigned*)ticket, dtot,
+                              S.st));
+      else
+        ODY_CUDA(launch_sumsq64((const float*)dptr[i], numels[i], (StatsPartial*)part, grid, (unsigned*)ticket,
+                                dtot, S.st));
+    }
+  }
+  ODY_CUDA(launch_clip_variant_coef(dtot, max_norm, dtot + 1, dtot + 2, S.st));
+  for (int i = 0; i < nt; i++)
+    if (numels[i] > 0) ODY_CUDA(launch_clip_variant_scale((float*)dptr[i], numels[i], dtot + 2, mode, S.st));
+  for (int i = 0; i < nt; i++) ODY_CUDA(S.copy_out(grads[i]));
+  double hn = 0.0;
+  ODY_CUDA(cudaMemcpyAsync(&hn, dtot + 1, 8, cudaMemcpyDeviceToHost, S.st));
+  ODY_CUDA(cudaStreamSynchronize(S.st));
+  if (total_norm) *total_norm = hn;
+  return ODY_OK;
+}
+
 static int opt_common(int opt, const float* p, const float* g, const float* s1, const float* s2, int64_t n,
                       int64_t t, double lr, double mu, double b1, double b2, double eps, double wd, float* op,
                       float* os1, float* os2, double alpha = 0.99) {

@@ -134,6 +134,11 @@ cudaError_t launch_count_nonfinite(int dtype, const void* g, int64_t n,
 cudaError_t launch_sumsq(const float* g, int64_t n, StatsPartial* partials, int grid,
                          unsigned* ticket, double* total, cudaStream_t st);
 cudaError_t launch_scale_inplace(float* g, int64_t n, const float* coef, cudaStream_t st);
+cudaError_t launch_sumsq64(const float* g, int64_t n, StatsPartial* partials, int grid, unsigned* ticket,
+                           double* total, cudaStream_t st);
+cudaError_t launch_clip_variant_coef(const double* total, double max_norm, double* norm_out, double* coef,
+                                     cudaStream_t st);
+cudaError_t launch_clip_variant_scale(float* g, int64_t n, const double* coef, int mode, cudaStream_t st);
 cudaError_t launch_clip_coef(const double* total, float max_norm, float* norm_out,
                              float* coef_out, cudaStream_t st);
 cudaError_t launch_opt_step(int opt, const OptConsts& oc, const float* p, const float* g,

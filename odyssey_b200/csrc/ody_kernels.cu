@@ -1495,6 +1495,10 @@ cudaError_t launch_count_nonfinite(int dt, const void* g, int64_t n, unsigned lo
 
 // sum of float32 squares in float64 (8-element float32 groups, as sq8),
 // per-CTA partials + fixed-order final sum
+// SQ64: squares taken in float64 (optimizer_utils.mojo:189-229); else float32
+// squares reduced per 8 lanes (gradient_clipping.mojo:52-67,
+// numerical_safety.mojo:581-594)
+template <bool SQ64>
 __global__ void sumsq_kernel(const float* g, int64_t n, StatsPartial* partials, unsigned* ticket,
                              double* total) {
   double acc = 0.0;
@@ -1505,7 +1509,12 @@ __global__ void sumsq_kernel(const float* g, int64_t n, StatsPartial* partials, 
     float v[8];
 #pragma unroll
     for (int k = 0; k < 8; k++) v[k] = (i * 8 + k < n) ? g[i * 8 + k] : 0.0f;
-    acc += (double)sq8(v);
+    if (SQ64) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) acc = __dadd_rn(acc, __dmul_rn((double)v[k], (double)v[k]));
+    } else {
+      acc += (double)sq8(v);
+    }
   }
   block_sum2(acc, dummy);
   __shared__ bool last;
@@ -1529,7 +1538,46 @@ __global__ void sumsq_kernel(const float* g, int64_t n, StatsPartial* partials, 
 
 cudaError_t launch_sumsq(const float* g, int64_t n, StatsPartial* partials, int grid, unsigned* ticket,
                          double* total, cudaStream_t st) {
-  sumsq_kernel<<<grid, kThreads, 0, st>>>(g, n, partials, ticket, total);
+  sumsq_kernel<false><<<grid, kThreads, 0, st>>>(g, n, partials, ticket, total);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_sumsq64(const float* g, int64_t n, StatsPartial* partials, int grid, unsigned* ticket,
+                           double* total, cudaStream_t st) {
+  sumsq_kernel<true><<<grid, kThreads, 0, st>>>(g, n, partials, ticket, total);
+  return cudaGetLastError();
+}
+
+// clip_grad_global_norm_ (numerical_safety.mojo:760-815, mode 0) and
+// clip_global_norm (optimizer_utils.mojo:303-348, mode 1): norm =
+// sqrt(sumsq) in float64; when norm > max_norm and norm > 0 the factor is
+// max_norm / norm in float64, applied as a float32 multiplier (mode 0) or as
+// a float64 product rounded back to float32 (mode 1); coef[1] = 1 marks "scale"
+__global__ void clip_variant_coef_kernel(const double* total, double max_norm, double* norm_out, double* coef) {
+  const double norm = __dsqrt_rn(*total);
+  *norm_out = norm;
+  const bool clip = norm > max_norm && norm > 0.0;
+  coef[0] = clip ? __ddiv_rn(max_norm, norm) : 1.0;
+  coef[1] = clip ? 1.0 : 0.0;
+}
+
+__global__ void clip_variant_scale_kernel(float* g, int64_t n, const double* coef, int mode) {
+  if (coef[1] == 0.0) return;
+  const double c = coef[0];
+  const float c32 = __double2float_rn(c);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    g[i] = mode == 0 ? __fmul_rn(g[i], c32) : __double2float_rn(__dmul_rn((double)g[i], c));
+}
+
+cudaError_t launch_clip_variant_coef(const double* total, double max_norm, double* norm_out, double* coef,
+                                     cudaStream_t st) {
+  clip_variant_coef_kernel<<<1, 1, 0, st>>>(total, max_norm, norm_out, coef);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_clip_variant_scale(float* g, int64_t n, const double* coef, int mode, cudaStream_t st) {
+  clip_variant_scale_kernel<<<grid_for(n), kThreads, 0, st>>>(g, n, coef, mode);
   return cudaGetLastError();
 }
 

@@ -29,3 +29,32 @@ def compute_gradient_norm_list(gradients):
     copies = [np.array(g, dtype=np.float32, copy=True) if not L.is_torch(g) else g.float().contiguous().clone()
               for g in gradients]
     return clip_gradients_by_global_norm(copies, float(np.finfo(np.float32).max))
+
+
+def _clip_variant(tensors, max_norm, mode, name):
+    for g in tensors:
+        if L.dtype_code(g) != L.F32:
+            raise L.OdysseyError(f"{name} takes float32 tensors", L.ERR_DTYPE)
+        if (L.is_torch(g) and not g.is_contiguous()) or (not L.is_torch(g) and not g.flags["C_CONTIGUOUS"]):
+            raise L.OdysseyError("tensors must be contiguous (clipped in place)", L.ERR_ARG)
+    n = len(tensors)
+    ptrs = (C.c_void_p * max(n, 1))(*[L.ptr(g) for g in tensors])
+    numels = np.array([L.numel(g) for g in tensors] or [0], np.int64)
+    norm = C.c_double(0.0)
+    L.check(L.lib().ody_clip_global_norm_variant(ptrs, numels.ctypes.data, n, float(max_norm), mode,
+                                                 C.byref(norm)))
+    return norm.value
+
+
+def clip_grad_global_norm_(grads, max_norm):
+    """core/numerical_safety.mojo:760-815: float32 squares, factor
+    max_norm / norm (no +1e-6) applied as a float32 multiplier when
+    norm > max_norm and norm > 0; returns the float64 norm before clipping."""
+    return _clip_variant(grads, max_norm, 0, "clip_grad_global_norm_")
+
+
+def clip_global_norm(tensors, max_norm):
+    """training/optimizers/optimizer_utils.mojo:303-348: float64 squares,
+    each value scaled in float64 and rounded to float32; returns the float64
+    norm before clipping."""
+    return _clip_variant(tensors, max_norm, 1, "clip_global_norm")

@@ -192,3 +192,16 @@ def test_chunk_elems_validation(L):
     cfg.chunk_elems = 4096
     assert L.lib().ody_ctx_create(C.byref(ctx), C.byref(cfg)) == 0
     L.lib().ody_ctx_destroy(ctx)
+
+
+def test_clip_variants_argument_errors():
+    """clip_grad_global_norm_ / clip_global_norm messages
+    (numerical_safety.mojo:775-778, optimizer_utils.mojo:326-329), raised
+    before any device work."""
+    from odyssey_b200 import OdysseyError, clip_global_norm, clip_grad_global_norm_
+    with pytest.raises(OdysseyError, match="max_norm must be non-negative, got: -1"):
+        clip_grad_global_norm_([np.ones(4, np.float32)], -1.0)
+    with pytest.raises(OdysseyError, match="grads list cannot be empty"):
+        clip_grad_global_norm_([], 1.0)
+    with pytest.raises(OdysseyError, match="tensors list cannot be empty"):
+        clip_global_norm([], 1.0)

@@ -1,6 +1,8 @@
 """GPU parity of the single-op entry points (unscale, finite check, global-
 norm clip, SGD / Adam / AdamW / Lion / RMSprop / Adagrad) against the oracle
 and the reference's golden vectors."""
+import math
+
 import numpy as np
 import pytest
 
@@ -180,3 +182,32 @@ def test_master_conversions(ody):
     assert p[0] == 2.0
     with pytest.raises(ody.OdysseyError, match="sizes must match"):
         ody.update_model_from_master(p, np.zeros(3, np.float32))
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_clip_variants(ody, oracle, mode):
+    """clip_grad_global_norm_ (mode 0) and clip_global_norm (mode 1): the
+    norm within float64 summation-order rounding of the reference's, the
+    clipped values bit-exact given that norm, and the reference's example
+    (ones(100), ones(50), max 5 -> norm sqrt(150))."""
+    fn = ody.clip_grad_global_norm_ if mode == 0 else ody.clip_global_norm
+    g = [_rand(1000, 1, 3.0), _rand(37, 2, 0.5), _rand(70001, 3, 0.01)]
+    orig = [x.copy() for x in g]
+    norm = fn(g, 2.0)
+    if mode == 0:
+        ref = math.sqrt(sum(oracle.sumsq_f32(x) for x in orig))
+    else:
+        ref = math.sqrt(sum(float(np.sum(x.astype(np.float64) ** 2)) for x in orig))
+    assert abs(norm - ref) <= 1e-12 * ref
+    for a, o in zip(g, orig):
+        want = o * np.float32(2.0 / norm) if mode == 0 else (o.astype(np.float64) * (2.0 / norm)).astype(np.float32)
+        np.testing.assert_array_equal(a.view(np.uint32), want.astype(np.float32).view(np.uint32))
+    # below the bound: untouched
+    h = [_rand(100, 4, 1e-3)]
+    h0 = h[0].copy()
+    fn(h, 100.0)
+    np.testing.assert_array_equal(h[0], h0)
+    a, b = np.ones(100, np.float32), np.ones(50, np.float32)
+    n = fn([a, b], 5.0)
+    assert n == pytest.approx(math.sqrt(150.0), rel=1e-12)
+    np.testing.assert_allclose(a, 5.0 / math.sqrt(150.0), rtol=1e-6)

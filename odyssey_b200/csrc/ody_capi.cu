@@ -370,33 +370,58 @@ static cudaError_t dalloc(T** p, size_t bytes) {
 // update jobs; what is left runs at the end.  A model of fewer than eight
 // grid-widths of update jobs puts every requant job at the end (measured
 // faster there: its interleaved requant jobs would mostly wait).
-static void build_jobs(ody_ctx* c) {
-  c->jobs.clear();
+// nchunks[i], quant[i]: the local tensors in arena order; W: the apply grid
+static std::vector<uint32_t> plan_jobs(const std::vector<int>& nchunks, const std::vector<int>& quant, size_t W) {
+  std::vector<uint32_t> jobs;
   std::vector<std::pair<size_t, uint32_t>> pending;  // (eligible position, chunk)
   size_t head = 0;
-  const size_t W = (size_t)(c->grid_apply > 0 ? c->grid_apply : 1);
-  const size_t nl = c->tdesc.size();
-  const size_t delay = c->chunks_upd.size() >= 8 * W ? 2 * W : SIZE_MAX / 2;
+  if (W == 0) W = 1;
+  const size_t nl = nchunks.size();
   std::vector<size_t> first(nl), order(nl);
   size_t ci = 0;
   for (size_t li = 0; li < nl; li++) {
     first[li] = ci;
-    ci += (size_t)c->tdesc[li].nchunks;
+    ci += (size_t)nchunks[li];
     order[li] = li;
   }
-  std::stable_sort(order.begin(), order.end(),
-                     [&](size_t x, size_t y) { return c->tdesc[x].nchunks > c->tdesc[y].nchunks; });
+  const size_t delay = ci >= 8 * W ? 2 * W : SIZE_MAX / 2;
+  std::stable_sort(order.begin(), order.end(), [&](size_t x, size_t y) { return nchunks[x] > nchunks[y]; });
   for (size_t li : order) {
-    const TensorDesc& d = c->tdesc[li];
-    for (int k = 0; k < d.nchunks; k++) {
-      c->jobs.push_back((uint32_t)(first[li] + k));
-      for (int r = 0; r < 2 && head < pending.size() && pending[head].first <= c->jobs.size(); r++)
-        c->jobs.push_back(0x80000000u | pending[head++].second);
+    for (int k = 0; k < nchunks[li]; k++) {
+      jobs.push_back((uint32_t)(first[li] + k));
+      for (int r = 0; r < 2 && head < pending.size() && pending[head].first <= jobs.size(); r++)
+        jobs.push_back(kRequantJob | pending[head++].second);
     }
-    if (d.quant == Q_FP8_E4M3_TENSOR || d.quant == Q_NVFP4_TENSOR)
-      for (int k = 0; k < d.nchunks; k++) pending.push_back({c->jobs.size() + delay, (uint32_t)(first[li] + k)});
+    if (quant[li] == Q_FP8_E4M3_TENSOR || quant[li] == Q_NVFP4_TENSOR)
+      for (int k = 0; k < nchunks[li]; k++) pending.push_back({jobs.size() + delay, (uint32_t)(first[li] + k)});
   }
-  while (head < pending.size()) c->jobs.push_back(0x80000000u | pending[head++].second);
+  while (head < pending.size()) jobs.push_back(kRequantJob | pending[head++].second);
+  return jobs;
+}
+
+static void build_jobs(ody_ctx* c) {
+  std::vector<int> nchunks, quant;
+  for (const TensorDesc& d : c->tdesc) {
+    nchunks.push_back(d.nchunks);
+    quant.push_back(d.quant);
+  }
+  c->jobs = plan_jobs(nchunks, quant, (size_t)(c->grid_apply > 0 ? c->grid_apply : 1));
+}
+
+// Test hook (not part of include/odyssey_mp.h): the apply kernel's job list
+// for tensors of nchunks[i] chunks and kind quant[i] on a grid of W CTAs;
+// jobs_out (capacity cap) receives the list, *njobs its length.
+extern "C" int odyx_plan_jobs(const int32_t* nchunks, const int32_t* quant, int32_t nt, int32_t W,
+                              uint32_t* jobs_out, int64_t cap, int64_t* njobs) {
+  if (nt < 0 || (nt > 0 && (!nchunks || !quant)) || !njobs) return fail(ODY_ERR_ARG, "bad argument");
+  const std::vector<uint32_t> jobs =
+      plan_jobs(std::vector<int>(nchunks, nchunks + nt), std::vector<int>(quant, quant + nt), (size_t)W);
+  *njobs = (int64_t)jobs.size();
+  if (jobs_out) {
+    if (cap < (int64_t)jobs.size()) return fail(ODY_ERR_ARG, "job buffer too small");
+    std::copy(jobs.begin(), jobs.end(), jobs_out);
+  }
+  return ODY_OK;
 }
 
 extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const void* uid) {

@@ -19,6 +19,7 @@ constexpr int kVec = 8;
 constexpr int kTile = kThreads * kVec;  // 2048 elements
 constexpr int kChunk = 32 * kTile;      // 65536 elements per chunk-table entry (at most)
 constexpr int kPad = 64;                // arena alignment of every tensor (elements)
+constexpr uint32_t kRequantJob = 0x80000000u;  // job-list entry flag: a requant job
 constexpr int kMxTileBytes = (kTile / 32) * 17;  // 1088
 constexpr int kNvTileBytes = (kTile / 16) * 9;   // 1152
 

@@ -849,8 +849,6 @@ struct ApplyArgs {
   uint32_t* sync;  // [0] job ticket, [1..] update jobs done per tensor
   Decision* dec;
 };
-
-constexpr uint32_t kRequantJob = 0x80000000u;
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {

@@ -425,7 +425,9 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-serial", action="store_true",
+                    help="e2e without double-buffered gradients (each upload waits for the previous step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tensors", type=int, default=64,
                     help="number of 4096x4096 tensors (64 = the 1B workload; fewer only for profiling)")
@@ -442,6 +444,8 @@ def main():
     ap.add_argument("--workload", default="flat1b", choices=["flat1b", "resnet18", "lenet", "mxfp4", "nvfp4"],
                     help="flat1b = the headline 1B model; resnet18 / lenet = secondary step lines; mxfp4 / "
                          "nvfp4 = the standalone quantiser on configs[1] / configs[2]")
+    ap.add_argument("--placement", default="auto", choices=["auto", "interleaved", "at_end"],
+                    help="where the apply kernel runs the per-tensor-scaled requant jobs (results identical)")
     args = ap.parse_args()
     if args.workload in QUANT_WORKLOADS:
         return run_quant(args)
@@ -470,6 +474,7 @@ def main():
     kw = wl.step_kwargs()
     kw["device"] = local
     kw["quant"] = QUANT
+    kw["requant_placement"] = args.placement
     if world > 1:
         ctx = ody.MixedPrecisionStep.from_process_group(wl.numels, **kw)
     else:
@@ -586,7 +591,16 @@ def main():
         ev1.synchronize()
     barrier()
     ms_total = ev0.elapsed_time(ev1)
+    # each rank's own pass times (per step), taken over the same untimed
+    # window: the exchange of a rank that finished its stats pass early
+    # includes its wait for the slowest rank
+    keys = ("stats", "exchange", "update")
+    mine = torch.tensor([passes[k] / max(nsteps, 1) for k in keys], dtype=torch.float64)
+    per_rank = [mine.tolist()]
     if world > 1:
+        allp = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allp, mine)
+        per_rank = [p.tolist() for p in allp]
         x = torch.tensor([ms_total, passes["update"], passes["stats"], passes["requant"], passes["exchange"]],
                          dtype=torch.float64)
         dist.all_reduce(x, op=dist.ReduceOp.MAX)
@@ -612,6 +626,12 @@ def main():
                 L.check(lib.ody_upload_async(ctx._ctx, e2e_buf, i, pinned[k].data_ptr(), pinned[k].numel()),
                         ctx._ctx)
 
+        # double-buffered gradient arenas (not with data-parallel gradients):
+        # step t+1's upload is queued right after step t, on a copy stream,
+        # so the PCIe copy overlaps step t's kernels
+        dbuf = args.dp == "none" and not args.e2e_serial
+        if dbuf:
+            ctx.set_grad_double_buffer(True)
         upload_all()
         ctx.step(t)
         t += 1
@@ -619,13 +639,24 @@ def main():
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         w0 = time.perf_counter()
         e0.record(stream)
-        for _ in range(args.e2e_steps):
+        if dbuf:
             upload_all()
-            ctx.step(t)  # synchronous: includes the device->host read of the step result
-            t += 1
+            for k in range(args.e2e_steps):
+                ctx.step_async(t)
+                t += 1
+                if k + 1 < args.e2e_steps:
+                    upload_all()  # the next step's gradients, while this step runs
+                ctx.wait()  # the device->host read of this step's result
+        else:
+            for _ in range(args.e2e_steps):
+                upload_all()
+                ctx.step(t)  # synchronous: includes the device->host read of the step result
+                t += 1
         e1.record(stream)
         e1.synchronize()
         wall = time.perf_counter() - w0
+        if dbuf:
+            ctx.set_grad_double_buffer(False)
         barrier()
         e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
         if world > 1:
@@ -666,6 +697,8 @@ def main():
             "hbm_gbs_per_gpu": step_gbs_gpu, "hbm_frac_per_gpu": step_gbs_gpu / peak,
             "alg_bytes_per_param": ALG_BYTES_STEP,
             "passes_ms_per_step": {k: v / max(nsteps, 1) for k, v in passes.items()},
+            "passes_ms_per_rank": {k: [r[j] for r in per_rank] for j, k in enumerate(keys)},
+            "requant_placement": args.placement,
             "roofline": {"kernel": "apply_kernel (update + per-tensor requant)", "bound": "hbm", "achieved": upd_gbs, "peak": peak,
                          "unit": "GB/s", "frac": upd_gbs / peak, "peak_source": peak_kind,
                          "alg_bytes_per_launch": ALG_BYTES_UPDATE * nloc,
@@ -676,7 +709,10 @@ def main():
             "e2e": None if e2e_ms is None else {
                 "value": TOTAL / (e2e_ms * 1e-3), "unit": "params/s", "ms_per_step": e2e_ms,
                 "wall_ms_per_step": wall * 1e3 / args.e2e_steps,
-                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": 80},
+                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": 80,
+                "overlap": "double-buffered gradients" if (args.dp == "none" and not args.e2e_serial) else "none",
+                "outputs": "the step result (80 B) is read back every step; master weights, states and the "
+                           "re-quantised weights stay in device memory for the next forward pass"},
             "gpu_launches": args.steps * (2 if world == 1 else 3),
             "graph_mode": use_graph,
             "dp_gradients": args.dp,

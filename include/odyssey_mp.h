@@ -61,6 +61,16 @@ extern "C" {
 #define ODY_Q_NVFP4 7          /* AnyTensor.to_nvfp4() (any_tensor.mojo:2329-2401), 9-byte blocks */
 #define ODY_Q_NVFP4_TENSOR 8   /* to_nvfp4(w / s_t), s_t = amax/(448*6) (per-tensor scale; extension) */
 
+/* ---- requant job placement (ody_config.requant_placement) ---------------
+ * INTERLEAVED: a tensor's requant jobs follow its last update job by two
+ * grid-widths of jobs, two per update job of the tensors after it; a
+ * tensor with fewer than two grid-widths of update jobs after it has its
+ * requant jobs at the end.  AT_END: all requant jobs after all update jobs.
+ * AUTO: INTERLEAVED.  Results are identical under every placement. */
+#define ODY_REQUANT_AUTO 0
+#define ODY_REQUANT_INTERLEAVED 1
+#define ODY_REQUANT_AT_END 2
+
 /* ---- context buffers ------------------------------------------------------ */
 #define ODY_BUF_MASTER 0 /* float32 master weights */
 #define ODY_BUF_STATE1 1 /* SGD velocity / Adam(W) first moment m (float32) */
@@ -99,7 +109,9 @@ typedef struct ody_config {
   double alpha;                 /* RMSprop smoothing constant (default 0.99) */
   int32_t chunk_elems;          /* apply-job chunk length in elements, a multiple of 2048 up to
                                    65536; 0 (default): chosen from the model size */
-  int32_t reserved[3];
+  int32_t requant_placement;    /* where the per-tensor-scaled kinds' requant jobs run inside the
+                                   apply kernel: ODY_REQUANT_AUTO (default), _INTERLEAVED, _AT_END */
+  int32_t reserved[2];
 } ody_config;
 
 /* What one step did (PrecisionConfig.step bookkeeping,
@@ -196,6 +208,21 @@ int ody_ctx_pass_times(ody_ctx* ctx, double* ms_out, int64_t* steps_out);
  * identical to the eager path. */
 int ody_ctx_set_graph(ody_ctx* ctx, int32_t enable);
 
+/* Double-buffered gradients (no reference counterpart; the reference's step
+ * reads host tensors).  Enabling allocates a second gradient arena.  From
+ * then on ODY_BUF_GRAD names the arena the NEXT step reads; ody_upload /
+ * ody_upload_async into it run on a separate copy stream, ordered after the
+ * step that last read that arena, and the step waits for them.  The arenas
+ * alternate with every step, so the host can queue step t+1's gradient
+ * upload right after ody_step_async(t) and the copy overlaps step t's
+ * kernels: a host-fed loop then runs at the rate of the slower of the PCIe
+ * copy and the kernels rather than their sum.  ody_ctx_device_ptr(...,
+ * ODY_BUF_GRAD, ...) also names the next step's arena, which changes with
+ * every step.  Graph mode is not used while this is on (steps run eagerly),
+ * and it does not combine with ody_ctx_dp_attach.  Disabling keeps the arena
+ * the next step would have read. */
+int ody_ctx_set_grad_double_buffer(ody_ctx* ctx, int32_t enable);
+
 /* Data-parallel gradients (collective over the context's ranks, at most 8).
  * Allocates this rank's full-model gradient buffer (every tensor, in the
  * context's gradient dtype, padded like the arenas; filled through
@@ -257,13 +284,17 @@ int ody_global_norm_clip(float* const* grads, const int64_t* numels, int32_t nte
  * Allocates nothing: its pointer table, per-block partial sums and results
  * live in one file-scope __device__ array of about 32 KB, which every GPU
  * that loads this library holds until the process exits.  grads must be
- * device pointers (clipped in place); at most 1024 tensors per call, more
- * is rejected with ODY_ERR_SHAPE.  The first call on a device looks up the
+ * device pointers of the calling thread's current GPU (clipped in place;
+ * another GPU's memory is refused with ODY_ERR_ARG); at most 1024 tensors
+ * per call, more is rejected with ODY_ERR_SHAPE.  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress) with that device current;
  * make that first call before any stream capture.  All calls on a device
  * share the array, which keeps the last call's contents (each call clears
  * what must start at zero); calls that overlap on the GPU race.  Runs on
- * the calling thread's default stream and returns after it completes. */
+ * the calling thread's per-thread default stream and returns after it
+ * completes.  That stream is ordered with the legacy default stream but not
+ * with the caller's non-blocking streams (a PyTorch side stream, say):
+ * finish or synchronise the stream that produced grads before the call. */
 int ody_global_norm_clip_noalloc(float* const* grads, const int64_t* numels, int32_t ntensors,
                                  float max_norm, float* total_norm);
 /* The two other global-norm clips of the reference, in place on float32

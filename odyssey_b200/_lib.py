@@ -42,7 +42,8 @@ class Config(C.Structure):
         ("growth_factor", C.c_float), ("backoff_factor", C.c_float), ("growth_interval", C.c_int64),
         ("min_scale", C.c_float), ("max_scale", C.c_float), ("clip_enabled", C.c_int32),
         ("max_norm", C.c_float), ("comm_timeout_ms", C.c_int32), ("reserved0", C.c_int32),
-        ("alpha", C.c_double), ("chunk_elems", C.c_int32), ("reserved", C.c_int32 * 3),
+        ("alpha", C.c_double), ("chunk_elems", C.c_int32), ("requant_placement", C.c_int32),
+        ("reserved", C.c_int32 * 2),
     ]
 
 
@@ -84,6 +85,7 @@ _SIGS = {
     "ody_ctx_set_timing": (C.c_int, [_p, _i32]),
     "ody_ctx_pass_times": (C.c_int, [_p, _p, _p]),
     "ody_ctx_set_graph": (C.c_int, [_p, _i32]),
+    "ody_ctx_set_grad_double_buffer": (C.c_int, [_p, _i32]),
     "ody_ctx_dp_attach": (C.c_int, [_p]),
     "ody_ctx_quant_layout": (C.c_int, [_p, _i32, _p, _p, _p]),
     "ody_ctx_gather_quant": (C.c_int, [_p, _p, _p]),

@@ -111,6 +111,7 @@ struct ody_ctx {
   std::vector<int32_t> rank_tbeg, rank_tend;   // per rank, tensor indices
   int64_t gq_total = 0;
   std::vector<uint32_t> jobs;  // apply-kernel job list (bit 31: requant job)
+  unsigned long long wait_ns = kWaitLimitNs;  // bound on the apply kernel's readiness wait
   int64_t n_total = 0, q_total = 0;
   cudaStream_t stream = nullptr;
   cudaEvent_t done = nullptr;
@@ -157,7 +158,19 @@ struct ody_ctx {
   cudaGraphExec_t gexec = nullptr;
   cudaGraphNode_t gapply = nullptr;
   OptConsts goc;
+  // double-buffered gradients (ody_ctx_set_grad_double_buffer): uploads of
+  // step t+1's gradients into one arena on a copy stream while step t reads
+  // the other; grad_slot[0] is `grad`
+  bool dbuf = false;
+  void* grad_slot[2] = {nullptr, nullptr};
+  int upload_slot = 0;                 // the arena ODY_BUF_GRAD names (the next step reads it)
+  cudaStream_t copy_stream = nullptr;  // non-blocking
+  cudaEvent_t slot_read[2] = {nullptr, nullptr};  // last step reading the slot is done with it
+  cudaEvent_t slot_filled[2] = {nullptr, nullptr};  // uploads into the slot are done
 };
+
+// the gradient arena the next step reads
+static void* step_grad(const ody_ctx* c) { return c->dbuf ? c->grad_slot[c->upload_slot] : c->grad; }
 
 static constexpr int kTimingRing = 64;
 
@@ -175,7 +188,7 @@ static cudaError_t timing_collect(ody_ctx* c, int64_t slot) {
   return cudaSuccess;
 }
 
-static bool is_device_ptr(const void* p);
+static bool is_device_ptr(const void* p);  // device memory of the current GPU, or managed
 
 static int ctx_fail(ody_ctx* c, int code, const std::string& msg) {
   g_err = msg;
@@ -279,6 +292,8 @@ extern "C" int ody_ctx_create(ody_ctx** out, const ody_config* cfg) {
   if (cfg->chunk_elems < 0 || cfg->chunk_elems % kTile != 0 || cfg->chunk_elems > kChunk)
     return fail(ODY_ERR_ARG, "chunk_elems must be 0 or a multiple of " + std::to_string(kTile) + " up to " +
                                  std::to_string(kChunk));
+  if (cfg->requant_placement < ODY_REQUANT_AUTO || cfg->requant_placement > ODY_REQUANT_AT_END)
+    return fail(ODY_ERR_ARG, "unknown requant_placement " + std::to_string(cfg->requant_placement));
   ody_ctx* c = new ody_ctx();
   c->cfg = *cfg;
   if (c->cfg.comm_timeout_ms <= 0) c->cfg.comm_timeout_ms = 60000;
@@ -364,38 +379,54 @@ static cudaError_t dalloc(T** p, size_t bytes) {
 
 // Job list of the apply kernel: every update chunk, tensors in descending
 // size (stable), so that the largest per-tensor-scaled tensors finish their
-// updates first.  The requant chunks of a per-tensor-scaled tensor become
-// eligible two grid-widths of jobs after that tensor's last update job and
-// are interleaved, up to two per update job, with the following tensors'
-// update jobs; what is left runs at the end.  A model of fewer than eight
-// grid-widths of update jobs puts every requant job at the end (measured
-// faster there: its interleaved requant jobs would mostly wait).
+// updates first.  Interleaved placement (the default): the requant chunks of
+// a per-tensor-scaled tensor become eligible two grid-widths of jobs after
+// that tensor's last update job and are slotted in, up to two per update
+// job, between the following tensors' update jobs; a tensor followed by
+// fewer than two grid-widths of update jobs (the last ones of every rank)
+// has its requant jobs at the end.  The decision is per tensor, so a rank of
+// few large tensors (the 1B model on 4 or 8 ranks: 4,096 update jobs on a
+// 592-CTA grid) still hides most of its requant work behind update traffic:
+// measured 5 % faster there than all-at-end, and equal on ResNet-18.
+// At-end placement: every requant job after every update job.
 // nchunks[i], quant[i]: the local tensors in arena order; W: the apply grid
-static std::vector<uint32_t> plan_jobs(const std::vector<int>& nchunks, const std::vector<int>& quant, size_t W) {
+static std::vector<uint32_t> plan_jobs(const std::vector<int>& nchunks, const std::vector<int>& quant, size_t W,
+                                       int placement) {
   std::vector<uint32_t> jobs;
   std::vector<std::pair<size_t, uint32_t>> pending;  // (eligible position, chunk)
+  std::vector<uint32_t> tail;                          // requant jobs placed at the end
   size_t head = 0;
   if (W == 0) W = 1;
   const size_t nl = nchunks.size();
   std::vector<size_t> first(nl), order(nl);
-  size_t ci = 0;
+  size_t total = 0;
   for (size_t li = 0; li < nl; li++) {
-    first[li] = ci;
-    ci += (size_t)nchunks[li];
+    first[li] = total;
+    total += (size_t)nchunks[li];
     order[li] = li;
   }
-  const size_t delay = ci >= 8 * W ? 2 * W : SIZE_MAX / 2;
+  const bool interleave = placement != ODY_REQUANT_AT_END;
+  const size_t delay = 2 * W;
   std::stable_sort(order.begin(), order.end(), [&](size_t x, size_t y) { return nchunks[x] > nchunks[y]; });
+  size_t updates_done = 0;
   for (size_t li : order) {
     for (int k = 0; k < nchunks[li]; k++) {
       jobs.push_back((uint32_t)(first[li] + k));
       for (int r = 0; r < 2 && head < pending.size() && pending[head].first <= jobs.size(); r++)
         jobs.push_back(kRequantJob | pending[head++].second);
     }
-    if (quant[li] == Q_FP8_E4M3_TENSOR || quant[li] == Q_NVFP4_TENSOR)
-      for (int k = 0; k < nchunks[li]; k++) pending.push_back({jobs.size() + delay, (uint32_t)(first[li] + k)});
+    updates_done += (size_t)nchunks[li];
+    if (quant[li] != Q_FP8_E4M3_TENSOR && quant[li] != Q_NVFP4_TENSOR) continue;
+    const bool here = interleave && total - updates_done >= delay;
+    for (int k = 0; k < nchunks[li]; k++) {
+      if (here)
+        pending.push_back({jobs.size() + delay, (uint32_t)(first[li] + k)});
+      else
+        tail.push_back((uint32_t)(first[li] + k));
+    }
   }
   while (head < pending.size()) jobs.push_back(kRequantJob | pending[head++].second);
+  for (uint32_t ch : tail) jobs.push_back(kRequantJob | ch);
   return jobs;
 }
 
@@ -405,23 +436,85 @@ static void build_jobs(ody_ctx* c) {
     nchunks.push_back(d.nchunks);
     quant.push_back(d.quant);
   }
-  c->jobs = plan_jobs(nchunks, quant, (size_t)(c->grid_apply > 0 ? c->grid_apply : 1));
+  c->jobs = plan_jobs(nchunks, quant, (size_t)(c->grid_apply > 0 ? c->grid_apply : 1), c->cfg.requant_placement);
+}
+
+// (re)allocates the device copy of the job list and copies it in
+static int upload_jobs(ody_ctx* c) {
+  if (c->d_jobs) ODY_CUDA(cudaFree(c->d_jobs));
+  c->d_jobs = nullptr;
+  ODY_CUDA(dalloc(&c->d_jobs, sizeof(uint32_t) * (c->jobs.size() + 1)));
+  if (!c->jobs.empty())
+    ODY_CUDA(cudaMemcpyAsync(c->d_jobs, c->jobs.data(), sizeof(uint32_t) * c->jobs.size(), cudaMemcpyHostToDevice,
+                             c->stream));
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  return ODY_OK;
 }
 
 // Test hook (not part of include/odyssey_mp.h): the apply kernel's job list
-// for tensors of nchunks[i] chunks and kind quant[i] on a grid of W CTAs;
-// jobs_out (capacity cap) receives the list, *njobs its length.
+// for tensors of nchunks[i] chunks and kind quant[i] on a grid of W CTAs
+// under a requant placement (ODY_REQUANT_*); jobs_out (capacity cap)
+// receives the list, *njobs its length.
 extern "C" int odyx_plan_jobs(const int32_t* nchunks, const int32_t* quant, int32_t nt, int32_t W,
-                              uint32_t* jobs_out, int64_t cap, int64_t* njobs) {
+                              int32_t placement, uint32_t* jobs_out, int64_t cap, int64_t* njobs) {
   if (nt < 0 || (nt > 0 && (!nchunks || !quant)) || !njobs) return fail(ODY_ERR_ARG, "bad argument");
-  const std::vector<uint32_t> jobs =
-      plan_jobs(std::vector<int>(nchunks, nchunks + nt), std::vector<int>(quant, quant + nt), (size_t)W);
+  const std::vector<uint32_t> jobs = plan_jobs(std::vector<int>(nchunks, nchunks + nt),
+                                               std::vector<int>(quant, quant + nt), (size_t)W, placement);
   *njobs = (int64_t)jobs.size();
   if (jobs_out) {
     if (cap < (int64_t)jobs.size()) return fail(ODY_ERR_ARG, "job buffer too small");
     std::copy(jobs.begin(), jobs.end(), jobs_out);
   }
   return ODY_OK;
+}
+
+// Test hook: the live context's apply-kernel job list and grid (the list
+// ody_step runs); jobs_out may be NULL to query the length.
+extern "C" int odyx_ctx_jobs(const ody_ctx* c, uint32_t* jobs_out, int64_t cap, int64_t* njobs, int32_t* grid) {
+  if (!c || !njobs) return fail(ODY_ERR_ARG, "bad argument");
+  if (!c->finalized) return fail(ODY_ERR_STATE, "context not finalized");
+  *njobs = (int64_t)c->jobs.size();
+  if (grid) *grid = c->grid_apply;
+  if (jobs_out) {
+    if (cap < (int64_t)c->jobs.size()) return fail(ODY_ERR_ARG, "job buffer too small");
+    std::copy(c->jobs.begin(), c->jobs.end(), jobs_out);
+  }
+  return ODY_OK;
+}
+
+static void drop_graph(ody_ctx* c);
+
+// Test hook for the device-side bounded wait: replaces the context's job
+// list (NULL: back to the planned list) and the bound on a requant job's
+// readiness wait (wait_ns 0: the 2 s default).  Entries are checked against
+// the chunk table; a requant entry must name a chunk of a per-tensor-scaled
+// tensor.  A list that leaves out some update job of a tensor whose requant
+// job it keeps makes that wait run out, which ody_step_wait reports as
+// ODY_ERR_DEVICE_BOUNDS.
+extern "C" int odyx_ctx_set_jobs(ody_ctx* c, const uint32_t* jobs, int64_t n, uint64_t wait_ns) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  if (c->pending) return ctx_fail(c, ODY_ERR_STATE, "a step is in flight");
+  if (jobs) {
+    if (n < 0 || n > (int64_t)INT32_MAX) return ctx_fail(c, ODY_ERR_ARG, "bad job count");
+    for (int64_t i = 0; i < n; i++) {
+      const uint32_t ch = jobs[i] & ~kRequantJob;
+      if (ch >= c->chunks_upd.size()) return ctx_fail(c, ODY_ERR_ARG, "job " + std::to_string(i) + ": bad chunk");
+      const int q = c->tdesc[c->chunks_upd[ch].tensor].quant;
+      if ((jobs[i] & kRequantJob) && q != Q_FP8_E4M3_TENSOR && q != Q_NVFP4_TENSOR)
+        return ctx_fail(c, ODY_ERR_ARG, "job " + std::to_string(i) + ": requant of a tensor without a per-tensor scale");
+    }
+    c->jobs.assign(jobs, jobs + n);
+  } else {
+    build_jobs(c);
+  }
+  c->wait_ns = wait_ns ? (unsigned long long)wait_ns : kWaitLimitNs;
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  if (c->gexec) {
+    ODY_CUDA(cudaStreamSynchronize(c->stream));
+    drop_graph(c);
+  }
+  return upload_jobs(c);
 }
 
 extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const void* uid) {
@@ -542,10 +635,10 @@ extern "C" int ody_ctx_finalize(ody_ctx* c, int32_t world, int32_t rank, const v
   c->grid_apply = apply_grid(c->gdt, c->cfg.optimizer, c->cfg.device);
   if ((size_t)c->grid_apply > c->chunks_upd.size()) c->grid_apply = (int)std::max<size_t>(1, c->chunks_upd.size());
   build_jobs(c);
-  ODY_CUDA(dalloc(&c->d_jobs, sizeof(uint32_t) * (c->jobs.size() + 1)));
-  if (!c->jobs.empty())
-    ODY_CUDA(cudaMemcpyAsync(c->d_jobs, c->jobs.data(), sizeof(uint32_t) * c->jobs.size(), cudaMemcpyHostToDevice,
-                             c->stream));
+  {
+    const int rc = upload_jobs(c);
+    if (rc) return rc;
+  }
   ODY_CUDA(dalloc(&c->sync, sizeof(uint32_t) * (nl + 1)));
   ODY_CUDA(cudaMemsetAsync(c->sync, 0, sizeof(uint32_t) * (nl + 1), c->stream));
   // one unrolled round (4 groups of 8 gradients) per thread, at most the
@@ -634,7 +727,7 @@ static int locate(ody_ctx* c, int32_t which, int32_t i, void** base, size_t* byt
       *bytes = (size_t)d.numel * 4;
       break;
     case ODY_BUF_GRAD:
-      *base = (uint8_t*)c->grad + (size_t)d.off * dtype_size(c->gdt);
+      *base = (uint8_t*)step_grad(c) + (size_t)d.off * dtype_size(c->gdt);
       *bytes = (size_t)d.numel * dtype_size(c->gdt);
       break;
     default:
@@ -653,6 +746,19 @@ static int copy_tensor(ody_ctx* c, int32_t which, int32_t i, void* dst_or_src, s
     return ctx_fail(c, ODY_ERR_SHAPE, "size mismatch: expected " + std::to_string(need) + " bytes, got " +
                                           std::to_string(bytes));
   ODY_CUDA(cudaSetDevice(c->cfg.device));
+  if (c->dbuf && which == ODY_BUF_GRAD) {
+    // the copy stream: after the step that last read this arena, and ahead
+    // of the step that reads it next (which waits on slot_filled)
+    const int s = c->upload_slot;
+    ODY_CUDA(cudaStreamWaitEvent(c->copy_stream, c->slot_read[s], 0));
+    if (up)
+      ODY_CUDA(cudaMemcpyAsync(base, dst_or_src, bytes, cudaMemcpyDefault, c->copy_stream));
+    else
+      ODY_CUDA(cudaMemcpyAsync(dst_or_src, base, bytes, cudaMemcpyDefault, c->copy_stream));
+    ODY_CUDA(cudaEventRecord(c->slot_filled[s], c->copy_stream));
+    if (sync) ODY_CUDA(cudaStreamSynchronize(c->copy_stream));
+    return ODY_OK;
+  }
   if (up)
     ODY_CUDA(cudaMemcpyAsync(base, dst_or_src, bytes, cudaMemcpyDefault, c->stream));
   else
@@ -730,10 +836,10 @@ static DecideParams make_decide(const ody_config& cfg) {
 static cudaError_t launch_pass1(ody_ctx* c, const DecideParams& dp, int world_mode) {
   const int nl = (int)c->tdesc.size();
   if (c->dp_on)
-    return launch_rs_stats(c->gdt, c->d_peers, c->world, c->dp_shard_off, c->grad, c->n_total,
+    return launch_rs_stats(c->gdt, c->d_peers, c->world, c->dp_shard_off, step_grad(c), c->n_total,
                            c->cfg.use_gradient_scaler, c->scaler, c->partials, c->grid_stats, c->ticket, world_mode,
                            c->local_stats, dp, c->dec, c->amax, c->sync, nl, c->stream);
-  return launch_stats(c->gdt, c->grad, c->n_total, c->cfg.use_gradient_scaler, c->scaler, c->partials,
+  return launch_stats(c->gdt, step_grad(c), c->n_total, c->cfg.use_gradient_scaler, c->scaler, c->partials,
                       c->grid_stats, c->ticket, world_mode, c->local_stats, dp, c->dec, c->amax, c->sync, nl,
                       c->stream);
 }
@@ -758,7 +864,7 @@ static int step_graph(ody_ctx* c, const OptConsts& oc, const DecideParams& dp) {
     if (e == cudaSuccess)
       e = launch_apply(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd, c->d_jobs,
                        (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout, c->amax,
-                       c->qscale, c->sync, c->dec, c->grid_apply, c->stream);
+                       c->qscale, c->sync, c->dec, c->grid_apply, c->stream, c->wait_ns);
     if (e == cudaSuccess)
       e = cudaMemcpyAsync(c->h_dec, c->dec, sizeof(Decision), cudaMemcpyDeviceToHost, c->stream);
     cudaGraph_t g = nullptr;
@@ -796,7 +902,7 @@ static int step_graph(ody_ctx* c, const OptConsts& oc, const DecideParams& dp) {
   } else if (memcmp(&c->goc, &oc, sizeof(OptConsts)) != 0) {
     ODY_CUDA(set_apply_node(c->gexec, c->gapply, c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler,
                             c->d_chunks_upd, c->d_jobs, (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2,
-                            c->grad, c->qout, c->amax, c->qscale, c->sync, c->dec, c->grid_apply));
+                            c->grad, c->qout, c->amax, c->qscale, c->sync, c->dec, c->grid_apply, c->wait_ns));
     c->goc = oc;
   }
   ODY_CUDA(cudaGraphLaunch(c->gexec, c->stream));
@@ -823,6 +929,7 @@ extern "C" int ody_ctx_dp_attach(ody_ctx* c) {
   if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
   if (c->broken) return ctx_fail(c, ODY_ERR_STATE, "context unusable after a communicator failure");
   if (c->dp_on) return ctx_fail(c, ODY_ERR_STATE, "data-parallel gradients already attached");
+  if (c->dbuf) return ctx_fail(c, ODY_ERR_STATE, "data-parallel gradients do not combine with double-buffered gradients");
   if (c->world > 8) return ctx_fail(c, ODY_ERR_ARG, "data-parallel gradients support at most 8 ranks");
   ODY_CUDA(cudaSetDevice(c->cfg.device));
   dp_release(c);  // what a failed earlier attempt left
@@ -892,6 +999,48 @@ extern "C" int ody_ctx_dp_attach(ody_ctx* c) {
   return ODY_OK;
 }
 
+extern "C" int ody_ctx_set_grad_double_buffer(ody_ctx* c, int32_t enable) {
+  if (!c) return fail(ODY_ERR_ARG, "null context");
+  if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
+  if (c->pending) return ctx_fail(c, ODY_ERR_STATE, "a step is in flight");
+  if (c->dp_on) return ctx_fail(c, ODY_ERR_STATE, "double-buffered gradients do not combine with data-parallel gradients");
+  ODY_CUDA(cudaSetDevice(c->cfg.device));
+  if (!enable) {
+    if (!c->dbuf) return ODY_OK;
+    ODY_CUDA(cudaStreamSynchronize(c->copy_stream));
+    ODY_CUDA(cudaStreamSynchronize(c->stream));
+    // the arena the next step would read becomes the single arena
+    if (c->upload_slot == 1) std::swap(c->grad_slot[0], c->grad_slot[1]);
+    c->grad = c->grad_slot[0];
+    ODY_CUDA(cudaFree(c->grad_slot[1]));
+    c->grad_slot[1] = nullptr;
+    c->upload_slot = 0;
+    c->dbuf = false;
+    return ODY_OK;
+  }
+  if (c->dbuf) return ODY_OK;
+  const size_t bytes = (size_t)(c->n_total > 0 ? c->n_total : kPad) * dtype_size(c->gdt);
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  if (!c->copy_stream) {
+    ODY_CUDA(cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking));
+    for (int s = 0; s < 2; s++) {
+      ODY_CUDA(cudaEventCreateWithFlags(&c->slot_read[s], cudaEventDisableTiming));
+      ODY_CUDA(cudaEventCreateWithFlags(&c->slot_filled[s], cudaEventDisableTiming));
+      ODY_CUDA(cudaEventRecord(c->slot_read[s], c->stream));
+      ODY_CUDA(cudaEventRecord(c->slot_filled[s], c->stream));
+    }
+  }
+  void* alt = nullptr;
+  ODY_CUDA(dalloc((uint8_t**)&alt, bytes));
+  ODY_CUDA(cudaMemsetAsync(alt, 0, bytes, c->stream));
+  ODY_CUDA(cudaStreamSynchronize(c->stream));
+  c->grad_slot[0] = c->grad;
+  c->grad_slot[1] = alt;
+  c->upload_slot = 0;
+  c->dbuf = true;
+  return ODY_OK;
+}
+
 extern "C" int ody_ctx_set_graph(ody_ctx* c, int32_t enable) {
   if (!c) return fail(ODY_ERR_ARG, "null context");
   if (!c->finalized) return ctx_fail(c, ODY_ERR_STATE, "context not finalized");
@@ -914,7 +1063,8 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   const OptConsts oc = make_consts(c->cfg, t);
   const DecideParams dp = make_decide(c->cfg);
   const int nl = (int)c->tdesc.size();
-  if (c->graph_mode && c->world == 1 && !c->timing && !c->jobs.empty()) return step_graph(c, oc, dp);
+  if (c->graph_mode && c->world == 1 && !c->timing && !c->dbuf && !c->jobs.empty()) return step_graph(c, oc, dp);
+  if (c->dbuf) ODY_CUDA(cudaStreamWaitEvent(c->stream, c->slot_filled[c->upload_slot], 0));
   cudaEvent_t* tev = nullptr;
   if (c->timing) {
     const int64_t slot = c->tnext++;
@@ -958,12 +1108,18 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   if (tev) ODY_CUDA(cudaEventRecord(tev[2], c->stream));
   if (!c->jobs.empty()) {
     e = launch_apply(c->gdt, c->cfg.optimizer, oc, c->cfg.use_gradient_scaler, c->d_chunks_upd, c->d_jobs,
-                     (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2, c->grad, c->qout, c->amax, c->qscale,
-                     c->sync, c->dec, c->grid_apply, c->stream);
+                     (int)c->jobs.size(), c->d_tdesc, c->master, c->s1, c->s2, step_grad(c), c->qout, c->amax, c->qscale,
+                     c->sync, c->dec, c->grid_apply, c->stream, c->wait_ns);
     if (e != cudaSuccess) return ctx_fail(c, ODY_ERR_CUDA, std::string("apply kernel: ") + cudaGetErrorString(e));
   }
   if (tev) ODY_CUDA(cudaEventRecord(tev[3], c->stream));
   if (tev) ODY_CUDA(cudaEventRecord(tev[4], c->stream));
+  if (c->dbuf) {
+    // this step's arena is free for uploads once the apply kernel is done;
+    // the next step reads the other one
+    ODY_CUDA(cudaEventRecord(c->slot_read[c->upload_slot], c->stream));
+    c->upload_slot ^= 1;
+  }
   ODY_CUDA(cudaMemcpyAsync(c->h_dec, c->dec, sizeof(Decision), cudaMemcpyDeviceToHost, c->stream));
   ODY_CUDA(cudaEventRecord(c->done, c->stream));
   c->pending = true;
@@ -1076,7 +1232,7 @@ extern "C" int ody_ctx_gather_quant(ody_ctx* c, void* dst, float* scales) {
   if (c->broken) return ctx_fail(c, ODY_ERR_STATE, "context unusable after a communicator failure");
   if (!dst || !scales) return ctx_fail(c, ODY_ERR_ARG, "null destination");
   if (!is_device_ptr(dst) || !is_device_ptr(scales))
-    return ctx_fail(c, ODY_ERR_ARG, "gather destinations must be device memory");
+    return ctx_fail(c, ODY_ERR_ARG, "gather destinations must be device memory of the context's GPU");
   ODY_CUDA(cudaSetDevice(c->cfg.device));
   const int r = c->rank;
   const int64_t nb = c->rank_qend[r] - c->rank_qbeg[r];
@@ -1280,6 +1436,13 @@ extern "C" void ody_ctx_destroy(ody_ctx* c) {
   for (void* b : bufs)
     if (b) cudaFree(b);
   for (auto& e : c->tev) cudaEventDestroy(e);
+  if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+  if (c->grad_slot[1]) cudaFree(c->grad_slot[1]);
+  for (int s = 0; s < 2; s++) {
+    if (c->slot_read[s]) cudaEventDestroy(c->slot_read[s]);
+    if (c->slot_filled[s]) cudaEventDestroy(c->slot_filled[s]);
+  }
+  if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
   drop_graph(c);
   dp_release(c);
   if (c->h_dec) cudaFreeHost(c->h_dec);
@@ -1293,14 +1456,33 @@ extern "C" void ody_ctx_destroy(ody_ctx* c) {
 // host operands are staged through temporary device buffers on the calling
 // thread's default stream.
 // ---------------------------------------------------------------------------
-static bool is_device_ptr(const void* p) {
-  if (!p) return false;
+// Device memory usable by this call's kernels: managed memory, or device
+// memory of the calling thread's current GPU.  Another GPU's memory is not
+// (without peer access a kernel reading it faults): device_elsewhere() names
+// that case so the caller can refuse it before any launch.
+static int device_of(const void* p) {
+  if (!p) return -1;
   cudaPointerAttributes a;
   if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
     cudaGetLastError();
-    return false;
+    return -1;
   }
-  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+  if (a.type == cudaMemoryTypeManaged) return INT32_MAX;  // reachable from every GPU
+  return a.type == cudaMemoryTypeDevice ? a.device : -1;
+}
+
+static bool is_device_ptr(const void* p) {
+  const int d = device_of(p);
+  if (d < 0) return false;
+  if (d == INT32_MAX) return true;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  return d == cur;
+}
+
+static bool device_elsewhere(const void* p) {
+  const int d = device_of(p);
+  return d >= 0 && d != INT32_MAX && !is_device_ptr(p);
 }
 
 namespace {
@@ -1324,6 +1506,7 @@ struct Scope {
       *dev = nullptr;
       return cudaSuccess;
     }
+    if (device_elsewhere(user)) return cudaErrorInvalidDevice;
     if (is_device_ptr(user)) {
       *dev = const_cast<void*>(user);
       bufs.push_back({const_cast<void*>(user), *dev, bytes, false});
@@ -1351,6 +1534,8 @@ struct Scope {
 #define ODY_STAGE(S, ptr, bytes, in, dev)                                             \
   do {                                                                                \
     cudaError_t se_ = (S).stage((ptr), (bytes), (in), (void**)(dev));                 \
+    if (se_ == cudaErrorInvalidDevice)                                                \
+      return fail(ODY_ERR_ARG, "a buffer is device memory of another GPU than the current one"); \
     if (se_ != cudaSuccess)                                                           \
       return fail(ODY_ERR_CUDA, std::string("staging a buffer: ") + cudaGetErrorString(se_)); \
   } while (0)

@@ -20,6 +20,7 @@ constexpr int kTile = kThreads * kVec;  // 2048 elements
 constexpr int kChunk = 32 * kTile;      // 65536 elements per chunk-table entry (at most)
 constexpr int kPad = 64;                // arena alignment of every tensor (elements)
 constexpr uint32_t kRequantJob = 0x80000000u;  // job-list entry flag: a requant job
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // default bound on a device-side wait (2 s)
 constexpr int kMxTileBytes = (kTile / 32) * 17;  // 1088
 constexpr int kNvTileBytes = (kTile / 16) * 9;   // 1152
 
@@ -100,7 +101,7 @@ cudaError_t launch_finalize(const double* gathered, int world, DevScaler* scaler
 cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
                          const uint32_t* jobs, int njobs, const TensorDesc* tensors, float* master, float* s1,
                          float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
-                         uint32_t* sync, Decision* dec, int grid, cudaStream_t st);
+                         uint32_t* sync, Decision* dec, int grid, cudaStream_t st, unsigned long long wait_ns);
 // pass 1 with the data-parallel gradient reduce-scatter fused in (up to 8
 // ranks; peers: device array of the ranks' full gradient buffers)
 cudaError_t launch_rs_stats(int gdt, const void* const* peers, int world, int64_t shard_off, void* grad, int64_t n,
@@ -119,7 +120,7 @@ cudaError_t set_apply_node(cudaGraphExec_t exec, cudaGraphNode_t node, int gdt, 
                            int use_scaler, const Chunk* chunks, const uint32_t* jobs, int njobs,
                            const TensorDesc* tensors, float* master, float* s1, float* s2, const void* grad,
                            uint8_t* qout, uint32_t* amax_slots, float* qscale, uint32_t* sync, Decision* dec,
-                           int grid);
+                           int grid, unsigned long long wait_ns);
 int stats_grid(int device);
 
 // stateless whole-tensor operations (device pointers)

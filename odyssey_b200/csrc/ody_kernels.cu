@@ -848,8 +848,8 @@ struct ApplyArgs {
   float* qscale;
   uint32_t* sync;  // [0] job ticket, [1..] update jobs done per tensor
   Decision* dec;
+  unsigned long long wait_ns;  // bound on a requant job's readiness wait (2 s unless a test shortens it)
 };
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -974,7 +974,7 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
     if (ld_acquire(done) < (uint32_t)td.nchunks) {
       const unsigned long long t0 = globaltimer_ns();
       while (ld_acquire(done) < (uint32_t)td.nchunks) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > a.wait_ns) {
           ok = 0;
           atomicOr(&a.dec->err, 1);
           break;
@@ -1112,9 +1112,9 @@ int apply_grid(int gdt, int opt, int device) {
 cudaError_t launch_apply(int gdt, int opt, const OptConsts& oc, int use_scaler, const Chunk* chunks,
                          const uint32_t* jobs, int njobs, const TensorDesc* tensors, float* master, float* s1,
                          float* s2, const void* grad, uint8_t* qout, uint32_t* amax_slots, float* qscale,
-                         uint32_t* sync, Decision* dec, int grid, cudaStream_t st) {
+                         uint32_t* sync, Decision* dec, int grid, cudaStream_t st, unsigned long long wait_ns) {
   ApplyArgs a{oc, use_scaler, chunks, jobs, njobs, tensors, master, s1, s2, grad, qout, amax_slots, qscale, sync,
-              dec};
+              dec, wait_ns};
   // programmatic dependent launch: the CTAs start while the stats (or
   // finalize) grid is still running and wait on it inside the kernel
   cudaLaunchConfig_t cfg = {};
@@ -1158,9 +1158,9 @@ cudaError_t set_apply_node(cudaGraphExec_t exec, cudaGraphNode_t node, int gdt, 
                            int use_scaler, const Chunk* chunks, const uint32_t* jobs, int njobs,
                            const TensorDesc* tensors, float* master, float* s1, float* s2, const void* grad,
                            uint8_t* qout, uint32_t* amax_slots, float* qscale, uint32_t* sync, Decision* dec,
-                           int grid) {
+                           int grid, unsigned long long wait_ns) {
   ApplyArgs a{oc, use_scaler, chunks, jobs, njobs, tensors, master, s1, s2, grad, qout, amax_slots, qscale, sync,
-              dec};
+              dec, wait_ns};
   void* args[1] = {&a};
   cudaKernelNodeParams kp = {};
   kp.func = const_cast<void*>(apply_kernel_fn(gdt, opt));

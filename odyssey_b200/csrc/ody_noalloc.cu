@@ -176,6 +176,12 @@ extern "C" int ody_global_norm_clip_noalloc(float* const* grads, const int64_t* 
         return na_fail(ODY_ERR_ARG, "ody_global_norm_clip_noalloc: gradient " + std::to_string(i) +
                                         " is not device memory");
       }
+      // another GPU's memory: without peer access the kernels below would
+      // fault on it, so it is refused before anything is launched
+      if (a.type == cudaMemoryTypeDevice && a.device != dev)
+        return na_fail(ODY_ERR_ARG, "ody_global_norm_clip_noalloc: gradient " + std::to_string(i) +
+                                        " is memory of GPU " + std::to_string(a.device) +
+                                        ", not of the current GPU " + std::to_string(dev));
     }
     ptrs[i] = grads[i];
     ns[i] = numels[i];

@@ -19,6 +19,9 @@ from .quant import QuantizedTensor
 _OPT = {"sgd": L.SGD, "adam": L.ADAM, "adamw": L.ADAMW, "lion": L.LION, "rmsprop": L.RMSPROP,
         "adagrad": L.ADAGRAD}
 _GDT = {"float32": L.F32, "float16": L.F16, "bfloat16": L.BF16}
+# where the apply kernel runs the per-tensor-scaled kinds' requant jobs
+# (ody_config.requant_placement); results are identical under each
+_PLACEMENT = {"auto": 0, "interleaved": 1, "at_end": 2}
 
 
 def nccl_unique_id():
@@ -40,7 +43,8 @@ class MixedPrecisionStep:
                  momentum=0.0, beta1=0.9, beta2=0.999, epsilon=1e-8, weight_decay=0.0,
                  use_gradient_scaler=True, initial_scale=65536.0, growth_factor=2.0, backoff_factor=0.5,
                  growth_interval=2000, min_scale=1.0, max_scale=65536.0, clip_max_norm=None, device=0,
-                 world_size=1, rank=0, unique_id=None, comm_timeout_ms=60000, alpha=0.99, chunk_elems=0):
+                 world_size=1, rank=0, unique_id=None, comm_timeout_ms=60000, alpha=0.99, chunk_elems=0,
+                 requant_placement="auto"):
         cfg = L.default_config()
         cfg.optimizer = _OPT[optimizer] if isinstance(optimizer, str) else int(optimizer)
         cfg.device = int(device)
@@ -54,6 +58,8 @@ class MixedPrecisionStep:
         cfg.comm_timeout_ms = int(comm_timeout_ms)
         cfg.alpha = float(alpha)
         cfg.chunk_elems = int(chunk_elems)
+        cfg.requant_placement = (_PLACEMENT[requant_placement] if isinstance(requant_placement, str)
+                                 else int(requant_placement))
         self.cfg = cfg
         self.numels = [int(n) for n in numels]
         self.grad_dtype = _GDT[grad_dtype] if isinstance(grad_dtype, str) else int(grad_dtype)
@@ -182,6 +188,12 @@ class MixedPrecisionStep:
         """Replay each step as one CUDA graph launch (one GPU; see
         ody_ctx_set_graph)."""
         L.check(L.lib().ody_ctx_set_graph(self._ctx, int(bool(enable))), self._ctx)
+
+    def set_grad_double_buffer(self, enable=True):
+        """Two gradient arenas, alternating per step: set_grad(..., sync=False)
+        for step t+1 right after step_async(t) copies on a separate stream
+        while step t runs (see ody_ctx_set_grad_double_buffer)."""
+        L.check(L.lib().ody_ctx_set_grad_double_buffer(self._ctx, int(bool(enable))), self._ctx)
 
     def pass_times(self):
         """{'stats','exchange','update','requant'} milliseconds accumulated over

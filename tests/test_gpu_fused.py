@@ -423,3 +423,49 @@ def test_long_chunks(oracle, chunk):
     ctx, model, res = run_pair(oracle, wl, 3, quants=["nvfp4_tensor", "mxfp4", "fp8_tensor"],
                                ctx_kwargs={"chunk_elems": chunk})
     ctx.close()
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_double_buffered_gradients(oracle, graph):
+    """Double-buffered gradient arenas: step t+1's gradients uploaded (async,
+    copy stream) while step t runs give the oracle's results step by step,
+    with an inf step in between; turning it off keeps the staged arena."""
+    from odyssey_b200 import MixedPrecisionStep
+    wl = W.flat1b(ntensors=3, side=384)
+    wl.inf_every = 3
+    kw = wl.step_kwargs()
+    ctx = MixedPrecisionStep(wl.numels, **kw)
+    ctx.set_graph(graph)  # ignored while double-buffering
+    specs = [{"numel": n, "grad_dtype": GDT[wl.grad_dtype], "quant": QK[wl.quant]} for n in wl.numels]
+    hy = wl.hyper
+    model = oracle.Model(specs, OPT[wl.optimizer], hy["learning_rate"], beta1=hy["beta1"], beta2=hy["beta2"],
+                         epsilon=hy["epsilon"], weight_decay=hy["weight_decay"], clip_enabled=True,
+                         max_norm=wl.clip, scaler_kwargs={"initial_scale": kw["initial_scale"]})
+    for i, m in enumerate(wl.master(0)):
+        ctx.set_master(i, m)
+        model.master[i][:] = m
+    ctx.set_grad_double_buffer(True)
+    nsteps = 7
+    grads = [wl.grads(s) for s in range(nsteps + 1)]
+    kept = []  # the host arrays must outlive their async copies
+    for i, g in enumerate(grads[0]):
+        kept.append(ctx.set_grad(i, g, sync=False))
+    t = to = 1
+    for s in range(nsteps):
+        ctx.step_async(t)
+        for i, g in enumerate(grads[s + 1]):
+            kept.append(ctx.set_grad(i, g, sync=False))
+        r = ctx.wait()
+        ro = model.step(grads[s], to)
+        assert r["skipped"] == ro.skipped and r["clip_coef"] == ro.coef and r["scale_next"] == ro.scale_next, s
+        if not r["skipped"]:
+            t += 1
+            to += 1
+    compare_state(ctx, model, wl.numels, [wl.quant] * len(wl.numels), wl.optimizer)
+    # off: the arena staged for the next step (grads[nsteps]) is the one kept
+    ctx.set_grad_double_buffer(False)
+    r = ctx.step(t)
+    ro = model.step(grads[nsteps], to)
+    assert r["skipped"] == ro.skipped and r["clip_coef"] == ro.coef
+    compare_state(ctx, model, wl.numels, [wl.quant] * len(wl.numels), wl.optimizer)
+    ctx.close()

@@ -173,15 +173,72 @@ def test_global_norm_clip_vs_oracle(ody, oracle):
         np.testing.assert_array_equal(x, y)
 
 
-def test_master_conversions(ody):
-    h = np.full(100, 0.5, np.float16)
-    m = ody.convert_to_fp32_master(h)
-    assert m.dtype == np.float32 and m[0] == 0.5
+def _cast_cases(half_bits, seed):
+    """float32 inputs for a cast to a 16-bit format: random magnitudes across
+    the format's range (subnormals and overflow included), exact midpoints
+    between neighbouring codes (ties, both parities), the values one float32
+    ulp either side of those ties, and the specials."""
+    rng = np.random.default_rng(seed)
+    up = ((lambda h: h.astype(np.float32)) if half_bits == "f16"
+          else (lambda h: (h.astype(np.uint32) << 16).view(np.float32)))
+    codes = rng.integers(0, 0x7C00 if half_bits == "f16" else 0x7F80, 20000).astype(np.uint16)
+    lo = up(codes.view(np.float16) if half_bits == "f16" else codes)
+    hi = up((codes + 1).view(np.float16) if half_bits == "f16" else codes + 1)
+    mid = ((lo.astype(np.float64) + hi.astype(np.float64)) / 2).astype(np.float32)  # exact in float32
+    near = np.concatenate([np.nextafter(mid, np.float32(np.inf)), np.nextafter(mid, np.float32(0))])
+    rnd = (rng.standard_normal(20000) * np.exp2(rng.uniform(-30, 20, 20000))).astype(np.float32)
+    spec = np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 65504.0, 65520.0, 65519.996, 6e-8, 3e-8, 2.9e-8,
+                     np.float32(3.4e38)], np.float32)
+    x = np.concatenate([lo, mid, near, rnd, spec])
+    sign = np.where(rng.random(x.size) < 0.5, np.float32(-1.0), np.float32(1.0))
+    return np.concatenate([x, x * sign]).astype(np.float32)
+
+
+def test_master_conversions(ody, oracle):
+    """update_model_from_master (mixed_precision.mojo:299-354) rounds to
+    FP16 / BF16 to nearest even: bit-exact against the oracle on random,
+    tie, near-tie, subnormal, overflow and special inputs; and
+    convert_to_fp32_master (:240-296) is the exact upcast of every FP16 and
+    BF16 bit pattern."""
+    for fmt, seed in (("f16", 1), ("bf16", 2)):
+        x = _cast_cases(fmt, seed)
+        if fmt == "f16":
+            model = np.zeros(x.size, np.float16)
+            ody.update_model_from_master(model, x)
+            got = model.view(np.uint16)
+            want = oracle.f32_to_f16_bits(x)
+        else:
+            model = np.zeros(x.size, np.uint16)
+            ody.update_model_from_master(model, x, dtype="bfloat16")
+            got = model
+            want = oracle.f32_to_bf16_bits(x)
+        nan = np.isnan(x)
+        np.testing.assert_array_equal(got[~nan], want[~nan], err_msg=fmt)
+        assert np.all(np.isnan(oracle.upcast(got[nan], 1 if fmt == "f16" else 2)))
+    every = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    m16 = ody.convert_to_fp32_master(every.view(np.float16))
+    want16 = oracle.upcast(every.view(np.float16))
+    nan16 = np.isnan(want16)  # the 2,046 NaN codes: NaN out (the payload is not part of the contract)
+    np.testing.assert_array_equal(m16.view(np.uint32)[~nan16], want16.view(np.uint32)[~nan16])
+    assert np.all(np.isnan(m16[nan16]))
+    mb = ody.convert_to_fp32_master(every, dtype="bfloat16")
+    np.testing.assert_array_equal(mb.view(np.uint32), (every.astype(np.uint32) << 16))
     p = np.full(100, 1.0, np.float16)
-    ody.update_model_from_master(p, np.full(100, 2.0, np.float32))
-    assert p[0] == 2.0
     with pytest.raises(ody.OdysseyError, match="sizes must match"):
         ody.update_model_from_master(p, np.zeros(3, np.float32))
+
+
+def test_single_ops_refuse_another_gpus_memory(ody):
+    """A device buffer of a GPU other than the current one is refused with
+    ODY_ERR_ARG before any launch."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    torch.cuda.set_device(0)
+    g = torch.ones(64, dtype=torch.float32, device="cuda:1")
+    with pytest.raises(ody.OdysseyError, match="another GPU") as ei:
+        ody.GradientScaler().unscale_gradients(g)
+    assert ei.value.code == -1
 
 
 @pytest.mark.parametrize("mode", [0, 1])

@@ -1,0 +1,224 @@
+// ody_fp4fast.cuh -- FP4 (E2M1) block encoding with one thread per block.
+//
+// The reference encodes each element as the ladder code of q = RN(x / scale)
+// (IEEE division): <0.5 -> 0, <1.25 -> 1.0, <1.75 -> 1.5, <2.5 -> 2.0,
+// <3.5 -> 3.0, <5.0 -> 4.0, else 6.0, with the sign of q when q != 0
+// (mxfp4.mojo:144-224, nvfp4.mojo:125-205).
+//
+// Two facts make this cheap:
+//  1. The ladder depends only on the top 16 bits of |q|.  Its break points
+//     0.5, 1.25, 1.75, 2.5, 3.5, 5.0 are 0x3F00, 0x3FA0, 0x3FE0, 0x4020,
+//     0x4060, 0x40A0 as bit patterns >> 16 (all multiples of 0x20), so with
+//     h = bits(|q|) >> 16 the magnitude code is 0 for h < 0x3F00 and
+//     ((clamp(h, 0x3F60, 0x40A0) - 0x3EE0) >> 6) otherwise (2..7; code 1 is
+//     never produced).  Checked over every 16-bit h against the ladder.  Two
+//     elements are coded at once in the halves of one 32-bit word with the
+//     16x2 integer min/max instructions.
+//  2. q itself is exact with one multiply (and two FMAs for a scale that is
+//     not a power of two): MXFP4 scales are powers of two, so x * 2^-k is
+//     RN(x / 2^k); for an E4M3 (or per-tensor) scale s with r = RN(1/s),
+//     q0 = x*r, q = q0 + (x - q0*s)*r (the remainder exact by FMA) is the
+//     correctly rounded quotient while nothing under- or overflows
+//     (Markstein).  Blocks where that can fail (a non-finite element, a
+//     quotient amax past 2^120, a zero scale) take the reference's
+//     element-by-element division instead, and elements too small for the
+//     range condition have |q| far below 0.5, where any nearby value codes
+//     the same.
+// The sign of a nonzero q is decided exactly with the per-scale threshold
+// t0 = least |x| with RN(|x| / scale) > 0 (x <= -t0), as in the threshold
+// tables.
+#pragma once
+#include <stdint.h>
+
+#include "ody_numerics.cuh"
+
+namespace ody {
+
+// Exact division x / s with s's reciprocal r = RN(1/s) precomputed: the
+// product estimate is corrected once with the exactly computed remainder
+// (Markstein's correction: q0 = x*r is within one ulp, x - q0*s is exact by
+// FMA, and q0 + rem*r rounded once is the correctly rounded quotient when r
+// is the correctly rounded reciprocal, provided nothing under- or overflows:
+// the remainder is a multiple of about ulp(x) * 2^-24, exact only while |x|
+// stays above 2^-100).  Zero, non-finite and extreme magnitudes take the
+// IEEE division.
+__device__ __forceinline__ float div_by(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float q = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
+  const float aq = fabsf(q0), ax = fabsf(x);
+  return (aq >= 0x1p-125f && aq <= 0x1p+125f && ax >= 0x1p-100f && ax <= 0x1p+125f) ? q : __fdiv_rn(x, s);
+}
+
+// Block scale value amax / 6 (block_scale_value) through the exact
+// reciprocal division.
+__device__ __forceinline__ float block_scale_value_fast(float amax) {
+  float v = div_by(amax, 6.0f, __frcp_rn(6.0f));
+  if (v < 1e-10f) v = 1.0f;
+  return v;
+}
+
+
+__device__ __forceinline__ uint32_t u16x2_max(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t u16x2_min(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// prmt in its default mode: a selector nibble with bit 3 set replicates the
+// sign bit of the selected byte
+__device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(d) : "r"(a), "r"(sel));
+  return d;
+}
+// all ones when a <= b (false for NaN)
+__device__ __forceinline__ uint32_t set_le(float a, float b) {
+  uint32_t d;
+  asm("set.le.u32.f32 %0, %1, %2;" : "=r"(d) : "f"(a), "f"(b));
+  return d;
+}
+// three-input max that propagates NaN (a NaN element marks the block special)
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// q = RN(x / s) from r = RN(1/s) (valid range: see the header comment)
+__device__ __forceinline__ float div_mk(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  return __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
+}
+
+// One byte of two codes: element a (quotient qa, value xa) in the high
+// nibble, element b in the low nibble.  neg_t0 = -t0 of the block's scale.
+// Only bits 0..7 of the result are meaningful.
+__device__ __forceinline__ uint32_t fp4_pair_byte(float qa, float qb, float xa, float xb, float neg_t0) {
+  // low half: hi16(|qb|), high half: hi16(|qa|)
+  const uint32_t H = __byte_perm(__float_as_uint(qb), __float_as_uint(qa), 0x7632) & 0x7FFF7FFFu;
+  uint32_t C = u16x2_min(u16x2_max(H, 0x3F603F60u), 0x40A040A0u);
+  C = (C - 0x3EE03EE0u) >> 6;
+  // bit 15 of each half of T: h >= 0x3F00 (|q| >= 0.5); spread to 0xFFFF
+  const uint32_t M = prmt_sign(H + 0x41004100u, 0xBB99u);
+  C &= 0x00070007u & M;
+  C |= set_le(xa, neg_t0) & 0x00080000u;
+  C |= set_le(xb, neg_t0) & 0x00000008u;
+  return C | (C >> 12);
+}
+
+// 8 codes (4 bytes, element 2i in the high nibble of byte i) of quotients q
+// and values x
+__device__ __forceinline__ uint32_t fp4_word(const float* q, const float* x, float neg_t0) {
+  const uint32_t b0 = fp4_pair_byte(q[0], q[1], x[0], x[1], neg_t0);
+  const uint32_t b1 = fp4_pair_byte(q[2], q[3], x[2], x[3], neg_t0);
+  const uint32_t b2 = fp4_pair_byte(q[4], q[5], x[4], x[5], neg_t0);
+  const uint32_t b3 = fp4_pair_byte(q[6], q[7], x[6], x[7], neg_t0);
+  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
+// 8 codes by the reference's element-wise rule (thresholds of the block's
+// scale; the special cases of NaN / Inf elements and a zero scale)
+__device__ __forceinline__ uint32_t fp4_word_slow(const float* x, const float* t, bool scale_zero) {
+  uint32_t w = 0;
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+    w |= ((fp4_encode(x[2 * i], t, scale_zero) << 4) | fp4_encode(x[2 * i + 1], t, scale_zero)) << (8 * i);
+  return w;
+}
+
+// a warp's staged bytes out: 16-byte stores when the whole slice may be
+// written and the destination is aligned, else bytes up to limit
+__device__ __forceinline__ void flush_warp_bytes(const uint8_t* ws, uint8_t* dst, int nbytes, int64_t limit) {
+  const int lane = threadIdx.x & 31;
+  if (limit >= nbytes && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    for (int i = lane; i < nbytes / 16; i += 32)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(ws)[i];
+  } else {
+    const int m = (int)(limit < nbytes ? (limit > 0 ? limit : 0) : nbytes);
+    for (int i = lane; i < m; i += 32) dst[i] = ws[i];
+  }
+}
+
+// Per-code constants of the NVFP4 E4M3 block scales: RN(1/scale) and t0.
+struct __align__(8) NvScaleConst {
+  float rcp;
+  float t0;
+};
+
+// ---- one NVFP4 block (16 elements) -------------------------------------
+// x: the block's values (zero padded).  TS: per-tensor scale st (r_st =
+// RN(1/st)) applied first, as the reference's x / s_t before the block
+// encode; t0_ts[e] is then the composite t0 of E4M3 code e for this st.
+// Writes the 8 code bytes (w[0], w[1]) and returns the scale byte.
+template <bool TS>
+__device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, float rst, bool st_fast,
+                                                    const float* t0_ts, const NvScaleConst* nvc,
+                                                    const Fp4Thr* thr_nv, uint32_t* w) {
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 16; k += 2) am = max3_nan(am, fabsf(x[k]), fabsf(x[k + 1]));
+  // am: NaN when an element is NaN, +Inf when one is infinite
+  const float amq = TS ? div_by(am, st, rst) : am;
+  const uint32_t e = e4m3_scale_from_f32(block_scale_value_fast(amq));
+  const bool fast = st_fast && amq <= 0x1p120f && e != 0;  // false for NaN / Inf
+  if (fast) {
+    const float bs = e4m3_to_f32((uint8_t)e);
+    const NvScaleConst c = nvc[e];
+    const float neg_t0 = -(TS ? t0_ts[e] : c.t0);
+    float q[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) q[k] = div_mk(TS ? div_mk(x[k], st, rst) : x[k], bs, c.rcp);
+    w[0] = fp4_word(q, x, neg_t0);
+    w[1] = fp4_word(q + 8, x + 8, neg_t0);
+    return e;
+  }
+  // the reference's path: amax ignoring NaN, element-wise IEEE division
+  float amr = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 16; k++) amr = amax_acc(amr, x[k]);
+  const float amrq = TS ? div_by(amr, st, rst) : amr;
+  const uint32_t er = e4m3_scale_from_f32(block_scale_value_fast(amrq));
+  float t[8];
+  thr_load(&thr_nv[er], t);
+  float y[16];
+#pragma unroll
+  for (int k = 0; k < 16; k++) y[k] = TS ? __fdiv_rn(x[k], st) : x[k];
+  w[0] = fp4_word_slow(y, t, er == 0);
+  w[1] = fp4_word_slow(y + 8, t, er == 0);
+  return er;
+}
+
+// ---- one MXFP4 block (32 elements) --------------------------------------
+// Writes the 16 code bytes (w[0..3]) and returns the E8M0 scale byte.
+__device__ __forceinline__ uint32_t mx_encode_block(const float* x, const Fp4Thr* thr_mx, uint32_t* w) {
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 32; k += 2) am = max3_nan(am, fabsf(x[k]), fabsf(x[k + 1]));
+  const uint32_t e = e8m0_from_f32(block_scale_value_fast(am));
+  if (am <= 0x1p127f && e >= 1 && e <= 254) {  // finite elements, a finite nonzero scale
+    // 1 / 2^(e-127) exactly (2^-127 is subnormal)
+    const float r = e <= 253 ? __uint_as_float((254u - e) << 23) : __uint_as_float(0x00400000u);
+    const float neg_t0 = -thr_mx[e].t[0];
+    float q[32];
+#pragma unroll
+    for (int k = 0; k < 32; k++) q[k] = __fmul_rn(x[k], r);
+#pragma unroll
+    for (int i = 0; i < 4; i++) w[i] = fp4_word(q + 8 * i, x + 8 * i, neg_t0);
+    return e;
+  }
+  float amr = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 32; k++) amr = amax_acc(amr, x[k]);
+  const uint32_t er = e8m0_from_f32(block_scale_value_fast(amr));
+  float t[8];
+  thr_load(&thr_mx[er], t);
+#pragma unroll
+  for (int i = 0; i < 4; i++) w[i] = fp4_word_slow(x + 8 * i, t, false);
+  return er;
+}
+
+}  // namespace ody

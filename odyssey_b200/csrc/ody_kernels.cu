@@ -16,7 +16,10 @@
 #include <math.h>
 #include <stdio.h>
 
+#include <algorithm>
+
 #include "ody_internal.h"
+#include "ody_fp4fast.cuh"
 
 namespace ody {
 
@@ -26,6 +29,7 @@ namespace ody {
 // ---------------------------------------------------------------------------
 __device__ Fp4Thr g_thr_mx[256];
 __device__ Fp4Thr g_thr_nv[128];
+__device__ NvScaleConst g_nv_const[128];  // RN(1/scale) and t0 per E4M3 scale code
 
 static float host_bits(uint32_t b) {
   float f;
@@ -73,6 +77,7 @@ static float host_e4m3_to_f32(int b) {
 }
 
 static Fp4Thr h_thr_mx[256], h_thr_nv[128];
+static NvScaleConst h_nv_const[128];
 static bool h_thr_ready = false;
 static bool d_thr_ready[64] = {false};
 
@@ -80,11 +85,17 @@ void upload_fp4_tables(int device) {
   if (!h_thr_ready) {
     for (int e = 0; e < 256; e++) host_fill_thr(host_e8m0_to_f32(e), &h_thr_mx[e]);
     for (int b = 0; b < 128; b++) host_fill_thr(b == 127 ? 0.0f : host_e4m3_to_f32(b), &h_thr_nv[b]);
+    for (int b = 0; b < 128; b++) {
+      volatile float s = b == 127 ? 0.0f : host_e4m3_to_f32(b);
+      h_nv_const[b].rcp = 1.0f / s;  // IEEE division on the host: RN(1/s)
+      h_nv_const[b].t0 = h_thr_nv[b].t[0];
+    }
     h_thr_ready = true;
   }
   if (device >= 0 && device < 64 && !d_thr_ready[device]) {
     cudaMemcpyToSymbol(g_thr_mx, h_thr_mx, sizeof(h_thr_mx));
     cudaMemcpyToSymbol(g_thr_nv, h_thr_nv, sizeof(h_thr_nv));
+    cudaMemcpyToSymbol(g_nv_const, h_nv_const, sizeof(h_nv_const));
     d_thr_ready[device] = true;
   }
 }
@@ -610,7 +621,7 @@ cudaError_t launch_finalize(const double* gathered, int world, DevScaler* scaler
 // nibble, then the scale byte) and writes it out with 16-byte (NVFP4, 144 B
 // per warp) or 8-byte (MXFP4, 136 B per warp) stores; no CTA-wide barrier.
 // ---------------------------------------------------------------------------
-constexpr int kWarpStage = 160;  // bytes of shared memory per warp
+constexpr int kWarpStage = 288;  // bytes of shared memory per warp (32 NVFP4 blocks)
 constexpr int kNvWarpBytes = 144;
 constexpr int kMxWarpBytes = 136;
 
@@ -622,29 +633,6 @@ __device__ __forceinline__ bool any_nonfinite8(const float v[8]) {
 #pragma unroll
   for (int k = 0; k < 8; k++) z = __fmaf_rn(v[k], 0.0f, z);
   return z != z;
-}
-
-// Exact division x / s with s's reciprocal r = RN(1/s) precomputed: the
-// product estimate is corrected once with the exactly computed remainder
-// (Markstein's correction: q0 = x*r is within one ulp, x - q0*s is exact by
-// FMA, and q0 + rem*r rounded once is the correctly rounded quotient when r
-// is the correctly rounded reciprocal, provided nothing under- or overflows:
-// the remainder is a multiple of about ulp(x) * 2^-24, exact only while |x|
-// stays above 2^-100).  Zero, non-finite and extreme magnitudes take the
-// IEEE division.
-__device__ __forceinline__ float div_by(float x, float s, float r) {
-  const float q0 = __fmul_rn(x, r);
-  const float q = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
-  const float aq = fabsf(q0), ax = fabsf(x);
-  return (aq >= 0x1p-125f && aq <= 0x1p+125f && ax >= 0x1p-100f && ax <= 0x1p+125f) ? q : __fdiv_rn(x, s);
-}
-
-// Block scale value amax / 6 (block_scale_value) through the exact
-// reciprocal division.
-__device__ __forceinline__ float block_scale_value_fast(float amax) {
-  float v = div_by(amax, 6.0f, __frcp_rn(6.0f));
-  if (v < 1e-10f) v = 1.0f;
-  return v;
 }
 
 // the threshold ladder without special cases (finite x, positive finite scale)
@@ -747,13 +735,6 @@ __device__ __forceinline__ float tensor_scale_from_amax(int kind, uint32_t amax_
 // for s_t once (one exact double product per threshold) and then encodes
 // the raw master with compares only, dividing once per block instead of once
 // per element.
-// The composite table covers the block-scale codes 64..127 (E4M3 2.0 up):
-// with s_t = amax / 2688 a block's q amax is at most 2688, so its scale code
-// is at most 0x7e, and only a block whose amax is below about 1/224 of the
-// tensor's falls under the table and divides element by element.
-constexpr int kCxFirst = 64;
-constexpr int kCxCount = 128 - kCxFirst;
-
 __device__ __forceinline__ float composite_threshold(float Q, float s) {
   // RN(y) >= Q exactly when y is at least the midpoint m between Q and its
   // predecessor (at a tie RN picks the even encoding: Q itself when Q's last
@@ -769,38 +750,6 @@ __device__ __forceinline__ float composite_threshold(float Q, float s) {
   float x = __double2float_ru(P);
   if ((qb & 1u) && (double)x == P) x = __uint_as_float(__float_as_uint(x) + 1u);
   return x;
-}
-
-// one warp's slice of an NVFP4 per-tensor-scaled tile from the raw master
-// values x (s_t > 0 finite); blocks with a non-finite element, an infinite
-// q amax or a zero block scale divide element by element as the reference does
-__device__ __forceinline__ void stage_nvfp4_tensor(const float x[8], uint8_t* ws, const Fp4Thr* thr_q,
-                                                   const Fp4Thr* thr_x, float st, float rst) {
-  float am = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 8; k++) am = amax_acc(am, x[k]);
-  am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-  const float amq = div_by(am, st, rst);
-  const uint8_t e = e4m3_scale_from_f32(block_scale_value_fast(amq));
-  const bool z = e == 0;
-  const bool special = e < kCxFirst || amq == __uint_as_float(0x7f800000u) || any_nonfinite8(x);
-  const int lane = threadIdx.x & 31;
-  uint8_t* dst = ws + (lane >> 1) * 9 + 4 * (lane & 1);
-  if (!special) {
-    float t[8];
-    thr_load(&thr_x[e - kCxFirst], t);
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-      dst[i] = (uint8_t)((fp4_encode_plain(x[2 * i], t) << 4) | fp4_encode_plain(x[2 * i + 1], t));
-  } else {
-    float t[8];
-    thr_load(&thr_q[e], t);
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-      dst[i] = (uint8_t)((fp4_encode(__fdiv_rn(x[2 * i], st), t, z) << 4) |
-                         fp4_encode(__fdiv_rn(x[2 * i + 1], st), t, z));
-  }
-  if (lane & 1) ws[(lane >> 1) * 9 + 8] = e;
 }
 
 __device__ __forceinline__ float block_amax_reduce(float v) {
@@ -964,8 +913,13 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
   }
 }
 
+// A requant job: one chunk of a per-tensor-scaled tensor once all of the
+// tensor's update jobs are done.  NVFP4: one thread per 16-element block
+// (ody_fp4fast.cuh), a warp per 32 consecutive blocks; FP8-E4M3: 8
+// elements per thread.  The CTA keeps the composite t0 table of the last
+// tensor it re-quantised.
 __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& ch, const Fp4Thr* s_nv,
-                                              Fp4Thr* s_cx, int* s_cx_tensor, uint8_t* stage) {
+                                              float* s_t0, int* s_t0_tensor, uint8_t* stage) {
   const TensorDesc td = a.tensors[ch.tensor];
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
@@ -990,18 +944,50 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
   const float s = tensor_scale_from_amax(kind, __ldcg(&a.amax_slots[ch.tensor]));
   const float r = __frcp_rn(s);
   if (ch.start == td.off && threadIdx.x == 0) a.qscale[ch.tensor] = s;
-  if (kind == Q_NVFP4_TENSOR && *s_cx_tensor != ch.tensor) {
-    // composite thresholds for this tensor's scale (kept for the CTA's next
-    // requant job of the same tensor)
-    float* cx = reinterpret_cast<float*>(s_cx);
-    const float* q = reinterpret_cast<const float*>(s_nv);
-    for (int i = threadIdx.x; i < kCxCount * 8; i += blockDim.x)
-      cx[i] = (i & 7) == 7 ? 0.0f : composite_threshold(q[kCxFirst * 8 + i], s);
-    __syncthreads();
-    if (threadIdx.x == 0) *s_cx_tensor = ch.tensor;
-  }
   const int64_t end = ch.start + ch.len;
-  // the next tile's master values are loaded before this tile is encoded
+  if (kind == Q_NVFP4_TENSOR) {
+    if (*s_t0_tensor != ch.tensor) {
+      // composite t0 of every E4M3 code for this tensor's scale (the sign rule)
+      for (int i = threadIdx.x; i < 128; i += blockDim.x) s_t0[i] = composite_threshold(s_nv[i].t[0], s);
+      __syncthreads();
+      if (threadIdx.x == 0) *s_t0_tensor = ch.tensor;
+    }
+    const bool st_fast = s >= 0x1p-60f && s <= 0x1p60f;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* ws = stage + w * kWarpStage;
+    const int64_t nb = ch.len / 16;
+    const int64_t blk0 = (ch.start - td.off) / 16;  // the chunk's first block within the tensor
+    for (int64_t b0 = (int64_t)w * 32; b0 < nb; b0 += (kThreads / 32) * 32) {
+      const int64_t b = b0 + lane;
+      float v[16];
+      if (b < nb) {
+        const float4* pp = reinterpret_cast<const float4*>(a.master + ch.start + b * 16);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const float4 t = __ldcg(pp + k);
+          v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 16; k++) v[k] = 0.0f;
+      }
+      uint32_t cw[2];
+      const uint32_t sb = nv_encode_block<true>(v, s, r, st_fast, s_t0, g_nv_const, s_nv, cw);
+      uint8_t* d = ws + lane * 9;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        d[k] = (uint8_t)(cw[0] >> (8 * k));
+        d[4 + k] = (uint8_t)(cw[1] >> (8 * k));
+      }
+      d[8] = (uint8_t)sb;
+      __syncwarp();
+      flush_warp_bytes(ws, a.qout + td.qoff + (blk0 + b0) * 9, 32 * 9, (nb - b0) * 9);
+      __syncwarp();
+    }
+    return;
+  }
+  // FP8-E4M3 with a per-tensor scale; the next tile's master values are
+  // loaded before this tile is encoded
   float4 n0 = make_float4(0.f, 0.f, 0.f, 0.f), n1 = n0;
   {
     const int64_t e0 = ch.start + (int64_t)threadIdx.x * kVec;
@@ -1024,25 +1010,8 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
     if (act) {
       x[0] = p0.x; x[1] = p0.y; x[2] = p0.z; x[3] = p0.w;
       x[4] = p1.x; x[5] = p1.y; x[6] = p1.z; x[7] = p1.w;
-      if (kind != Q_NVFP4_TENSOR) {
 #pragma unroll
-        for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 8; k++) x[k] = 0.0f;
-    }
-    if (kind == Q_NVFP4_TENSOR) {
-      if (tb + (int64_t)(threadIdx.x & ~31) * kVec < end) {
-        const int64_t tile_in_tensor = (tb - td.off) / kTile;
-        const int w = threadIdx.x >> 5;
-        uint8_t* ws = stage + w * kWarpStage;
-        stage_nvfp4_tensor(x, ws, s_nv, s_cx, s, r);
-        __syncwarp();
-        flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
-        __syncwarp();
-      }
-    } else if (act) {
+      for (int k = 0; k < 8; k++) x[k] = div_by(x[k], s, r);
       store_elem8(Q_FP8_E4M3, x, a.qout + td.qoff + (e0 - td.off));
     }
   }
@@ -1053,8 +1022,8 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ Fp4Thr s_mx[256];
   __shared__ Fp4Thr s_nv[128];
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
-  __shared__ Fp4Thr s_cx[kCxCount];
-  __shared__ int s_cx_tensor;
+  __shared__ float s_t0[128];
+  __shared__ int s_t0_tensor;
   __shared__ uint32_t s_next;
   // prologue independent of the preceding stats/finalize grid
   load_thr_smem(s_mx, s_nv);
@@ -1067,7 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   const float coef = dec->coef;
   if (threadIdx.x == 0) {
     s_next = atomicAdd(&a.sync[0], 1u);
-    s_cx_tensor = -1;
+    s_t0_tensor = -1;
   }
   __syncthreads();
   uint32_t j = s_next;
@@ -1077,7 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
     const uint32_t job = a.jobs[j];
     const Chunk ch = a.chunks[job & ~kRequantJob];
     if (job & kRequantJob)
-      requant_chunk(a, ch, s_nv, s_cx, &s_cx_tensor, stage);
+      requant_chunk(a, ch, s_nv, s_t0, &s_t0_tensor, stage);
     else
       update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, stage);
     __syncthreads();
@@ -1250,39 +1219,16 @@ cudaError_t launch_amax(int sdt, const void* x, int64_t n, uint32_t* amax, cudaS
   return cudaGetLastError();
 }
 
+// FP16 / BF16 / FP8 kinds (with or without a per-tensor scale): 8 elements
+// per thread, the next tile's values loaded before this tile is converted.
 __global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, int sdt, const void* x, int64_t n,
                                                             uint8_t* out, int64_t out_bytes,
                                                             const uint32_t* amax, float* tscale) {
-  __shared__ Fp4Thr s_mx[256];
-  __shared__ Fp4Thr s_nv[128];
-  __shared__ Fp4Thr s_cx[kCxCount];
-  __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
-  // only the table this format reads
-  if (kind == Q_MXFP4) {
-    float* d = reinterpret_cast<float*>(s_mx);
-    const float* g = reinterpret_cast<const float*>(g_thr_mx);
-    for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) d[i] = g[i];
-  } else if (kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
-    float* d = reinterpret_cast<float*>(s_nv);
-    const float* g = reinterpret_cast<const float*>(g_thr_nv);
-    for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x) d[i] = g[i];
-  }
-  __syncthreads();
-  const bool scaled = (kind == Q_NVFP4_TENSOR || kind == Q_FP8_E4M3_TENSOR);
+  const bool scaled = kind == Q_FP8_E4M3_TENSOR;
   const float s = scaled ? tensor_scale_from_amax(kind, *amax) : 1.0f;
   const float r = __frcp_rn(s);
   if (blockIdx.x == 0 && threadIdx.x == 0 && tscale) *tscale = s;
-  if (kind == Q_NVFP4_TENSOR) {
-    // composite thresholds for s (see stage_nvfp4_tensor): compares of the
-    // raw values, one division per block
-    float* cx = reinterpret_cast<float*>(s_cx);
-    const float* q = reinterpret_cast<const float*>(s_nv);
-    for (int i = threadIdx.x; i < kCxCount * 8; i += blockDim.x)
-      cx[i] = (i & 7) == 7 ? 0.0f : composite_threshold(q[kCxFirst * 8 + i], s);
-    __syncthreads();
-  }
   const int64_t ntiles = (n + kTile - 1) / kTile;
-  // the next tile's values are loaded before this tile is encoded
   float nx[8];
   if ((int64_t)blockIdx.x < ntiles) load_src8(sdt, x, n, (int64_t)blockIdx.x * kTile + (int64_t)threadIdx.x * kVec, nx);
   for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -1291,46 +1237,96 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(int kind, int sdt, c
 #pragma unroll
     for (int k = 0; k < 8; k++) v[k] = nx[k];
     if (t + gridDim.x < ntiles) load_src8(sdt, x, n, e0 + (int64_t)gridDim.x * kTile, nx);
-    if (kind == Q_FP8_E4M3_TENSOR) {
+    if (scaled) {
 #pragma unroll
       for (int k = 0; k < 8; k++) v[k] = div_by(v[k], s, r);
     }
-    if (kind == Q_MXFP4 || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
-      const int w = threadIdx.x >> 5;
-      uint8_t* ws = stage + w * kWarpStage;
-      if (kind == Q_MXFP4) {
-        stage_fp4<true>(v, ws, s_mx);
-        __syncwarp();
-        const int64_t off = t * kMxTileBytes + w * kMxWarpBytes;
-        flush_warp<true>(ws, out + off, out_bytes - off);
-      } else {
-        if (kind == Q_NVFP4_TENSOR)
-          stage_nvfp4_tensor(v, ws, s_nv, s_cx, s, r);
-        else
-          stage_fp4<false>(v, ws, s_nv);
-        __syncwarp();
-        const int64_t off = t * kNvTileBytes + w * kNvWarpBytes;
-        flush_warp<false>(ws, out + off, out_bytes - off);
-      }
-      __syncwarp();
+    const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
+    const int qk = scaled ? Q_FP8_E4M3 : kind;
+    uint8_t* dst = out + e0 * esz;
+    if (e0 + 8 <= n && (reinterpret_cast<uintptr_t>(dst) & (esz == 2 ? 15u : 7u)) == 0) {
+      store_elem8(qk, v, dst);
     } else {
-      const int esz = (kind == Q_FP16 || kind == Q_BF16) ? 2 : 1;
-      const int qk = kind == Q_FP8_E4M3_TENSOR ? Q_FP8_E4M3 : kind;
-      uint8_t* dst = out + e0 * esz;
-      if (e0 + 8 <= n && (reinterpret_cast<uintptr_t>(dst) & (esz == 2 ? 15u : 7u)) == 0) {
-        store_elem8(qk, v, dst);
-      } else {
-        for (int k = 0; k < 8 && e0 + k < n; k++) {
-          if (esz == 2) {
-            uint16_t h = qk == Q_FP16 ? f32_to_f16_bits(v[k]) : f32_to_bf16_bits(v[k]);
-            reinterpret_cast<uint16_t*>(out)[e0 + k] = h;
-          } else {
-            out[e0 + k] = qk == Q_FP8_E5M2 ? f32_to_e5m2(v[k]) : f32_to_e4m3(v[k]);
-          }
+      for (int k = 0; k < 8 && e0 + k < n; k++) {
+        if (esz == 2) {
+          uint16_t h = qk == Q_FP16 ? f32_to_f16_bits(v[k]) : f32_to_bf16_bits(v[k]);
+          reinterpret_cast<uint16_t*>(out)[e0 + k] = h;
+        } else {
+          out[e0 + k] = qk == Q_FP8_E5M2 ? f32_to_e5m2(v[k]) : f32_to_e4m3(v[k]);
         }
       }
     }
   }
+  (void)out_bytes;
+}
+
+// ---------------------------------------------------------------------------
+// FP4 kinds: one thread per block (16 elements for NVFP4, 32 for MXFP4),
+// encoded with the cheap exact path of ody_fp4fast.cuh.  A warp covers 32
+// consecutive blocks, whose 288 (NVFP4) or 544 (MXFP4) output bytes it
+// stages in shared memory and writes with 16-byte stores.
+// ---------------------------------------------------------------------------
+template <int SDT, int NE>
+__device__ __forceinline__ void load_block(const void* x, int64_t n, int64_t e0, float* v) {
+#pragma unroll
+  for (int k = 0; k < NE; k += 8) load_src8(SDT, x, n, e0 + k, v + k);
+}
+
+template <int KIND, int SDT>
+__global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int64_t n, uint8_t* out,
+                                                             int64_t out_bytes, const uint32_t* amax,
+                                                             float* tscale) {
+  constexpr bool MX = KIND == Q_MXFP4;
+  constexpr bool TS = KIND == Q_NVFP4_TENSOR;
+  constexpr int BE = MX ? 32 : 16;  // elements per block
+  constexpr int BB = MX ? 17 : 9;   // bytes per block
+  constexpr int WB = 32 * BB;       // bytes per warp
+  __shared__ __align__(16) uint8_t stage[kThreads / 32][WB];
+  __shared__ float s_t0[TS ? 128 : 1];
+  float st = 1.0f, rst = 1.0f;
+  bool st_fast = true;
+  if (TS) {
+    st = tensor_scale_from_amax(KIND, *amax);
+    rst = __frcp_rn(st);
+    st_fast = st >= 0x1p-60f && st <= 0x1p60f;
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) s_t0[i] = composite_threshold(g_thr_nv[i].t[0], st);
+    __syncthreads();
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && tscale) *tscale = st;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ws = stage[w];
+  const int64_t nblocks = (n + BE - 1) / BE;
+  const int64_t step = (int64_t)gridDim.x * (kThreads / 32) * 32;
+  for (int64_t b0 = ((int64_t)blockIdx.x * (kThreads / 32) + w) * 32; b0 < nblocks; b0 += step) {
+    const int64_t b = b0 + lane;
+    float v[BE];
+    load_block<SDT, BE>(x, n, b * BE, v);  // zero beyond n
+    uint32_t cw[BE / 8];
+    uint32_t sb;
+    if (MX)
+      sb = mx_encode_block(v, g_thr_mx, cw);
+    else
+      sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, cw);
+    uint8_t* d = ws + lane * BB;
+#pragma unroll
+    for (int i = 0; i < BE / 8; i++) {
+#pragma unroll
+      for (int k = 0; k < 4; k++) d[4 * i + k] = (uint8_t)(cw[i] >> (8 * k));
+    }
+    d[BB - 1] = (uint8_t)sb;
+    __syncwarp();
+    flush_warp_bytes(ws, out + b0 * BB, WB, out_bytes - b0 * BB);
+    __syncwarp();
+  }
+}
+
+template <int KIND>
+static void launch_fp4_kind(int sdt, const void* x, int64_t n, uint8_t* out, int64_t out_bytes, const uint32_t* amax,
+                            float* tscale, int grid, cudaStream_t st) {
+  if (sdt == DT_F32)
+    quant_fp4_kernel<KIND, DT_F32><<<grid, kThreads, 0, st>>>(x, n, out, out_bytes, amax, tscale);
+  else
+    quant_fp4_kernel<KIND, DT_BF16><<<grid, kThreads, 0, st>>>(x, n, out, out_bytes, amax, tscale);
 }
 
 static int64_t quant_bytes_dev(int kind, int64_t n) {
@@ -1353,6 +1349,21 @@ static int64_t quant_bytes_dev(int kind, int64_t n) {
 
 cudaError_t launch_quantize(int kind, int sdt, const void* x, int64_t n, uint8_t* out,
                             const uint32_t* amax, float* tscale, cudaStream_t st) {
+  if (kind == Q_MXFP4 || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
+    const int64_t be = kind == Q_MXFP4 ? 32 : 16;
+    const int64_t warps = ((n + be - 1) / be + 31) / 32;
+    const int64_t want = (warps + kThreads / 32 - 1) / (kThreads / 32);
+    const int64_t cap = (int64_t)sm_count() * 4;
+    const int grid = (int)std::max<int64_t>(1, std::min(want, cap));
+    const int64_t ob = quant_bytes_dev(kind, n);
+    if (kind == Q_MXFP4)
+      launch_fp4_kind<Q_MXFP4>(sdt, x, n, out, ob, amax, tscale, grid, st);
+    else if (kind == Q_NVFP4)
+      launch_fp4_kind<Q_NVFP4>(sdt, x, n, out, ob, amax, tscale, grid, st);
+    else
+      launch_fp4_kind<Q_NVFP4_TENSOR>(sdt, x, n, out, ob, amax, tscale, grid, st);
+    return cudaGetLastError();
+  }
   int64_t ntiles = (n + kTile - 1) / kTile;
   int64_t cap = (int64_t)sm_count() * 8;
   int grid = (int)(ntiles < cap ? ntiles : cap);

@@ -469,3 +469,45 @@ def test_double_buffered_gradients(oracle, graph):
     assert r["skipped"] == ro.skipped and r["clip_coef"] == ro.coef
     compare_state(ctx, model, wl.numels, [wl.quant] * len(wl.numels), wl.optimizer)
     ctx.close()
+
+
+def test_resnet18_adamw_fp8_tensor_1000_steps(oracle):
+    """Config 4 at its stated length: 1,000 AdamW steps (numbered 1..1000) on
+    ResNet-18 with an inf injected on every 100th step, FP8-E4M3 per-tensor
+    requant, against the oracle (state compared every 100 steps).  Exactly
+    the 10 inf steps are skipped, each backs the scale off by half, and the
+    step / overflow counters match (the reference's overflow-recovery
+    sequence, test_multi_precision_training.mojo:141-177)."""
+    from odyssey_b200 import MixedPrecisionStep
+    wl = W.resnet18()  # inf_every = 100
+    kw = wl.step_kwargs()
+    ctx = MixedPrecisionStep(wl.numels, **kw)
+    specs = [{"numel": n, "grad_dtype": GDT[wl.grad_dtype], "quant": QK[wl.quant]} for n in wl.numels]
+    hy = wl.hyper
+    sk = {k: kw[k] for k in ("initial_scale", "growth_factor", "backoff_factor", "growth_interval", "min_scale",
+                             "max_scale")}
+    model = oracle.Model(specs, OPT[wl.optimizer], hy["learning_rate"], beta1=hy["beta1"], beta2=hy["beta2"],
+                         epsilon=hy["epsilon"], weight_decay=hy["weight_decay"], scaler_kwargs=sk)
+    for i, m in enumerate(wl.master(0)):
+        ctx.set_master(i, m)
+        model.master[i][:] = m
+    qlist = [wl.quant] * len(wl.numels)
+    t, skipped, scales = 1, [], []
+    for s in range(1, 1001):
+        grads = wl.grads(s)
+        for i, g in enumerate(grads):
+            ctx.set_grad(i, g)
+        r = ctx.step(t)
+        ro = model.step(grads, t)
+        assert r["skipped"] == ro.skipped and r["scale_next"] == ro.scale_next, s
+        assert r["step_count"] == ro.step_count == s and r["overflow_count"] == ro.overflow_count, s
+        if r["skipped"]:
+            skipped.append(s)
+            scales.append(r["scale_next"])
+        else:
+            t += 1
+        if s % 100 == 0:
+            compare_state(ctx, model, wl.numels, qlist, wl.optimizer)
+    assert skipped == list(range(100, 1001, 100))
+    assert scales == [65536.0 * 0.5 ** k for k in range(1, 11)]
+    ctx.close()

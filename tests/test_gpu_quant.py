@@ -107,6 +107,66 @@ def test_fp4_threshold_tables_every_scale(ody, oracle, kind):
     np.testing.assert_array_equal(got, want)
 
 
+def _ulp_sweep(c, k):
+    """float32 values k ulps either side of each c (same sign), c included."""
+    b = np.asarray(c, np.float32).view(np.int32).astype(np.int64)
+    out = (b[:, None] + np.arange(-k, k + 1)[None, :]).ravel()
+    out = out[(out > 0) & (out < 0x7F800000)]
+    return out.astype(np.int32).view(np.float32)
+
+
+def _boundary_blocks(B, scales, mult, rng):
+    """Blocks of B elements: element 0 = 6 * scale * mult (selects the block
+    scale), the rest sweep the ladder break points T * scale * mult and the
+    smallest quotients, +-8 ulps, both signs."""
+    T = np.float32([0.5, 1.25, 1.75, 2.5, 3.5, 5.0])
+    blocks = []
+    for sc in scales:
+        sc = np.float32(sc)
+        pts = np.concatenate([_ulp_sweep(T * sc * np.float32(mult), 8),
+                              _ulp_sweep(np.float32([2.0 ** -149, 2.0 ** -148, 1e-40]) * sc, 3)])
+        pts = pts * np.where(rng.random(pts.size) < 0.5, np.float32(-1), np.float32(1))
+        head = np.float32(6.0) * sc * np.float32(mult)
+        for i in range(0, pts.size, B - 1):
+            blk = np.zeros(B, np.float32)
+            chunk = pts[i:i + B - 1]
+            blk[1:1 + chunk.size] = chunk
+            blk[0] = head
+            blocks.append(blk)
+    return np.concatenate(blocks)
+
+
+@pytest.mark.parametrize("kind", [6, 7, 8])
+def test_fp4_encode_break_points_every_scale(ody, oracle, kind):
+    """The one-thread-per-block encoder (exact quotient + top-16-bit ladder)
+    against the oracle's IEEE division at every ladder break point +-8 ulps,
+    for every block scale the format reaches: all E4M3 codes (NVFP4), E8M0
+    exponents 2^-120..2^120 (MXFP4), and for the per-tensor-scaled NVFP4
+    several tensor scales (the tensor amax set by one extra element)."""
+    rng = np.random.default_rng(11)
+    if kind == 6:
+        scales = 2.0 ** np.arange(-120, 121, 3, dtype=np.float64)
+        x = _boundary_blocks(32, scales, 1.0, rng)
+        got, _ = _gpu_quant(ody, kind, x)
+        want, _ = oracle.quantize(kind, x)
+        np.testing.assert_array_equal(got, want)
+        return
+    e4m3 = oracle.e4m3_to_f32(np.arange(1, 127, dtype=np.uint8))
+    mults = [1.0] if kind == 7 else [1.0, 3.7e-5, 1e-3, 2.5e7]
+    for mult in mults:
+        x = _boundary_blocks(16, e4m3, mult, rng)
+        if kind == 8:
+            # the tensor's amax (one more block) sets s_t = amax / 2688, so
+            # that q = x / s_t puts block scales on every E4M3 code
+            tail = np.zeros(16, np.float32)
+            tail[0] = np.float32(2688.0 * mult)
+            x = np.concatenate([x, tail])
+        got, ts = _gpu_quant(ody, kind, x)
+        want, wts = oracle.quantize(kind, x)
+        np.testing.assert_array_equal(got, want, err_msg=f"mult {mult}")
+        assert np.float32(ts) == np.float32(wts)
+
+
 @pytest.mark.parametrize("kind", KINDS)
 def test_dequantize_bit_exact(ody, oracle, kind):
     x = np.nan_to_num(_mixed(4099, kind), nan=0.0, posinf=1.0, neginf=-1.0)

@@ -143,6 +143,24 @@ __device__ __forceinline__ void flush_warp_bytes(const uint8_t* ws, uint8_t* dst
   }
 }
 
+// ---- asynchronous global -> shared copies (cp.async, 16 bytes per thread) --
+// bytes < 16 zero-fills the rest of the 16-byte slot (bytes 0: all zeros)
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+// 16-byte slot p of a staged segment, XOR-swizzled within each 128-byte row
+// so that both the coalesced fill (consecutive lanes, consecutive slots) and
+// the per-block read (lane l takes slots l*P .. l*P+P-1) hit distinct banks
+__device__ __forceinline__ int swz16(int p) { return (p & ~7) | ((p ^ (p >> 3)) & 7); }
+
 // Per-code constants of the NVFP4 E4M3 block scales: RN(1/scale) and t0.
 struct __align__(8) NvScaleConst {
   float rcp;

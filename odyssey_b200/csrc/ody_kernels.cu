@@ -1320,6 +1320,143 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int6
   }
 }
 
+// The same with the input staged through shared memory: each warp fills a
+// ring of kFp4Stages segments (32 blocks each) with coalesced 16-byte
+// cp.async copies, several segments ahead of the one it encodes, so that the
+// loads of a thread are neither strided nor waited for one block at a time.
+// Needs a 16-byte-aligned source.
+constexpr int kFp4Stages = 3;
+
+template <int KIND, int SDT>
+struct Fp4Pipe {
+  static constexpr int BE = KIND == Q_MXFP4 ? 32 : 16;
+  static constexpr int BB = KIND == Q_MXFP4 ? 17 : 9;
+  static constexpr int ESZ = SDT == DT_F32 ? 4 : 2;
+  static constexpr int P = BE * ESZ / 16;  // 16-byte slots per block
+  static constexpr int SEG = 32 * P * 16;  // input bytes per warp segment
+  static constexpr int WB = (32 * BB + 15) / 16 * 16;
+  static constexpr int SMEM = (kThreads / 32) * (kFp4Stages * SEG + WB);
+};
+
+template <int KIND, int SDT>
+__global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x, int64_t n, uint8_t* out,
+                                                                  int64_t out_bytes, const uint32_t* amax,
+                                                                  float* tscale) {
+  using PP = Fp4Pipe<KIND, SDT>;
+  constexpr bool MX = KIND == Q_MXFP4;
+  constexpr bool TS = KIND == Q_NVFP4_TENSOR;
+  constexpr int NS = kFp4Stages;
+  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ float s_t0[TS ? 128 : 1];
+  float st = 1.0f, rst = 1.0f;
+  bool st_fast = true;
+  if (TS) {
+    st = tensor_scale_from_amax(KIND, *amax);
+    rst = __frcp_rn(st);
+    st_fast = st >= 0x1p-60f && st <= 0x1p60f;
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) s_t0[i] = composite_threshold(g_thr_nv[i].t[0], st);
+    __syncthreads();
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && tscale) *tscale = st;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = dsm + w * (NS * PP::SEG);
+  uint8_t* ws = dsm + (kThreads / 32) * (NS * PP::SEG) + w * PP::WB;
+  const int64_t in_bytes = n * PP::ESZ;
+  const int64_t ngroups = ((n + PP::BE - 1) / PP::BE + 31) / 32;
+  const int64_t gstep = (int64_t)gridDim.x * (kThreads / 32);
+  const int64_t g0 = (int64_t)blockIdx.x * (kThreads / 32) + w;
+  const char* src = reinterpret_cast<const char*>(x);
+  auto issue = [&](int64_t g, int s) {
+    const uint32_t base = smem_u32(ring + s * PP::SEG);
+#pragma unroll
+    for (int k = 0; k < PP::P; k++) {
+      const int p = k * 32 + lane;
+      const int64_t off = g * PP::SEG + (int64_t)p * 16;
+      const int64_t rem = in_bytes - off;
+      const int bytes = rem >= 16 ? 16 : (rem > 0 ? (int)rem : 0);
+      cp_async16(base + swz16(p) * 16, bytes > 0 ? src + off : src, bytes);
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < NS - 1; s++) {
+    const int64_t g = g0 + s * gstep;
+    if (g < ngroups) issue(g, s);
+    cp_async_commit();
+  }
+  int cur = 0;
+  for (int64_t g = g0; g < ngroups; g += gstep) {
+    const int64_t gn = g + (NS - 1) * gstep;
+    if (gn < ngroups) issue(gn, cur == 0 ? NS - 1 : cur - 1);
+    cp_async_commit();
+    cp_async_wait<NS - 1>();
+    __syncwarp();
+    float v[PP::BE];
+    const uint8_t* seg = ring + cur * PP::SEG;
+#pragma unroll
+    for (int j = 0; j < PP::P; j++) {
+      const uint4 r = *reinterpret_cast<const uint4*>(seg + swz16(lane * PP::P + j) * 16);
+      if (SDT == DT_F32) {
+        v[4 * j] = __uint_as_float(r.x);
+        v[4 * j + 1] = __uint_as_float(r.y);
+        v[4 * j + 2] = __uint_as_float(r.z);
+        v[4 * j + 3] = __uint_as_float(r.w);
+      } else {
+        const uint32_t ww[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          v[8 * j + 2 * k] = __uint_as_float(ww[k] << 16);
+          v[8 * j + 2 * k + 1] = __uint_as_float(ww[k] & 0xFFFF0000u);
+        }
+      }
+    }
+    __syncwarp();  // every lane has its block: the slot may be refilled
+    uint32_t cw[PP::BE / 8];
+    uint32_t sb;
+    if (MX)
+      sb = mx_encode_block(v, g_thr_mx, cw);
+    else
+      sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, cw);
+    uint8_t* d = ws + lane * PP::BB;
+#pragma unroll
+    for (int i = 0; i < PP::BE / 8; i++) {
+#pragma unroll
+      for (int k = 0; k < 4; k++) d[4 * i + k] = (uint8_t)(cw[i] >> (8 * k));
+    }
+    d[PP::BB - 1] = (uint8_t)sb;
+    __syncwarp();
+    const int64_t ob = g * 32 * PP::BB;
+    flush_warp_bytes(ws, out + ob, 32 * PP::BB, out_bytes - ob);
+    __syncwarp();
+    cur = cur + 1 == NS ? 0 : cur + 1;
+  }
+  cp_async_wait<0>();
+}
+
+template <int KIND, int SDT>
+static cudaError_t launch_fp4_pipe(const void* x, int64_t n, uint8_t* out, int64_t out_bytes, const uint32_t* amax,
+                                   float* tscale, cudaStream_t st) {
+  using PP = Fp4Pipe<KIND, SDT>;
+  static int per_sm[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto fn = quant_fp4_pipe_kernel<KIND, SDT>;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (per_sm[dev] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, PP::SMEM);
+    if (e != cudaSuccess) return e;
+    int k = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, fn, kThreads, PP::SMEM);
+    if (e != cudaSuccess) return e;
+    per_sm[dev] = k > 0 ? k : 1;
+  }
+  const int64_t groups = ((n + PP::BE - 1) / PP::BE + 31) / 32;
+  const int64_t want = (groups + kThreads / 32 - 1) / (kThreads / 32);
+  const int64_t cap = (int64_t)sm_count() * per_sm[dev];
+  const int grid = (int)std::max<int64_t>(1, std::min(want, cap));
+  fn<<<grid, kThreads, PP::SMEM, st>>>(x, n, out, out_bytes, amax, tscale);
+  return cudaGetLastError();
+}
+
 template <int KIND>
 static void launch_fp4_kind(int sdt, const void* x, int64_t n, uint8_t* out, int64_t out_bytes, const uint32_t* amax,
                             float* tscale, int grid, cudaStream_t st) {
@@ -1356,6 +1493,14 @@ cudaError_t launch_quantize(int kind, int sdt, const void* x, int64_t n, uint8_t
     const int64_t cap = (int64_t)sm_count() * 4;
     const int grid = (int)std::max<int64_t>(1, std::min(want, cap));
     const int64_t ob = quant_bytes_dev(kind, n);
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+#define ODY_P(K)                                                                          \
+  if (kind == K)                                                                          \
+    return sdt == DT_F32 ? launch_fp4_pipe<K, DT_F32>(x, n, out, ob, amax, tscale, st)    \
+                         : launch_fp4_pipe<K, DT_BF16>(x, n, out, ob, amax, tscale, st);
+      ODY_P(Q_MXFP4) ODY_P(Q_NVFP4) ODY_P(Q_NVFP4_TENSOR)
+#undef ODY_P
+    }
     if (kind == Q_MXFP4)
       launch_fp4_kind<Q_MXFP4>(sdt, x, n, out, ob, amax, tscale, grid, st);
     else if (kind == Q_NVFP4)

@@ -225,6 +225,29 @@ def test_device_pointers_via_torch(ody, oracle):
     np.testing.assert_array_equal(d.cpu().numpy()[: x.size], oracle.dequantize(7, want, x.size))
 
 
+@pytest.mark.parametrize("kind", [6, 7, 8])
+@pytest.mark.parametrize("offset", [0, 1, 3])
+def test_fp4_device_source_alignments(ody, oracle, kind, offset):
+    """Device sources that start 0, 4 or 12 bytes past a 16-byte boundary
+    (the staged path needs 16-byte alignment; the others take the direct
+    one), float32 and bfloat16, ragged length: both paths bit-exact."""
+    torch = pytest.importorskip("torch")
+    x = _mixed(50001, 9 + offset)
+    base = torch.from_numpy(np.concatenate([np.zeros(offset, np.float32), x])).cuda()
+    got = np.zeros(ody._lib.quant_bytes(kind, x.size), np.uint8)
+    ts = C.c_float(0)
+    ody._lib.check(ody.lib().ody_quantize(kind, base[offset:].data_ptr(), 0, x.size, got.ctypes.data, C.byref(ts)))
+    want, wts = oracle.quantize(kind, x)
+    np.testing.assert_array_equal(got, want)
+    assert np.float32(ts.value) == np.float32(wts)
+    from odyssey_b200.workloads import f32_to_bf16_bits, bf16_bits_to_f32
+    hb = f32_to_bf16_bits(x)
+    bb = torch.from_numpy(np.concatenate([np.zeros(offset, np.uint16), hb]).view(np.int16)).cuda()
+    ody._lib.check(ody.lib().ody_quantize(kind, bb[offset:].data_ptr(), 2, x.size, got.ctypes.data, C.byref(ts)))
+    want, wts = oracle.quantize(kind, bf16_bits_to_f32(hb))
+    np.testing.assert_array_equal(got, want)
+
+
 def test_config2_full_size_mxfp4(ody, oracle):
     """Config 2 at full size (4096^2): bit-exact codes and round trip."""
     from odyssey_b200.workloads import mxfp4_tensor

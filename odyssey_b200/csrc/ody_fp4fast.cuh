@@ -6,14 +6,13 @@
 // (mxfp4.mojo:144-224, nvfp4.mojo:125-205).
 //
 // Two facts make this cheap:
-//  1. The ladder depends only on the top 16 bits of |q|.  Its break points
-//     0.5, 1.25, 1.75, 2.5, 3.5, 5.0 are 0x3F00, 0x3FA0, 0x3FE0, 0x4020,
-//     0x4060, 0x40A0 as bit patterns >> 16 (all multiples of 0x20), so with
-//     h = bits(|q|) >> 16 the magnitude code is 0 for h < 0x3F00 and
-//     ((clamp(h, 0x3F60, 0x40A0) - 0x3EE0) >> 6) otherwise (2..7; code 1 is
-//     never produced).  Checked over every 16-bit h against the ladder.  Two
-//     elements are coded at once in the halves of one 32-bit word with the
-//     16x2 integer min/max instructions.
+//  1. The ladder depends only on the top 11 bits of |q|.  Its break points
+//     0.5, 1.25, 1.75, 2.5, 3.5, 5.0 are the bit patterns 0x3F000000,
+//     0x3FA00000, 0x3FE00000, 0x40200000, 0x40600000, 0x40A00000, all
+//     multiples of 2^21, so the code is a function of bits(|q|) >> 21, which
+//     clamped to [0x1F7, 0x205] takes 15 values: a shift, two integer
+//     clamps and a 16-entry table lookup per element (checked over every
+//     bucket against the ladder).
 //  2. q itself is exact with one multiply (and two FMAs for a scale that is
 //     not a power of two): MXFP4 scales are powers of two, so x * 2^-k is
 //     RN(x / 2^k); for an E4M3 (or per-tensor) scale s with r = RN(1/s),
@@ -94,30 +93,38 @@ __device__ __forceinline__ float div_mk(float x, float s, float r) {
   return __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
 }
 
-// One byte of two codes: element a (quotient qa, value xa) in the high
-// nibble, element b in the low nibble.  neg_t0 = -t0 of the block's scale.
-// Only bits 0..7 of the result are meaningful.
-__device__ __forceinline__ uint32_t fp4_pair_byte(float qa, float qb, float xa, float xb, float neg_t0) {
-  // low half: hi16(|qb|), high half: hi16(|qa|)
-  const uint32_t H = __byte_perm(__float_as_uint(qb), __float_as_uint(qa), 0x7632) & 0x7FFF7FFFu;
-  uint32_t C = u16x2_min(u16x2_max(H, 0x3F603F60u), 0x40A040A0u);
-  C = (C - 0x3EE03EE0u) >> 6;
-  // bit 15 of each half of T: h >= 0x3F00 (|q| >= 0.5); spread to 0xFFFF
-  const uint32_t M = prmt_sign(H + 0x41004100u, 0xBB99u);
-  C &= 0x00070007u & M;
-  C |= set_le(xa, neg_t0) & 0x00080000u;
-  C |= set_le(xb, neg_t0) & 0x00000008u;
-  return C | (C >> 12);
+// Ladder index of a quotient q >= 0 (NaN and +Inf included): the ladder is
+// constant on each bucket bits(q) >> 21 (its break points are the buckets
+// 0x1F8, 0x1FD, 0x1FF, 0x201, 0x203, 0x205), so clamping the bucket to
+// [0x1F7, 0x205] leaves 15 indices and kFp4Ladder maps them to codes.
+__device__ __forceinline__ uint32_t ladder_idx(float q) {
+  const int b = (int)(__float_as_uint(q) >> 21);
+  return (uint32_t)(min(max(b, 0x1F7), 0x205) - 0x1F7);
+}
+// magnitude code per ladder index (code 1 = 0.5 is never produced)
+__device__ __constant__ const uint8_t kFp4Ladder[16] = {0, 2, 2, 2, 2, 2, 3, 3, 4, 4, 5, 5, 6, 6, 7, 7};
+
+// the 16-byte ladder table into shared memory (threads 0..15 of the CTA)
+__device__ __forceinline__ void load_ladder(uint8_t* lut) {
+  if (threadIdx.x < 16) lut[threadIdx.x] = kFp4Ladder[threadIdx.x];
 }
 
-// 8 codes (4 bytes, element 2i in the high nibble of byte i) of quotients q
-// and values x
-__device__ __forceinline__ uint32_t fp4_word(const float* q, const float* x, float neg_t0) {
-  const uint32_t b0 = fp4_pair_byte(q[0], q[1], x[0], x[1], neg_t0);
-  const uint32_t b1 = fp4_pair_byte(q[2], q[3], x[2], x[3], neg_t0);
-  const uint32_t b2 = fp4_pair_byte(q[4], q[5], x[4], x[5], neg_t0);
-  const uint32_t b3 = fp4_pair_byte(q[6], q[7], x[6], x[7], neg_t0);
-  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+// 8 codes (4 bytes, element 2i in the high nibble of byte i) of quotients
+// q = RN(|x| / scale) >= 0 and values x; neg_t0 = -t0 of the block's scale
+// decides the sign bit; lut = the ladder table in shared memory.  The byte
+// and word assembly and the sign insertion are integer multiply-adds, which
+// run beside the integer pipe that the clamps use.
+__device__ __forceinline__ uint32_t fp4_word(const float* q, const float* x, float neg_t0, const uint8_t* lut) {
+  uint32_t w = 0;
+#pragma unroll
+  for (int i = 3; i >= 0; i--) {
+    uint32_t b = (uint32_t)lut[ladder_idx(q[2 * i])] * 16u + lut[ladder_idx(q[2 * i + 1])];
+    // set_le is all ones (-1) for a negative element with a nonzero quotient
+    b = (uint32_t)((int)set_le(x[2 * i], neg_t0) * -128 + (int)b);
+    b = (uint32_t)((int)set_le(x[2 * i + 1], neg_t0) * -8 + (int)b);
+    w = w * 256u + b;
+  }
+  return w;
 }
 
 // 8 codes by the reference's element-wise rule (thresholds of the block's
@@ -175,7 +182,7 @@ struct __align__(8) NvScaleConst {
 template <bool TS>
 __device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, float rst, bool st_fast,
                                                     const float* t0_ts, const NvScaleConst* nvc,
-                                                    const Fp4Thr* thr_nv, uint32_t* w) {
+                                                    const Fp4Thr* thr_nv, const uint8_t* lut, uint32_t* w) {
   float am = 0.0f;
 #pragma unroll
   for (int k = 0; k < 16; k += 2) am = max3_nan(am, fabsf(x[k]), fabsf(x[k + 1]));
@@ -189,9 +196,9 @@ __device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, fl
     const float neg_t0 = -(TS ? t0_ts[e] : c.t0);
     float q[16];
 #pragma unroll
-    for (int k = 0; k < 16; k++) q[k] = div_mk(TS ? div_mk(x[k], st, rst) : x[k], bs, c.rcp);
-    w[0] = fp4_word(q, x, neg_t0);
-    w[1] = fp4_word(q + 8, x + 8, neg_t0);
+    for (int k = 0; k < 16; k++) q[k] = div_mk(TS ? div_mk(fabsf(x[k]), st, rst) : fabsf(x[k]), bs, c.rcp);
+    w[0] = fp4_word(q, x, neg_t0, lut);
+    w[1] = fp4_word(q + 8, x + 8, neg_t0, lut);
     return e;
   }
   // the reference's path: amax ignoring NaN, element-wise IEEE division
@@ -212,7 +219,8 @@ __device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, fl
 
 // ---- one MXFP4 block (32 elements) --------------------------------------
 // Writes the 16 code bytes (w[0..3]) and returns the E8M0 scale byte.
-__device__ __forceinline__ uint32_t mx_encode_block(const float* x, const Fp4Thr* thr_mx, uint32_t* w) {
+__device__ __forceinline__ uint32_t mx_encode_block(const float* x, const Fp4Thr* thr_mx, const uint8_t* lut,
+                                                    uint32_t* w) {
   float am = 0.0f;
 #pragma unroll
   for (int k = 0; k < 32; k += 2) am = max3_nan(am, fabsf(x[k]), fabsf(x[k + 1]));
@@ -223,9 +231,9 @@ __device__ __forceinline__ uint32_t mx_encode_block(const float* x, const Fp4Thr
     const float neg_t0 = -thr_mx[e].t[0];
     float q[32];
 #pragma unroll
-    for (int k = 0; k < 32; k++) q[k] = __fmul_rn(x[k], r);
+    for (int k = 0; k < 32; k++) q[k] = __fmul_rn(fabsf(x[k]), r);
 #pragma unroll
-    for (int i = 0; i < 4; i++) w[i] = fp4_word(q + 8 * i, x + 8 * i, neg_t0);
+    for (int i = 0; i < 4; i++) w[i] = fp4_word(q + 8 * i, x + 8 * i, neg_t0, lut);
     return e;
   }
   float amr = 0.0f;

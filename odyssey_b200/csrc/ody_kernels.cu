@@ -919,7 +919,7 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
 // elements per thread.  The CTA keeps the composite t0 table of the last
 // tensor it re-quantised.
 __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& ch, const Fp4Thr* s_nv,
-                                              float* s_t0, int* s_t0_tensor, uint8_t* stage) {
+                                              float* s_t0, int* s_t0_tensor, const uint8_t* s_lut, uint8_t* stage) {
   const TensorDesc td = a.tensors[ch.tensor];
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
@@ -972,7 +972,7 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
         for (int k = 0; k < 16; k++) v[k] = 0.0f;
       }
       uint32_t cw[2];
-      const uint32_t sb = nv_encode_block<true>(v, s, r, st_fast, s_t0, g_nv_const, s_nv, cw);
+      const uint32_t sb = nv_encode_block<true>(v, s, r, st_fast, s_t0, g_nv_const, s_nv, s_lut, cw);
       uint8_t* d = ws + lane * 9;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
@@ -1024,9 +1024,11 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
   __shared__ float s_t0[128];
   __shared__ int s_t0_tensor;
+  __shared__ uint8_t s_lut[16];
   __shared__ uint32_t s_next;
   // prologue independent of the preceding stats/finalize grid
   load_thr_smem(s_mx, s_nv);
+  load_ladder(s_lut);
   // wait for the preceding grid (a no-op without a programmatic dependency)
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const Decision* dec = a.dec;
@@ -1046,7 +1048,7 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
     const uint32_t job = a.jobs[j];
     const Chunk ch = a.chunks[job & ~kRequantJob];
     if (job & kRequantJob)
-      requant_chunk(a, ch, s_nv, s_t0, &s_t0_tensor, stage);
+      requant_chunk(a, ch, s_nv, s_t0, &s_t0_tensor, s_lut, stage);
     else
       update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, stage);
     __syncthreads();
@@ -1179,25 +1181,54 @@ __device__ __forceinline__ void load_src8(int sdt, const void* x, int64_t n, int
   }
 }
 
-__global__ void amax_kernel(int sdt, const void* x, int64_t n, uint32_t* out) {
+// Per-tensor amax (NaN ignored, as the reference's compare): one resident
+// wave of CTAs, each thread with eight 16-byte loads in flight per round.
+template <int SDT>
+__global__ void __launch_bounds__(kThreads) amax_kernel(const void* x, int64_t n, uint32_t* out) {
+  constexpr int EPV = SDT == DT_F32 ? 4 : 8;  // elements per 16-byte vector
+  constexpr int U = 8;
   float am = 0.0f;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 8;
-  int64_t e0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
-  // four groups of 8 in flight per thread
-  for (; e0 + 3 * stride < n; e0 += 4 * stride) {
-    float v[4][8];
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  const int64_t nv = aligned ? n / EPV : 0;  // whole vectors
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + (U - 1) * stride < nv; i += U * stride) {
+    uint4 r[U];
 #pragma unroll
-    for (int u = 0; u < 4; u++) load_src8(sdt, x, n, e0 + u * stride, v[u]);
+    for (int u = 0; u < U; u++) r[u] = __ldcg(xv + i + u * stride);
 #pragma unroll
-    for (int u = 0; u < 4; u++)
+    for (int u = 0; u < U; u++) {
+      const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
 #pragma unroll
-      for (int k = 0; k < 8; k++) am = amax_acc(am, v[u][k]);
+      for (int k = 0; k < 4; k++) {
+        if (SDT == DT_F32) {
+          am = amax_acc(am, __uint_as_float(w[k]));
+        } else {
+          am = amax_acc(am, __uint_as_float(w[k] << 16));
+          am = amax_acc(am, __uint_as_float(w[k] & 0xFFFF0000u));
+        }
+      }
+    }
   }
-  for (; e0 < n; e0 += stride) {
-    float v[8];
-    load_src8(sdt, x, n, e0, v);
+  for (; i < nv; i += stride) {
+    const uint4 r = __ldcg(xv + i);
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-    for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
+    for (int k = 0; k < 4; k++) {
+      if (SDT == DT_F32) {
+        am = amax_acc(am, __uint_as_float(w[k]));
+      } else {
+        am = amax_acc(am, __uint_as_float(w[k] << 16));
+        am = amax_acc(am, __uint_as_float(w[k] & 0xFFFF0000u));
+      }
+    }
+  }
+  // the ragged tail (or everything, for an unaligned source)
+  for (int64_t e = nv * EPV + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride) {
+    const float v = SDT == DT_F32 ? reinterpret_cast<const float*>(x)[e]
+                                  : bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(x)[e]);
+    am = amax_acc(am, v);
   }
   am = block_amax_reduce(am);
   if (threadIdx.x == 0) atomicMax(out, __float_as_uint(am));
@@ -1211,11 +1242,20 @@ static int sm_count() {
 }
 
 cudaError_t launch_amax(int sdt, const void* x, int64_t n, uint32_t* amax, cudaStream_t st) {
-  int64_t groups = (n + 7) / 8;
-  int64_t want = (groups + kThreads - 1) / kThreads;
-  int grid = (int)(want < (int64_t)sm_count() * 8 ? want : (int64_t)sm_count() * 8);
-  if (grid < 1) grid = 1;
-  amax_kernel<<<grid, kThreads, 0, st>>>(sdt, x, n, amax);
+  static int per_sm[2] = {0, 0};
+  const int t = sdt == DT_F32 ? 0 : 1;
+  if (per_sm[t] == 0) {
+    int k = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, sdt == DT_F32 ? amax_kernel<DT_F32> : amax_kernel<DT_BF16>,
+                                                  kThreads, 0);
+    per_sm[t] = k > 0 ? k : 1;
+  }
+  const int64_t want = (n / 8 + kThreads - 1) / kThreads + 1;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sm_count() * per_sm[t]));
+  if (sdt == DT_F32)
+    amax_kernel<DT_F32><<<grid, kThreads, 0, st>>>(x, n, amax);
+  else
+    amax_kernel<DT_BF16><<<grid, kThreads, 0, st>>>(x, n, amax);
   return cudaGetLastError();
 }
 
@@ -1283,6 +1323,9 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int6
   constexpr int WB = 32 * BB;       // bytes per warp
   __shared__ __align__(16) uint8_t stage[kThreads / 32][WB];
   __shared__ float s_t0[TS ? 128 : 1];
+  __shared__ uint8_t s_lut[16];
+  load_ladder(s_lut);
+  __syncthreads();
   float st = 1.0f, rst = 1.0f;
   bool st_fast = true;
   if (TS) {
@@ -1304,9 +1347,9 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int6
     uint32_t cw[BE / 8];
     uint32_t sb;
     if (MX)
-      sb = mx_encode_block(v, g_thr_mx, cw);
+      sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
     else
-      sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, cw);
+      sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
     uint8_t* d = ws + lane * BB;
 #pragma unroll
     for (int i = 0; i < BE / 8; i++) {
@@ -1348,6 +1391,9 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
   constexpr int NS = kFp4Stages;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ float s_t0[TS ? 128 : 1];
+  __shared__ uint8_t s_lut[16];
+  load_ladder(s_lut);
+  __syncthreads();
   float st = 1.0f, rst = 1.0f;
   bool st_fast = true;
   if (TS) {
@@ -1413,9 +1459,9 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
     uint32_t cw[PP::BE / 8];
     uint32_t sb;
     if (MX)
-      sb = mx_encode_block(v, g_thr_mx, cw);
+      sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
     else
-      sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, cw);
+      sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
     uint8_t* d = ws + lane * PP::BB;
 #pragma unroll
     for (int i = 0; i < PP::BE / 8; i++) {

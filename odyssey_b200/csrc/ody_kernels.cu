@@ -1412,15 +1412,30 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
   const int64_t gstep = (int64_t)gridDim.x * (kThreads / 32);
   const int64_t g0 = (int64_t)blockIdx.x * (kThreads / 32) + w;
   const char* src = reinterpret_cast<const char*>(x);
-  auto issue = [&](int64_t g, int s) {
-    const uint32_t base = smem_u32(ring + s * PP::SEG);
+  constexpr int OP = (32 * PP::BB + 15) / 16;  // 16-byte output pieces per warp
+  const bool out_al = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  // loop-invariant swizzled offsets of this lane's fill and read slots
+  uint32_t fill_at[PP::P], read_at[PP::P];
+  const uint32_t ring_s = smem_u32(ring);
 #pragma unroll
-    for (int k = 0; k < PP::P; k++) {
-      const int p = k * 32 + lane;
-      const int64_t off = g * PP::SEG + (int64_t)p * 16;
-      const int64_t rem = in_bytes - off;
-      const int bytes = rem >= 16 ? 16 : (rem > 0 ? (int)rem : 0);
-      cp_async16(base + swz16(p) * 16, bytes > 0 ? src + off : src, bytes);
+  for (int k = 0; k < PP::P; k++) {
+    fill_at[k] = ring_s + swz16(k * 32 + lane) * 16;
+    read_at[k] = swz16(lane * PP::P + k) * 16;
+  }
+  auto issue = [&](int64_t g, int s) {
+    const int64_t off = g * PP::SEG;
+    if (off + PP::SEG <= in_bytes) {
+      const char* b = src + off + 16 * lane;
+#pragma unroll
+      for (int k = 0; k < PP::P; k++) cp_async16(fill_at[k] + s * PP::SEG, b + 512 * k, 16);
+    } else {
+#pragma unroll
+      for (int k = 0; k < PP::P; k++) {
+        const int64_t o = off + 512 * k + 16 * lane;
+        const int64_t rem = in_bytes - o;
+        const int bytes = rem >= 16 ? 16 : (rem > 0 ? (int)rem : 0);
+        cp_async16(fill_at[k] + s * PP::SEG, bytes > 0 ? src + o : src, bytes);
+      }
     }
   };
 #pragma unroll
@@ -1429,51 +1444,62 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
     if (g < ngroups) issue(g, s);
     cp_async_commit();
   }
-  int cur = 0;
-  for (int64_t g = g0; g < ngroups; g += gstep) {
-    const int64_t gn = g + (NS - 1) * gstep;
-    if (gn < ngroups) issue(gn, cur == 0 ? NS - 1 : cur - 1);
-    cp_async_commit();
-    cp_async_wait<NS - 1>();
-    __syncwarp();
-    float v[PP::BE];
-    const uint8_t* seg = ring + cur * PP::SEG;
+  int64_t g = g0;
+  while (g < ngroups) {
 #pragma unroll
-    for (int j = 0; j < PP::P; j++) {
-      const uint4 r = *reinterpret_cast<const uint4*>(seg + swz16(lane * PP::P + j) * 16);
-      if (SDT == DT_F32) {
-        v[4 * j] = __uint_as_float(r.x);
-        v[4 * j + 1] = __uint_as_float(r.y);
-        v[4 * j + 2] = __uint_as_float(r.z);
-        v[4 * j + 3] = __uint_as_float(r.w);
-      } else {
-        const uint32_t ww[4] = {r.x, r.y, r.z, r.w};
+    for (int s = 0; s < NS; s++) {  // this iteration encodes stage s (compile-time)
+      if (g >= ngroups) break;
+      const int64_t gn = g + (NS - 1) * gstep;
+      if (gn < ngroups) issue(gn, (s + NS - 1) % NS);
+      cp_async_commit();
+      cp_async_wait<NS - 1>();
+      __syncwarp();
+      float v[PP::BE];
+      const uint8_t* seg = ring + s * PP::SEG;
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-          v[8 * j + 2 * k] = __uint_as_float(ww[k] << 16);
-          v[8 * j + 2 * k + 1] = __uint_as_float(ww[k] & 0xFFFF0000u);
+      for (int j = 0; j < PP::P; j++) {
+        const uint4 r = *reinterpret_cast<const uint4*>(seg + read_at[j]);
+        if (SDT == DT_F32) {
+          v[4 * j] = __uint_as_float(r.x);
+          v[4 * j + 1] = __uint_as_float(r.y);
+          v[4 * j + 2] = __uint_as_float(r.z);
+          v[4 * j + 3] = __uint_as_float(r.w);
+        } else {
+          const uint32_t ww[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            v[8 * j + 2 * k] = __uint_as_float(ww[k] << 16);
+            v[8 * j + 2 * k + 1] = __uint_as_float(ww[k] & 0xFFFF0000u);
+          }
         }
       }
-    }
-    __syncwarp();  // every lane has its block: the slot may be refilled
-    uint32_t cw[PP::BE / 8];
-    uint32_t sb;
-    if (MX)
-      sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
-    else
-      sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
-    uint8_t* d = ws + lane * PP::BB;
+      __syncwarp();  // every lane has its block: the slot may be refilled
+      uint32_t cw[PP::BE / 8];
+      uint32_t sb;
+      if (MX)
+        sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
+      else
+        sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
+      uint8_t* d = ws + lane * PP::BB;
 #pragma unroll
-    for (int i = 0; i < PP::BE / 8; i++) {
+      for (int i = 0; i < PP::BE / 8; i++) {
 #pragma unroll
-      for (int k = 0; k < 4; k++) d[4 * i + k] = (uint8_t)(cw[i] >> (8 * k));
+        for (int k = 0; k < 4; k++) d[4 * i + k] = (uint8_t)(cw[i] >> (8 * k));
+      }
+      d[PP::BB - 1] = (uint8_t)sb;
+      __syncwarp();
+      const int64_t ob = g * 32 * PP::BB;
+      if (out_al && ob + 32 * PP::BB <= out_bytes) {
+        uint4* dst = reinterpret_cast<uint4*>(out + ob);
+#pragma unroll
+        for (int i = 0; i < (OP + 31) / 32; i++)
+          if (i * 32 + lane < OP) dst[i * 32 + lane] = reinterpret_cast<const uint4*>(ws)[i * 32 + lane];
+      } else {
+        flush_warp_bytes(ws, out + ob, 32 * PP::BB, out_bytes - ob);
+      }
+      __syncwarp();
+      g += gstep;
     }
-    d[PP::BB - 1] = (uint8_t)sb;
-    __syncwarp();
-    const int64_t ob = g * 32 * PP::BB;
-    flush_warp_bytes(ws, out + ob, 32 * PP::BB, out_bytes - ob);
-    __syncwarp();
-    cur = cur + 1 == NS ? 0 : cur + 1;
   }
   cp_async_wait<0>();
 }

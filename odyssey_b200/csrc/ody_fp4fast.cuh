@@ -127,6 +127,25 @@ __device__ __forceinline__ uint32_t fp4_word(const float* q, const float* x, flo
   return w;
 }
 
+// Signed variant for power-of-two scales: q = RN(x / 2^k) + 0 is computed
+// exactly with its sign (the "+ 0" turns -0 into +0, so a zero quotient,
+// whatever the sign of x, codes 0 as in the reference's `scaled == 0.0`),
+// and the bucket bits(q) >> 21 of the signed value indexes a 2048-entry
+// table whose upper half holds the codes with the sign bit.
+__device__ __forceinline__ void load_ladder_signed(uint8_t* lut) {
+  for (int i = threadIdx.x; i < 2048; i += blockDim.x) {
+    const int b = i & 0x3FF;
+    lut[i] = (uint8_t)(kFp4Ladder[min(max(b, 0x1F7), 0x205) - 0x1F7] | (i >= 0x400 ? 8 : 0));
+  }
+}
+__device__ __forceinline__ uint32_t fp4_word_signed(const float* q, const uint8_t* lut) {
+  uint32_t w = 0;
+#pragma unroll
+  for (int i = 3; i >= 0; i--)
+    w = w * 256u + (uint32_t)lut[__float_as_uint(q[2 * i]) >> 21] * 16u + lut[__float_as_uint(q[2 * i + 1]) >> 21];
+  return w;
+}
+
 // 8 codes by the reference's element-wise rule (thresholds of the block's
 // scale; the special cases of NaN / Inf elements and a zero scale)
 __device__ __forceinline__ uint32_t fp4_word_slow(const float* x, const float* t, bool scale_zero) {
@@ -219,7 +238,8 @@ __device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, fl
 
 // ---- one MXFP4 block (32 elements) --------------------------------------
 // Writes the 16 code bytes (w[0..3]) and returns the E8M0 scale byte.
-__device__ __forceinline__ uint32_t mx_encode_block(const float* x, const Fp4Thr* thr_mx, const uint8_t* lut,
+// lut_s: the signed table of load_ladder_signed
+__device__ __forceinline__ uint32_t mx_encode_block(const float* x, const Fp4Thr* thr_mx, const uint8_t* lut_s,
                                                     uint32_t* w) {
   float am = 0.0f;
 #pragma unroll
@@ -228,12 +248,11 @@ __device__ __forceinline__ uint32_t mx_encode_block(const float* x, const Fp4Thr
   if (am <= 0x1p127f && e >= 1 && e <= 254) {  // finite elements, a finite nonzero scale
     // 1 / 2^(e-127) exactly (2^-127 is subnormal)
     const float r = e <= 253 ? __uint_as_float((254u - e) << 23) : __uint_as_float(0x00400000u);
-    const float neg_t0 = -thr_mx[e].t[0];
     float q[32];
 #pragma unroll
-    for (int k = 0; k < 32; k++) q[k] = __fmul_rn(fabsf(x[k]), r);
+    for (int k = 0; k < 32; k++) q[k] = __fadd_rn(__fmul_rn(x[k], r), 0.0f);
 #pragma unroll
-    for (int i = 0; i < 4; i++) w[i] = fp4_word(q + 8 * i, x + 8 * i, neg_t0, lut);
+    for (int i = 0; i < 4; i++) w[i] = fp4_word_signed(q + 8 * i, lut_s);
     return e;
   }
   float amr = 0.0f;

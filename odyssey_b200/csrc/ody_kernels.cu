@@ -1323,8 +1323,11 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int6
   constexpr int WB = 32 * BB;       // bytes per warp
   __shared__ __align__(16) uint8_t stage[kThreads / 32][WB];
   __shared__ float s_t0[TS ? 128 : 1];
-  __shared__ uint8_t s_lut[16];
-  load_ladder(s_lut);
+  __shared__ uint8_t s_lut[KIND == Q_MXFP4 ? 2048 : 16];
+  if (KIND == Q_MXFP4)
+    load_ladder_signed(s_lut);
+  else
+    load_ladder(s_lut);
   __syncthreads();
   float st = 1.0f, rst = 1.0f;
   bool st_fast = true;
@@ -1391,8 +1394,11 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
   constexpr int NS = kFp4Stages;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ float s_t0[TS ? 128 : 1];
-  __shared__ uint8_t s_lut[16];
-  load_ladder(s_lut);
+  __shared__ uint8_t s_lut[KIND == Q_MXFP4 ? 2048 : 16];
+  if (KIND == Q_MXFP4)
+    load_ladder_signed(s_lut);
+  else
+    load_ladder(s_lut);
   __syncthreads();
   float st = 1.0f, rst = 1.0f;
   bool st_fast = true;

@@ -313,7 +313,7 @@ def run_quant(args):
     qb = L.quant_bytes(kind, n)
     out = torch.empty(qb, dtype=torch.uint8, device="cuda")
     ts = torch.zeros(1, dtype=torch.float32, device="cuda")
-    scratch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(2, dtype=torch.int32, device="cuda")
     # L2 flush by READING 256 MB (a write would leave L2 full of dirty lines
     # whose write-back the next launch would pay for)
     flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")

@@ -357,7 +357,8 @@ int ody_dequantize(int32_t kind, const void* q, int64_t n, float tensor_scale, f
 /* The same two operations stream-ordered on device memory only: no staging,
  * no synchronisation (for quantising inside a CUDA pipeline).  For the
  * per-tensor-scaled kinds, tensor_scale (device float, written) and
- * amax_scratch (device, 4 bytes, reset by the call) are required; else both
+ * amax_scratch (device, 8 bytes: the tensor's amax and smallest nonzero
+ * magnitude, reset by the call) are required; else both
  * may be NULL.  stream NULL is the legacy default stream. */
 int ody_quantize_on_stream(int32_t kind, const void* src, int32_t src_dtype, int64_t n, void* out,
                            float* tensor_scale, uint32_t* amax_scratch, void* stream);

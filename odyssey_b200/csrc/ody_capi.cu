@@ -1795,10 +1795,12 @@ extern "C" int ody_quantize(int32_t kind, const void* src, int32_t sdt, int64_t 
   const int64_t qb = ody_quant_bytes(kind, n);
   ODY_STAGE(S, src, (size_t)n * dtype_size(sdt), true, &dx);
   ODY_STAGE(S, out, (size_t)qb, false, &dout);
-  ODY_CUDA(cudaMallocAsync(&damax, 8, S.st));
+  // [0] amax bits, [1] smallest nonzero magnitude bits, [2] the tensor scale
+  ODY_CUDA(cudaMallocAsync(&damax, 16, S.st));
   S.bufs.push_back({nullptr, damax, 0, true});
-  dts = (uint32_t*)damax + 1;
-  ODY_CUDA(cudaMemsetAsync(damax, 0, 8, S.st));
+  dts = (uint32_t*)damax + 2;
+  ODY_CUDA(cudaMemsetAsync(damax, 0, 16, S.st));
+  ODY_CUDA(cudaMemsetAsync((uint32_t*)damax + 1, 0xFF, 4, S.st));
   if (kind == ODY_Q_NVFP4_TENSOR || kind == ODY_Q_FP8_E4M3_TENSOR)
     ODY_CUDA(launch_amax(sdt, dx, n, (uint32_t*)damax, S.st));
   ODY_CUDA(launch_quantize(kind, sdt, dx, n, (uint8_t*)dout, (const uint32_t*)damax, (float*)dts, S.st));
@@ -1827,6 +1829,7 @@ extern "C" int ody_quantize_on_stream(int32_t kind, const void* src, int32_t sdt
   cudaStream_t st = (cudaStream_t)stream;
   if (scaled) {
     ODY_CUDA(cudaMemsetAsync(amax_scratch, 0, 4, st));
+    ODY_CUDA(cudaMemsetAsync(amax_scratch + 1, 0xFF, 4, st));
     ODY_CUDA(launch_amax(sdt, src, n, amax_scratch, st));
   }
   ODY_CUDA(launch_quantize(kind, sdt, src, n, (uint8_t*)out, scaled ? amax_scratch : nullptr,

@@ -104,21 +104,17 @@ __device__ __forceinline__ uint32_t ladder_idx(float q) {
 // magnitude code per ladder index (code 1 = 0.5 is never produced)
 __device__ __constant__ const uint8_t kFp4Ladder[16] = {0, 2, 2, 2, 2, 2, 3, 3, 4, 4, 5, 5, 6, 6, 7, 7};
 
-// the 16-byte ladder table into shared memory (threads 0..15 of the CTA)
-__device__ __forceinline__ void load_ladder(uint8_t* lut) {
-  if (threadIdx.x < 16) lut[threadIdx.x] = kFp4Ladder[threadIdx.x];
-}
-
 // 8 codes (4 bytes, element 2i in the high nibble of byte i) of quotients
 // q = RN(|x| / scale) >= 0 and values x; neg_t0 = -t0 of the block's scale
-// decides the sign bit; lut = the ladder table in shared memory.  The byte
+// decides the sign bit; lut = the signed table of load_ladder_signed (its
+// entries 0x1F7.. are the ladder codes of the clamped buckets).  The byte
 // and word assembly and the sign insertion are integer multiply-adds, which
 // run beside the integer pipe that the clamps use.
 __device__ __forceinline__ uint32_t fp4_word(const float* q, const float* x, float neg_t0, const uint8_t* lut) {
   uint32_t w = 0;
 #pragma unroll
   for (int i = 3; i >= 0; i--) {
-    uint32_t b = (uint32_t)lut[ladder_idx(q[2 * i])] * 16u + lut[ladder_idx(q[2 * i + 1])];
+    uint32_t b = (uint32_t)lut[0x1F7 + ladder_idx(q[2 * i])] * 16u + lut[0x1F7 + ladder_idx(q[2 * i + 1])];
     // set_le is all ones (-1) for a negative element with a nonzero quotient
     b = (uint32_t)((int)set_le(x[2 * i], neg_t0) * -128 + (int)b);
     b = (uint32_t)((int)set_le(x[2 * i + 1], neg_t0) * -8 + (int)b);
@@ -198,9 +194,13 @@ struct __align__(8) NvScaleConst {
 // RN(1/st)) applied first, as the reference's x / s_t before the block
 // encode; t0_ts[e] is then the composite t0 of E4M3 code e for this st.
 // Writes the 8 code bytes (w[0], w[1]) and returns the scale byte.
+// sign_fast (TS only): no nonzero element of the tensor is small enough for
+// its quotient to come near zero (|x| >= 2^-124 * s_t * 2048, from the
+// tensor's smallest nonzero magnitude), so every nonzero quotient is a
+// normal number, exact, and carries the sign: the signed table codes it.
 template <bool TS>
 __device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, float rst, bool st_fast,
-                                                    const float* t0_ts, const NvScaleConst* nvc,
+                                                    bool sign_fast, const float* t0_ts, const NvScaleConst* nvc,
                                                     const Fp4Thr* thr_nv, const uint8_t* lut, uint32_t* w) {
   float am = 0.0f;
 #pragma unroll
@@ -212,6 +212,14 @@ __device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, fl
   if (fast) {
     const float bs = e4m3_to_f32((uint8_t)e);
     const NvScaleConst c = nvc[e];
+    if (TS && sign_fast) {
+      float q[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) q[k] = div_mk(div_mk(x[k], st, rst), bs, c.rcp);  // +-0 give +0
+      w[0] = fp4_word_signed(q, lut);
+      w[1] = fp4_word_signed(q + 8, lut);
+      return e;
+    }
     const float neg_t0 = -(TS ? t0_ts[e] : c.t0);
     float q[16];
 #pragma unroll

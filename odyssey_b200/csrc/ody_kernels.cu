@@ -972,7 +972,7 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
         for (int k = 0; k < 16; k++) v[k] = 0.0f;
       }
       uint32_t cw[2];
-      const uint32_t sb = nv_encode_block<true>(v, s, r, st_fast, s_t0, g_nv_const, s_nv, s_lut, cw);
+      const uint32_t sb = nv_encode_block<true>(v, s, r, st_fast, false, s_t0, g_nv_const, s_nv, s_lut, cw);
       uint8_t* d = ws + lane * 9;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
@@ -1024,11 +1024,11 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
   __shared__ __align__(16) uint8_t stage[(kThreads / 32) * kWarpStage];
   __shared__ float s_t0[128];
   __shared__ int s_t0_tensor;
-  __shared__ uint8_t s_lut[16];
+  __shared__ uint8_t s_lut[2048];
   __shared__ uint32_t s_next;
   // prologue independent of the preceding stats/finalize grid
   load_thr_smem(s_mx, s_nv);
-  load_ladder(s_lut);
+  load_ladder_signed(s_lut);
   // wait for the preceding grid (a no-op without a programmatic dependency)
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const Decision* dec = a.dec;
@@ -1181,13 +1181,20 @@ __device__ __forceinline__ void load_src8(int sdt, const void* x, int64_t n, int
   }
 }
 
-// Per-tensor amax (NaN ignored, as the reference's compare): one resident
-// wave of CTAs, each thread with eight 16-byte loads in flight per round.
+// Per-tensor amax (NaN ignored, as the reference's compare) into out[0] and
+// the smallest nonzero magnitude into out[1] (float bits; out[1] starts at
+// 0xFFFFFFFF): one resident wave of CTAs, each thread with eight 16-byte
+// loads in flight per round.
 template <int SDT>
 __global__ void __launch_bounds__(kThreads) amax_kernel(const void* x, int64_t n, uint32_t* out) {
   constexpr int EPV = SDT == DT_F32 ? 4 : 8;  // elements per 16-byte vector
   constexpr int U = 8;
-  float am = 0.0f;
+  float am = 0.0f, mn = __uint_as_float(0x7f800000u);
+  auto acc = [&](float v) {
+    const float a = fabsf(v);
+    am = fmaxf(am, a);
+    mn = fminf(mn, a > 0.0f ? a : __uint_as_float(0x7f800000u));
+  };
   const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
   const int64_t nv = aligned ? n / EPV : 0;  // whole vectors
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -1203,10 +1210,10 @@ __global__ void __launch_bounds__(kThreads) amax_kernel(const void* x, int64_t n
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         if (SDT == DT_F32) {
-          am = amax_acc(am, __uint_as_float(w[k]));
+          acc(__uint_as_float(w[k]));
         } else {
-          am = amax_acc(am, __uint_as_float(w[k] << 16));
-          am = amax_acc(am, __uint_as_float(w[k] & 0xFFFF0000u));
+          acc(__uint_as_float(w[k] << 16));
+          acc(__uint_as_float(w[k] & 0xFFFF0000u));
         }
       }
     }
@@ -1217,10 +1224,10 @@ __global__ void __launch_bounds__(kThreads) amax_kernel(const void* x, int64_t n
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       if (SDT == DT_F32) {
-        am = amax_acc(am, __uint_as_float(w[k]));
+        acc(__uint_as_float(w[k]));
       } else {
-        am = amax_acc(am, __uint_as_float(w[k] << 16));
-        am = amax_acc(am, __uint_as_float(w[k] & 0xFFFF0000u));
+        acc(__uint_as_float(w[k] << 16));
+        acc(__uint_as_float(w[k] & 0xFFFF0000u));
       }
     }
   }
@@ -1228,10 +1235,15 @@ __global__ void __launch_bounds__(kThreads) amax_kernel(const void* x, int64_t n
   for (int64_t e = nv * EPV + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride) {
     const float v = SDT == DT_F32 ? reinterpret_cast<const float*>(x)[e]
                                   : bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(x)[e]);
-    am = amax_acc(am, v);
+    acc(v);
   }
   am = block_amax_reduce(am);
-  if (threadIdx.x == 0) atomicMax(out, __float_as_uint(am));
+  // the smallest nonzero magnitude: a max-reduce of the negated bits order
+  const float mnr = block_amax_reduce(__uint_as_float(0x7f800000u - __float_as_uint(mn)));
+  if (threadIdx.x == 0) {
+    atomicMax(out, __float_as_uint(am));
+    atomicMin(out + 1, 0x7f800000u - __float_as_uint(mnr));
+  }
 }
 
 static int sm_count() {
@@ -1323,18 +1335,18 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int6
   constexpr int WB = 32 * BB;       // bytes per warp
   __shared__ __align__(16) uint8_t stage[kThreads / 32][WB];
   __shared__ float s_t0[TS ? 128 : 1];
-  __shared__ uint8_t s_lut[KIND == Q_MXFP4 ? 2048 : 16];
-  if (KIND == Q_MXFP4)
-    load_ladder_signed(s_lut);
-  else
-    load_ladder(s_lut);
+  __shared__ uint8_t s_lut[2048];
+  load_ladder_signed(s_lut);
   __syncthreads();
   float st = 1.0f, rst = 1.0f;
-  bool st_fast = true;
+  bool st_fast = true, sign_fast = false;
   if (TS) {
     st = tensor_scale_from_amax(KIND, *amax);
     rst = __frcp_rn(st);
     st_fast = st >= 0x1p-60f && st <= 0x1p60f;
+    // amax[1]: the smallest nonzero magnitude (all ones: none)
+    const float mnz = __uint_as_float(amax[1]);
+    sign_fast = st_fast && !(mnz < __fmul_rn(st, 0x1p-113f));
     for (int i = threadIdx.x; i < 128; i += blockDim.x) s_t0[i] = composite_threshold(g_thr_nv[i].t[0], st);
     __syncthreads();
   }
@@ -1352,7 +1364,7 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int6
     if (MX)
       sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
     else
-      sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
+      sb = nv_encode_block<TS>(v, st, rst, st_fast, sign_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
     uint8_t* d = ws + lane * BB;
 #pragma unroll
     for (int i = 0; i < BE / 8; i++) {
@@ -1394,18 +1406,18 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
   constexpr int NS = kFp4Stages;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ float s_t0[TS ? 128 : 1];
-  __shared__ uint8_t s_lut[KIND == Q_MXFP4 ? 2048 : 16];
-  if (KIND == Q_MXFP4)
-    load_ladder_signed(s_lut);
-  else
-    load_ladder(s_lut);
+  __shared__ uint8_t s_lut[2048];
+  load_ladder_signed(s_lut);
   __syncthreads();
   float st = 1.0f, rst = 1.0f;
-  bool st_fast = true;
+  bool st_fast = true, sign_fast = false;
   if (TS) {
     st = tensor_scale_from_amax(KIND, *amax);
     rst = __frcp_rn(st);
     st_fast = st >= 0x1p-60f && st <= 0x1p60f;
+    // amax[1]: the smallest nonzero magnitude (all ones: none)
+    const float mnz = __uint_as_float(amax[1]);
+    sign_fast = st_fast && !(mnz < __fmul_rn(st, 0x1p-113f));
     for (int i = threadIdx.x; i < 128; i += blockDim.x) s_t0[i] = composite_threshold(g_thr_nv[i].t[0], st);
     __syncthreads();
   }
@@ -1485,7 +1497,7 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
       if (MX)
         sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
       else
-        sb = nv_encode_block<TS>(v, st, rst, st_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
+        sb = nv_encode_block<TS>(v, st, rst, st_fast, sign_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
       uint8_t* d = ws + lane * PP::BB;
 #pragma unroll
       for (int i = 0; i < PP::BE / 8; i++) {

@@ -115,7 +115,7 @@ def _ulp_sweep(c, k):
     return out.astype(np.int32).view(np.float32)
 
 
-def _boundary_blocks(B, scales, mult, rng):
+def _boundary_blocks(B, scales, mult, rng, tiny=True):
     """Blocks of B elements: element 0 = 6 * scale * mult (selects the block
     scale), the rest sweep the ladder break points T * scale * mult and the
     smallest quotients, +-8 ulps, both signs."""
@@ -123,8 +123,10 @@ def _boundary_blocks(B, scales, mult, rng):
     blocks = []
     for sc in scales:
         sc = np.float32(sc)
-        pts = np.concatenate([_ulp_sweep(T * sc * np.float32(mult), 8),
-                              _ulp_sweep(np.float32([2.0 ** -149, 2.0 ** -148, 1e-40]) * sc, 3)])
+        parts = [_ulp_sweep(T * sc * np.float32(mult), 8)]
+        if tiny:
+            parts.append(_ulp_sweep(np.float32([2.0 ** -149, 2.0 ** -148, 1e-40]) * sc, 3))
+        pts = np.concatenate(parts)
         pts = pts * np.where(rng.random(pts.size) < 0.5, np.float32(-1), np.float32(1))
         head = np.float32(6.0) * sc * np.float32(mult)
         for i in range(0, pts.size, B - 1):
@@ -153,8 +155,11 @@ def test_fp4_encode_break_points_every_scale(ody, oracle, kind):
         return
     e4m3 = oracle.e4m3_to_f32(np.arange(1, 127, dtype=np.uint8))
     mults = [1.0] if kind == 7 else [1.0, 3.7e-5, 1e-3, 2.5e7]
-    for mult in mults:
-        x = _boundary_blocks(16, e4m3, mult, rng)
+    # per-tensor: with subnormal-range elements (the sign decided by the
+    # threshold t0) and without (every nonzero quotient normal: the sign
+    # comes with the quotient)
+    for mult, tiny in [(m, t) for m in mults for t in ((True,) if kind == 7 else (True, False))]:
+        x = _boundary_blocks(16, e4m3, mult, rng, tiny)
         if kind == 8:
             # the tensor's amax (one more block) sets s_t = amax / 2688, so
             # that q = x / s_t puts block scales on every E4M3 code
@@ -163,7 +168,7 @@ def test_fp4_encode_break_points_every_scale(ody, oracle, kind):
             x = np.concatenate([x, tail])
         got, ts = _gpu_quant(ody, kind, x)
         want, wts = oracle.quantize(kind, x)
-        np.testing.assert_array_equal(got, want, err_msg=f"mult {mult}")
+        np.testing.assert_array_equal(got, want, err_msg=f"mult {mult} tiny {tiny}")
         assert np.float32(ts) == np.float32(wts)
 
 
@@ -363,7 +368,7 @@ def test_quantize_on_stream_matches(ody, kind):
     dx = torch.from_numpy(x).cuda()
     out = torch.zeros(ref.size, dtype=torch.uint8, device="cuda")
     ts = torch.zeros(1, dtype=torch.float32, device="cuda")
-    scratch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scratch = torch.zeros(2, dtype=torch.int32, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
     ody._lib.check(ody.lib().ody_quantize_on_stream(kind, dx.data_ptr(), 0, x.size, out.data_ptr(), ts.data_ptr(),
                                                      scratch.data_ptr(), st))

@@ -167,6 +167,7 @@ struct ody_ctx {
   cudaStream_t copy_stream = nullptr;  // non-blocking
   cudaEvent_t slot_read[2] = {nullptr, nullptr};  // last step reading the slot is done with it
   cudaEvent_t slot_filled[2] = {nullptr, nullptr};  // uploads into the slot are done
+  bool slot_ordered = false;  // the copy stream already waits for the upload slot's last reader
 };
 
 // the gradient arena the next step reads
@@ -750,12 +751,14 @@ static int copy_tensor(ody_ctx* c, int32_t which, int32_t i, void* dst_or_src, s
     // the copy stream: after the step that last read this arena, and ahead
     // of the step that reads it next (which waits on slot_filled)
     const int s = c->upload_slot;
-    ODY_CUDA(cudaStreamWaitEvent(c->copy_stream, c->slot_read[s], 0));
+    if (!c->slot_ordered) {  // once per step, not once per tensor
+      ODY_CUDA(cudaStreamWaitEvent(c->copy_stream, c->slot_read[s], 0));
+      c->slot_ordered = true;
+    }
     if (up)
       ODY_CUDA(cudaMemcpyAsync(base, dst_or_src, bytes, cudaMemcpyDefault, c->copy_stream));
     else
       ODY_CUDA(cudaMemcpyAsync(dst_or_src, base, bytes, cudaMemcpyDefault, c->copy_stream));
-    ODY_CUDA(cudaEventRecord(c->slot_filled[s], c->copy_stream));
     if (sync) ODY_CUDA(cudaStreamSynchronize(c->copy_stream));
     return ODY_OK;
   }
@@ -1015,6 +1018,7 @@ extern "C" int ody_ctx_set_grad_double_buffer(ody_ctx* c, int32_t enable) {
     ODY_CUDA(cudaFree(c->grad_slot[1]));
     c->grad_slot[1] = nullptr;
     c->upload_slot = 0;
+    c->slot_ordered = false;
     c->dbuf = false;
     return ODY_OK;
   }
@@ -1037,6 +1041,7 @@ extern "C" int ody_ctx_set_grad_double_buffer(ody_ctx* c, int32_t enable) {
   c->grad_slot[0] = c->grad;
   c->grad_slot[1] = alt;
   c->upload_slot = 0;
+  c->slot_ordered = false;
   c->dbuf = true;
   return ODY_OK;
 }
@@ -1064,7 +1069,11 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
   const DecideParams dp = make_decide(c->cfg);
   const int nl = (int)c->tdesc.size();
   if (c->graph_mode && c->world == 1 && !c->timing && !c->dbuf && !c->jobs.empty()) return step_graph(c, oc, dp);
-  if (c->dbuf) ODY_CUDA(cudaStreamWaitEvent(c->stream, c->slot_filled[c->upload_slot], 0));
+  if (c->dbuf) {
+    // the step reads the slot after every upload queued into it so far
+    ODY_CUDA(cudaEventRecord(c->slot_filled[c->upload_slot], c->copy_stream));
+    ODY_CUDA(cudaStreamWaitEvent(c->stream, c->slot_filled[c->upload_slot], 0));
+  }
   cudaEvent_t* tev = nullptr;
   if (c->timing) {
     const int64_t slot = c->tnext++;
@@ -1119,6 +1128,7 @@ extern "C" int ody_step_async(ody_ctx* c, int64_t t) {
     // the next step reads the other one
     ODY_CUDA(cudaEventRecord(c->slot_read[c->upload_slot], c->stream));
     c->upload_slot ^= 1;
+    c->slot_ordered = false;
   }
   ODY_CUDA(cudaMemcpyAsync(c->h_dec, c->dec, sizeof(Decision), cudaMemcpyDeviceToHost, c->stream));
   ODY_CUDA(cudaEventRecord(c->done, c->stream));

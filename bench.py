@@ -102,22 +102,34 @@ class Clocks:
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        import tempfile
+        self.f = tempfile.TemporaryFile(mode="w+")
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
                                        "--format=csv,noheader,nounits", "-lms", "200"],
-                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                                      stdout=self.f, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.p = None
+        # the sampler needs a moment to start: wait (at most 5 s) for its
+        # first line, so that short timed regions are sampled too
+        t0 = time.time()
+        while self.p and self.p.poll() is None and time.time() - t0 < 5.0:
+            if os.fstat(self.f.fileno()).st_size > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *a):
         if self.p:
+            time.sleep(0.25)  # one more sample interval after the timed region
             self.p.terminate()
             try:
-                self.out, _ = self.p.communicate(timeout=5)
+                self.p.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.p.kill()
-                self.out = ""
+        self.f.seek(0)
+        self.out = self.f.read()
+        self.f.close()
 
     def summary(self):
         if not self.out:

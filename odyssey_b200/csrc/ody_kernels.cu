@@ -1189,11 +1189,11 @@ template <int SDT>
 __global__ void __launch_bounds__(kThreads) amax_kernel(const void* x, int64_t n, uint32_t* out) {
   constexpr int EPV = SDT == DT_F32 ? 4 : 8;  // elements per 16-byte vector
   constexpr int U = 8;
-  float am = 0.0f, mn = __uint_as_float(0x7f800000u);
+  float am = 0.0f;
+  uint32_t mn1 = 0xFFFFFFFFu;  // smallest (|v| bits - 1): zero wraps to the top, NaN sorts above +Inf
   auto acc = [&](float v) {
-    const float a = fabsf(v);
-    am = fmaxf(am, a);
-    mn = fminf(mn, a > 0.0f ? a : __uint_as_float(0x7f800000u));
+    am = fmaxf(am, fabsf(v));
+    mn1 = min(mn1, (__float_as_uint(v) & 0x7FFFFFFFu) - 1u);
   };
   const bool aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
   const int64_t nv = aligned ? n / EPV : 0;  // whole vectors
@@ -1238,11 +1238,12 @@ __global__ void __launch_bounds__(kThreads) amax_kernel(const void* x, int64_t n
     acc(v);
   }
   am = block_amax_reduce(am);
-  // the smallest nonzero magnitude: a max-reduce of the negated bits order
-  const float mnr = block_amax_reduce(__uint_as_float(0x7f800000u - __float_as_uint(mn)));
+  // the smallest nonzero magnitude (bits; anything from +Inf up means none)
+  uint32_t mn = mn1 >= 0x7F800000u ? 0x7F800000u : mn1 + 1u;
+  mn = 0x7F800000u - __float_as_uint(block_amax_reduce(__uint_as_float(0x7F800000u - mn)));
   if (threadIdx.x == 0) {
     atomicMax(out, __float_as_uint(am));
-    atomicMin(out + 1, 0x7f800000u - __float_as_uint(mnr));
+    atomicMin(out + 1, mn);
   }
 }
 
@@ -1379,11 +1380,16 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int6
 }
 
 // The same with the input staged through shared memory: each warp fills a
-// ring of kFp4Stages segments (32 blocks each) with coalesced 16-byte
+// ring of two or three segments (32 blocks each) with coalesced 16-byte
 // cp.async copies, several segments ahead of the one it encodes, so that the
 // loads of a thread are neither strided nor waited for one block at a time.
 // Needs a 16-byte-aligned source.
-constexpr int kFp4Stages = 3;
+// stages per warp ring: three, or two where a segment is 4 KB (MXFP4 from
+// float32), which keeps three CTAs per SM
+template <int SEGB>
+struct Fp4Stages {
+  static constexpr int N = SEGB >= 4096 ? 2 : 3;
+};
 
 template <int KIND, int SDT>
 struct Fp4Pipe {
@@ -1393,7 +1399,8 @@ struct Fp4Pipe {
   static constexpr int P = BE * ESZ / 16;  // 16-byte slots per block
   static constexpr int SEG = 32 * P * 16;  // input bytes per warp segment
   static constexpr int WB = (32 * BB + 15) / 16 * 16;
-  static constexpr int SMEM = (kThreads / 32) * (kFp4Stages * SEG + WB);
+  static constexpr int NS = Fp4Stages<SEG>::N;
+  static constexpr int SMEM = (kThreads / 32) * (NS * SEG + WB);
 };
 
 template <int KIND, int SDT>
@@ -1403,7 +1410,7 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
   using PP = Fp4Pipe<KIND, SDT>;
   constexpr bool MX = KIND == Q_MXFP4;
   constexpr bool TS = KIND == Q_NVFP4_TENSOR;
-  constexpr int NS = kFp4Stages;
+  constexpr int NS = PP::NS;
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ float s_t0[TS ? 128 : 1];
   __shared__ uint8_t s_lut[2048];

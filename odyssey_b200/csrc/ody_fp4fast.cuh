@@ -184,9 +184,11 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 __device__ __forceinline__ int swz16(int p) { return (p & ~7) | ((p ^ (p >> 3)) & 7); }
 
 // Per-code constants of the NVFP4 E4M3 block scales: RN(1/scale) and t0.
-struct __align__(8) NvScaleConst {
+struct __align__(16) NvScaleConst {
   float rcp;
   float t0;
+  float scale;  // the E4M3 value itself
+  float pad;
 };
 
 // ---- one NVFP4 block (16 elements) -------------------------------------
@@ -206,12 +208,17 @@ __device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, fl
 #pragma unroll
   for (int k = 0; k < 16; k += 2) am = max3_nan(am, fabsf(x[k]), fabsf(x[k + 1]));
   // am: NaN when an element is NaN, +Inf when one is infinite
-  const float amq = TS ? div_by(am, st, rst) : am;
-  const uint32_t e = e4m3_scale_from_f32(block_scale_value_fast(amq));
+  // Markstein without range guards: a tiny amax (below 2^-100) gives a
+  // quotient far below the 1e-10 fallback threshold either way, and a NaN
+  // or overflowing one fails the fast test below
+  const float amq = TS ? div_mk(am, st, rst) : am;
+  float bsv = div_mk(amq, 6.0f, 0x1.555556p-3f);  // RN(1/6)
+  if (bsv < 1e-10f) bsv = 1.0f;
+  const uint32_t e = e4m3_scale_from_f32(bsv);
   const bool fast = st_fast && amq <= 0x1p120f && e != 0;  // false for NaN / Inf
   if (fast) {
-    const float bs = e4m3_to_f32((uint8_t)e);
     const NvScaleConst c = nvc[e];
+    const float bs = c.scale;
     if (TS && sign_fast) {
       float q[16];
 #pragma unroll

@@ -89,6 +89,8 @@ void upload_fp4_tables(int device) {
       volatile float s = b == 127 ? 0.0f : host_e4m3_to_f32(b);
       h_nv_const[b].rcp = 1.0f / s;  // IEEE division on the host: RN(1/s)
       h_nv_const[b].t0 = h_thr_nv[b].t[0];
+      h_nv_const[b].scale = s;
+      h_nv_const[b].pad = 0.0f;
     }
     h_thr_ready = true;
   }

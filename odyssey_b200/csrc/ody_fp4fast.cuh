@@ -152,6 +152,27 @@ __device__ __forceinline__ uint32_t fp4_word_slow(const float* x, const float* t
   return w;
 }
 
+// A warp's 32 blocks into its shared staging area in the output byte layout,
+// with aligned 32-bit stores: each lane holds its block's NW code words and
+// scale byte; four lanes fill 4 * BB bytes = BB whole words, lane r of a
+// quad owning the words that start inside its bytes (its last word takes
+// up to three bytes of the next lane, fetched with one shuffle).
+template <int NW>
+__device__ __forceinline__ void stage_blocks(uint8_t* ws, const uint32_t* cw, uint32_t sb) {
+  constexpr int BB = 4 * NW + 1;
+  const int lane = threadIdx.x & 31, r = lane & 3;
+  const uint32_t nxt = __shfl_down_sync(0xffffffffu, cw[0], 1);
+  uint32_t W[NW + 1];
+#pragma unroll
+  for (int k = 0; k < NW; k++) W[k] = cw[k];
+  W[NW] = (sb & 0xFFu) | (nxt << 8);
+  const int o0 = (4 - r) & 3;  // first owned byte offset inside the block
+  uint32_t* dw = reinterpret_cast<uint32_t*>(ws) + BB * (lane >> 2) + ((BB * r + o0) >> 2);
+#pragma unroll
+  for (int k = 0; k < NW; k++) dw[k] = __funnelshift_r(W[k], W[k + 1], 8 * o0);
+  if (r == 0) dw[NW] = W[NW];
+}
+
 // a warp's staged bytes out: 16-byte stores when the whole slice may be
 // written and the destination is aligned, else bytes up to limit
 __device__ __forceinline__ void flush_warp_bytes(const uint8_t* ws, uint8_t* dst, int nbytes, int64_t limit) {

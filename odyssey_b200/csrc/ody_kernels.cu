@@ -975,13 +975,7 @@ __device__ __forceinline__ void requant_chunk(const ApplyArgs& a, const Chunk& c
       }
       uint32_t cw[2];
       const uint32_t sb = nv_encode_block<true>(v, s, r, st_fast, false, s_t0, g_nv_const, s_nv, s_lut, cw);
-      uint8_t* d = ws + lane * 9;
-#pragma unroll
-      for (int k = 0; k < 4; k++) {
-        d[k] = (uint8_t)(cw[0] >> (8 * k));
-        d[4 + k] = (uint8_t)(cw[1] >> (8 * k));
-      }
-      d[8] = (uint8_t)sb;
+      stage_blocks<2>(ws, cw, sb);
       __syncwarp();
       flush_warp_bytes(ws, a.qout + td.qoff + (blk0 + b0) * 9, 32 * 9, (nb - b0) * 9);
       __syncwarp();
@@ -1368,13 +1362,7 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int6
       sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
     else
       sb = nv_encode_block<TS>(v, st, rst, st_fast, sign_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
-    uint8_t* d = ws + lane * BB;
-#pragma unroll
-    for (int i = 0; i < BE / 8; i++) {
-#pragma unroll
-      for (int k = 0; k < 4; k++) d[4 * i + k] = (uint8_t)(cw[i] >> (8 * k));
-    }
-    d[BB - 1] = (uint8_t)sb;
+    stage_blocks<BE / 8>(ws, cw, sb);
     __syncwarp();
     flush_warp_bytes(ws, out + b0 * BB, WB, out_bytes - b0 * BB);
     __syncwarp();
@@ -1507,13 +1495,7 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
         sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
       else
         sb = nv_encode_block<TS>(v, st, rst, st_fast, sign_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
-      uint8_t* d = ws + lane * PP::BB;
-#pragma unroll
-      for (int i = 0; i < PP::BE / 8; i++) {
-#pragma unroll
-        for (int k = 0; k < 4; k++) d[4 * i + k] = (uint8_t)(cw[i] >> (8 * k));
-      }
-      d[PP::BB - 1] = (uint8_t)sb;
+      stage_blocks<PP::BE / 8>(ws, cw, sb);
       __syncwarp();
       const int64_t ob = g * 32 * PP::BB;
       if (out_al && ob + 32 * PP::BB <= out_bytes) {

@@ -239,6 +239,9 @@ QUANT_WORKLOADS = {
                   name="mxfp4_4096x4096_f32_outliers (configs[1])"),
     "nvfp4": dict(kind=8, side=8192, sdt="bfloat16", bytes_per_elem=2 + 2 + 9 / 16,
                   name="nvfp4_tensor_scaled_8192x8192_bf16_outliers (configs[2])"),
+    # configs[1] with its scale rule as BASELINE states it (OCP MX v1.0)
+    "mxfp4_ocp": dict(kind=9, side=4096, sdt="float32", bytes_per_elem=4 + 17 / 32,
+                      name="mxfp4_ocp_4096x4096_f32_outliers (configs[1], OCP MX rule)"),
 }
 QUANT_METRIC = "standalone quantiser: elements/s & HBM GB/s (% of peak)"
 
@@ -250,7 +253,7 @@ def _quant_input(spec, seed, device):
     n = spec["side"] ** 2
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    if spec["kind"] == 6:
+    if spec["kind"] in (6, 9):
         x = torch.randn(n, device=device, generator=g)
         idx = torch.randperm(n, device=device, generator=g)[: n // 1000]
         x[idx] *= 100.0
@@ -453,7 +456,7 @@ def main():
                     help="data-parallel gradients: every rank holds full-model gradients and each step first "
                          "reduce-scatters them, fused with pass 1 (fused) or by ncclReduceScatter (nccl, "
                          "for comparison); none = gradients already reduced (the headline)")
-    ap.add_argument("--workload", default="flat1b", choices=["flat1b", "resnet18", "lenet", "mxfp4", "nvfp4"],
+    ap.add_argument("--workload", default="flat1b", choices=["flat1b", "resnet18", "lenet", "mxfp4", "nvfp4", "mxfp4_ocp"],
                     help="flat1b = the headline 1B model; resnet18 / lenet = secondary step lines; mxfp4 / "
                          "nvfp4 = the standalone quantiser on configs[1] / configs[2]")
     ap.add_argument("--placement", default="auto", choices=["auto", "interleaved", "at_end"],

@@ -60,6 +60,14 @@ extern "C" {
 #define ODY_Q_MXFP4 6          /* AnyTensor.to_mxfp4() (any_tensor.mojo:2237-2302), 17-byte blocks */
 #define ODY_Q_NVFP4 7          /* AnyTensor.to_nvfp4() (any_tensor.mojo:2329-2401), 9-byte blocks */
 #define ODY_Q_NVFP4_TENSOR 8   /* to_nvfp4(w / s_t), s_t = amax/(448*6) (per-tensor scale; extension) */
+/* MXFP4 by the OCP Microscaling Formats v1.0 rule (no reference counterpart;
+ * the rule BASELINE's MXFP4 configuration states): per 32-element block the
+ * E8M0 byte X + 127 with X = floor(log2(max|x|)) - 2 clamped to [-127, 127],
+ * elements x / 2^X rounded to nearest even on the E2M1 grid (0.5 included)
+ * and saturated at 6, sign kept; a NaN or Inf element gives the NaN scale
+ * byte 0xFF.  Same 17-byte block layout as ODY_Q_MXFP4.  Stateless
+ * quantise / dequantise only (not a step context requant kind). */
+#define ODY_Q_MXFP4_OCP 9
 
 /* ---- requant job placement (ody_config.requant_placement) ---------------
  * INTERLEAVED: a tensor's requant jobs follow its last update job by two

@@ -20,5 +20,5 @@ from .optimizers import (adagrad_step, adagrad_step_simple, adam_step, adamw_ste
                          rmsprop_step, rmsprop_step_simple, sgd_step)
 from .precision_config import PrecisionConfig, PrecisionMode  # noqa: F401
 from .quant import (MXFP4, NVFP4, QuantizedTensor, dequantize, from_bf8, from_fp8, from_mxfp4, from_nvfp4,  # noqa: F401
-                    quantize, to_bf8, to_fp8, to_fp8_tensor_scaled, to_mxfp4, to_nvfp4,
+                    quantize, to_bf8, to_fp8, to_fp8_tensor_scaled, to_mxfp4, to_mxfp4_ocp, to_nvfp4,
                     to_nvfp4_tensor_scaled)

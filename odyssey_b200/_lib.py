@@ -16,13 +16,13 @@ ERR_ARG, ERR_SHAPE, ERR_DTYPE, ERR_CUDA, ERR_NCCL, ERR_COMM_TIMEOUT, ERR_DEVICE_
 F32, F16, BF16 = 0, 1, 2
 SGD, ADAM, ADAMW, LION, RMSPROP, ADAGRAD = 0, 1, 2, 3, 4, 5
 (Q_NONE, Q_FP16, Q_BF16, Q_FP8_E4M3, Q_FP8_E5M2, Q_FP8_E4M3_TENSOR, Q_MXFP4, Q_NVFP4,
- Q_NVFP4_TENSOR) = range(9)
+ Q_NVFP4_TENSOR, Q_MXFP4_OCP) = range(10)
 BUF_MASTER, BUF_STATE1, BUF_STATE2, BUF_GRAD, BUF_DP_GRAD = range(5)
 
 QUANT_NAMES = {
     "none": Q_NONE, "fp16": Q_FP16, "bf16": Q_BF16, "fp8": Q_FP8_E4M3, "fp8_e4m3": Q_FP8_E4M3,
     "bf8": Q_FP8_E5M2, "fp8_e5m2": Q_FP8_E5M2, "fp8_tensor": Q_FP8_E4M3_TENSOR, "mxfp4": Q_MXFP4,
-    "nvfp4": Q_NVFP4, "nvfp4_tensor": Q_NVFP4_TENSOR,
+    "nvfp4": Q_NVFP4, "nvfp4_tensor": Q_NVFP4_TENSOR, "mxfp4_ocp": Q_MXFP4_OCP,
 }
 
 

@@ -246,6 +246,7 @@ extern "C" int64_t ody_quant_bytes(int32_t kind, int64_t n) {
     case ODY_Q_FP8_E4M3_TENSOR:
       return n;
     case ODY_Q_MXFP4:
+    case ODY_Q_MXFP4_OCP:
       return ((n + 31) / 32) * 17;
     case ODY_Q_NVFP4:
     case ODY_Q_NVFP4_TENSOR:
@@ -1794,7 +1795,7 @@ extern "C" int ody_adagrad_step(const float* p, const float* g, const float* acc
 }
 
 extern "C" int ody_quantize(int32_t kind, const void* src, int32_t sdt, int64_t n, void* out, float* ts) {
-  if (kind <= ODY_Q_NONE || kind > ODY_Q_NVFP4_TENSOR)
+  if (kind <= ODY_Q_NONE || kind > ODY_Q_MXFP4_OCP)
     return fail(ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(kind));
   if (sdt != DT_F32 && sdt != DT_BF16) return fail(ODY_ERR_DTYPE, "quantize source must be float32 or bfloat16");
   if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot quantize an empty tensor");
@@ -1824,7 +1825,7 @@ extern "C" int ody_quantize(int32_t kind, const void* src, int32_t sdt, int64_t 
 
 extern "C" int ody_quantize_on_stream(int32_t kind, const void* src, int32_t sdt, int64_t n, void* out,
                                       float* tensor_scale, uint32_t* amax_scratch, void* stream) {
-  if (kind <= ODY_Q_NONE || kind > ODY_Q_NVFP4_TENSOR)
+  if (kind <= ODY_Q_NONE || kind > ODY_Q_MXFP4_OCP)
     return fail(ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(kind));
   if (sdt != DT_F32 && sdt != DT_BF16) return fail(ODY_ERR_DTYPE, "quantize source must be float32 or bfloat16");
   if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot quantize an empty tensor");
@@ -1849,7 +1850,7 @@ extern "C" int ody_quantize_on_stream(int32_t kind, const void* src, int32_t sdt
 
 extern "C" int ody_dequantize_on_stream(int32_t kind, const void* q, int64_t n, const float* tensor_scale,
                                         float* out, void* stream) {
-  if (kind <= ODY_Q_NONE || kind > ODY_Q_NVFP4_TENSOR)
+  if (kind <= ODY_Q_NONE || kind > ODY_Q_MXFP4_OCP)
     return fail(ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(kind));
   if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot dequantize an empty tensor");
   if (!q || !out) return fail(ODY_ERR_ARG, "null pointer");
@@ -1860,7 +1861,7 @@ extern "C" int ody_dequantize_on_stream(int32_t kind, const void* q, int64_t n, 
 }
 
 extern "C" int ody_dequantize(int32_t kind, const void* q, int64_t n, float ts, float* out) {
-  if (kind <= ODY_Q_NONE || kind > ODY_Q_NVFP4_TENSOR)
+  if (kind <= ODY_Q_NONE || kind > ODY_Q_MXFP4_OCP)
     return fail(ODY_ERR_ARG, "unknown quantisation kind " + std::to_string(kind));
   if (n <= 0) return fail(ODY_ERR_SHAPE, "cannot dequantize an empty tensor");
   if (!q || !out) return fail(ODY_ERR_ARG, "null pointer");

@@ -272,6 +272,58 @@ __device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, fl
   return er;
 }
 
+// ---- one MXFP4 block by the OCP MX v1.0 rule -----------------------------
+// Shared exponent X = floor(log2(max|x|)) - 2, clamped to [-127, 127],
+// stored as the E8M0 byte X + 127; elements x / 2^X (exact: a power of two)
+// converted by the hardware E2M1 conversion, round to nearest even with
+// saturation at +-6, sign kept.  A NaN or Inf element gives the NaN scale
+// byte 0xFF and zero codes; an all-zero block X = 0.
+__device__ __forceinline__ uint32_t cvt_e2m1x2(float hi, float lo) {
+  uint32_t d;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}"
+      : "=r"(d)
+      : "f"(hi), "f"(lo));
+  return d;
+}
+// OCP E2M1 value of a code (0, 0.5, 1, 1.5, 2, 3, 4, 6; bit 3 the sign)
+// times the block scale sf (exact: a power of two, or NaN)
+__device__ __forceinline__ float e2m1_ocp_decode(uint32_t code, float sf) {
+  const uint32_t m = code & 7u;
+  // twice the magnitude per code, as nibbles: 0, 1, 2, 3, 4, 6, 8, 12
+  const float mag = (float)((0xC8643210u >> (4 * m)) & 0xFu) * 0.5f;
+  const float v = __fmul_rn(mag, sf);
+  return (code & 8u) ? -v : v;
+}
+__device__ __forceinline__ uint32_t mx_ocp_encode_block(const float* x, uint32_t* w) {
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 32; k += 2) am = max3_nan(am, fabsf(x[k]), fabsf(x[k + 1]));
+  if (!(am <= 3.4028234664e38f)) {  // NaN or Inf
+#pragma unroll
+    for (int i = 0; i < 4; i++) w[i] = 0;
+    return 0xFF;
+  }
+  int X = 0;
+  if (am > 0.0f) {
+    const uint32_t b = __float_as_uint(am);
+    const int e = (int)(b >> 23);
+    // floor(log2 am): the exponent field, or for a subnormal the position of its top bit
+    const int fl = e != 0 ? e - 127 : (31 - __clz(b)) - 149;
+    X = min(max(fl - 2, -127), 127);
+  }
+  // 2^-X exactly (2^127 and the subnormal 2^-127 included)
+  const float r = X <= 126 ? __uint_as_float((uint32_t)(127 - X) << 23) : __uint_as_float(0x00400000u);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    uint32_t wd = 0;
+#pragma unroll
+    for (int k = 3; k >= 0; k--)
+      wd = wd * 256u + cvt_e2m1x2(__fmul_rn(x[8 * i + 2 * k], r), __fmul_rn(x[8 * i + 2 * k + 1], r));
+    w[i] = wd;
+  }
+  return (uint32_t)(X + 127);
+}
+
 // ---- one MXFP4 block (32 elements) --------------------------------------
 // Writes the 16 code bytes (w[0..3]) and returns the E8M0 scale byte.
 // lut_s: the signed table of load_ladder_signed

@@ -1325,7 +1325,7 @@ template <int KIND, int SDT>
 __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int64_t n, uint8_t* out,
                                                              int64_t out_bytes, const uint32_t* amax,
                                                              float* tscale) {
-  constexpr bool MX = KIND == Q_MXFP4;
+  constexpr bool MX = KIND == Q_MXFP4 || KIND == Q_MXFP4_OCP;
   constexpr bool TS = KIND == Q_NVFP4_TENSOR;
   constexpr int BE = MX ? 32 : 16;  // elements per block
   constexpr int BB = MX ? 17 : 9;   // bytes per block
@@ -1359,7 +1359,7 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_kernel(const void* x, int6
     uint32_t cw[BE / 8];
     uint32_t sb;
     if (MX)
-      sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
+      sb = KIND == Q_MXFP4_OCP ? mx_ocp_encode_block(v, cw) : mx_encode_block(v, g_thr_mx, s_lut, cw);
     else
       sb = nv_encode_block<TS>(v, st, rst, st_fast, sign_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
     stage_blocks<BE / 8>(ws, cw, sb);
@@ -1383,8 +1383,8 @@ struct Fp4Stages {
 
 template <int KIND, int SDT>
 struct Fp4Pipe {
-  static constexpr int BE = KIND == Q_MXFP4 ? 32 : 16;
-  static constexpr int BB = KIND == Q_MXFP4 ? 17 : 9;
+  static constexpr int BE = (KIND == Q_MXFP4 || KIND == Q_MXFP4_OCP) ? 32 : 16;
+  static constexpr int BB = (KIND == Q_MXFP4 || KIND == Q_MXFP4_OCP) ? 17 : 9;
   static constexpr int ESZ = SDT == DT_F32 ? 4 : 2;
   static constexpr int P = BE * ESZ / 16;  // 16-byte slots per block
   static constexpr int SEG = 32 * P * 16;  // input bytes per warp segment
@@ -1398,7 +1398,7 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
                                                                   int64_t out_bytes, const uint32_t* amax,
                                                                   float* tscale) {
   using PP = Fp4Pipe<KIND, SDT>;
-  constexpr bool MX = KIND == Q_MXFP4;
+  constexpr bool MX = KIND == Q_MXFP4 || KIND == Q_MXFP4_OCP;
   constexpr bool TS = KIND == Q_NVFP4_TENSOR;
   constexpr int NS = PP::NS;
   extern __shared__ __align__(128) uint8_t dsm[];
@@ -1492,7 +1492,7 @@ __global__ void __launch_bounds__(kThreads) quant_fp4_pipe_kernel(const void* x,
       uint32_t cw[PP::BE / 8];
       uint32_t sb;
       if (MX)
-        sb = mx_encode_block(v, g_thr_mx, s_lut, cw);
+        sb = KIND == Q_MXFP4_OCP ? mx_ocp_encode_block(v, cw) : mx_encode_block(v, g_thr_mx, s_lut, cw);
       else
         sb = nv_encode_block<TS>(v, st, rst, st_fast, sign_fast, s_t0, g_nv_const, g_thr_nv, s_lut, cw);
       stage_blocks<PP::BE / 8>(ws, cw, sb);
@@ -1557,6 +1557,7 @@ static int64_t quant_bytes_dev(int kind, int64_t n) {
     case Q_FP8_E4M3_TENSOR:
       return n;
     case Q_MXFP4:
+    case Q_MXFP4_OCP:
       return ((n + 31) / 32) * 17;
     case Q_NVFP4:
     case Q_NVFP4_TENSOR:
@@ -1567,8 +1568,8 @@ static int64_t quant_bytes_dev(int kind, int64_t n) {
 
 cudaError_t launch_quantize(int kind, int sdt, const void* x, int64_t n, uint8_t* out,
                             const uint32_t* amax, float* tscale, cudaStream_t st) {
-  if (kind == Q_MXFP4 || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
-    const int64_t be = kind == Q_MXFP4 ? 32 : 16;
+  if (kind == Q_MXFP4 || kind == Q_MXFP4_OCP || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
+    const int64_t be = (kind == Q_MXFP4 || kind == Q_MXFP4_OCP) ? 32 : 16;
     const int64_t warps = ((n + be - 1) / be + 31) / 32;
     const int64_t want = (warps + kThreads / 32 - 1) / (kThreads / 32);
     const int64_t cap = (int64_t)sm_count() * 4;
@@ -1579,11 +1580,13 @@ cudaError_t launch_quantize(int kind, int sdt, const void* x, int64_t n, uint8_t
   if (kind == K)                                                                          \
     return sdt == DT_F32 ? launch_fp4_pipe<K, DT_F32>(x, n, out, ob, amax, tscale, st)    \
                          : launch_fp4_pipe<K, DT_BF16>(x, n, out, ob, amax, tscale, st);
-      ODY_P(Q_MXFP4) ODY_P(Q_NVFP4) ODY_P(Q_NVFP4_TENSOR)
+      ODY_P(Q_MXFP4) ODY_P(Q_MXFP4_OCP) ODY_P(Q_NVFP4) ODY_P(Q_NVFP4_TENSOR)
 #undef ODY_P
     }
     if (kind == Q_MXFP4)
       launch_fp4_kind<Q_MXFP4>(sdt, x, n, out, ob, amax, tscale, grid, st);
+    else if (kind == Q_MXFP4_OCP)
+      launch_fp4_kind<Q_MXFP4_OCP>(sdt, x, n, out, ob, amax, tscale, grid, st);
     else if (kind == Q_NVFP4)
       launch_fp4_kind<Q_NVFP4>(sdt, x, n, out, ob, amax, tscale, grid, st);
     else
@@ -1609,13 +1612,27 @@ __global__ void __launch_bounds__(kThreads) dequantize_kernel(int kind, const ui
   for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
     const int64_t e0 = t * kTile + (int64_t)threadIdx.x * kVec;
     float v[8];
-    if (kind == Q_MXFP4 || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
-      const int tb = kind == Q_MXFP4 ? kMxTileBytes : kNvTileBytes;
+    const bool mx = kind == Q_MXFP4 || kind == Q_MXFP4_OCP;
+    if (mx || kind == Q_NVFP4 || kind == Q_NVFP4_TENSOR) {
+      const int tb = mx ? kMxTileBytes : kNvTileBytes;
       const int64_t off = t * tb;
       const int64_t lim = qbytes - off < tb ? qbytes - off : tb;
       for (int i = threadIdx.x; i < lim; i += blockDim.x) stage[i] = q[off + i];
       __syncthreads();
-      if (kind == Q_MXFP4) {
+      if (kind == Q_MXFP4_OCP) {
+        // OCP MX decode: the E2M1 value (0.5 included) times 2^(byte - 127); 0xFF is NaN
+        const int blk = threadIdx.x >> 2, j = threadIdx.x & 3;
+        const uint8_t sbyte = (blk * 17 + 16 < lim) ? stage[blk * 17 + 16] : 127;
+        const float sf = sbyte == 0xFF ? __uint_as_float(0x7fc00000u)
+                                       : (sbyte >= 1 ? __uint_as_float((uint32_t)sbyte << 23)
+                                                     : __uint_as_float(0x00400000u));
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const uint8_t b = (blk * 17 + 4 * j + i < lim) ? stage[blk * 17 + 4 * j + i] : 0;
+          v[2 * i] = e2m1_ocp_decode(b >> 4, sf);
+          v[2 * i + 1] = e2m1_ocp_decode(b & 15, sf);
+        }
+      } else if (kind == Q_MXFP4) {
         const int blk = threadIdx.x >> 2, j = threadIdx.x & 3;
         const float sf = (blk * 17 + 16 < lim) ? e8m0_to_f32(stage[blk * 17 + 16]) : 0.0f;
 #pragma unroll

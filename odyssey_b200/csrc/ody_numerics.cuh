@@ -26,7 +26,8 @@ enum : int {
   Q_FP8_E4M3_TENSOR = 5,
   Q_MXFP4 = 6,
   Q_NVFP4 = 7,
-  Q_NVFP4_TENSOR = 8
+  Q_NVFP4_TENSOR = 8,
+  Q_MXFP4_OCP = 9
 };
 
 // Optimizer constants, each a Float64 hyper-parameter rounded once to

@@ -96,6 +96,14 @@ def to_mxfp4(x, dtype=None):
     return quantize(_reference_source(x, dtype, "to_mxfp4()"), L.Q_MXFP4, dtype)
 
 
+def to_mxfp4_ocp(x, dtype=None):
+    """MXFP4 by the OCP Microscaling Formats v1.0 rule (extension, no
+    reference counterpart): E8M0 = floor(log2 amax) - 2 per 32-element
+    block, elements rounded to nearest even on the E2M1 grid.  float32 or
+    bfloat16 sources; decode with dequantize(q, ...) or from_mxfp4_ocp."""
+    return quantize(x, L.Q_MXFP4_OCP, dtype)
+
+
 def to_nvfp4(x, dtype=None):
     """AnyTensor.to_nvfp4 (any_tensor.mojo:2329-2401): float16/32/64 sources;
     bfloat16 through quantize() or to_nvfp4_tensor_scaled (extensions)."""

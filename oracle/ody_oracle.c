@@ -389,6 +389,7 @@ int64_t ora_quant_bytes(int kind, int64_t n) {
     case ORA_Q_FP8_E4M3_TENSOR:
       return n;
     case ORA_Q_MXFP4:
+    case ORA_Q_MXFP4_OCP:
       return ((n + 31) / 32) * 17;
     case ORA_Q_NVFP4:
     case ORA_Q_NVFP4_TENSOR:
@@ -416,6 +417,74 @@ static float tensor_scale(float amax, float denom) {
   float s = amax / denom;
   if (!(s > 0.0f) || isinf(s)) s = 1.0f;
   return s;
+}
+
+/* ------------------------------------------------------------------------ */
+/* MXFP4 by the OCP Microscaling Formats (MX) v1.0 rule (not the reference's */
+/* mxfp4.mojo rule; BASELINE configs[1] names it).  Per 32-element block:    */
+/* shared exponent X = floor(log2(max|x|)) - 2 (2 = the largest E2M1         */
+/* exponent), clamped to [-127, 127], stored as the E8M0 byte X + 127; each  */
+/* element is x / 2^X rounded to nearest-even on the E2M1 grid {0, 0.5, 1,   */
+/* 1.5, 2, 3, 4, 6} and saturated at 6, keeping the sign of x (so -0 codes  */
+/* 0x8).  A block with a NaN or Inf element gets the NaN scale byte 0xFF and */
+/* zero codes (this build's choice; the spec leaves it open).  All-zero      */
+/* blocks take X = 0.                                                        */
+/* ------------------------------------------------------------------------ */
+static uint8_t e2m1_rne(float q) {
+  float a = q < 0 || (q == 0 && signbit(q)) ? -q : q;
+  uint8_t c;
+  if (a <= 0.25f) c = 0;
+  else if (a < 0.75f) c = 1;
+  else if (a <= 1.25f) c = 2;
+  else if (a < 1.75f) c = 3;
+  else if (a <= 2.5f) c = 4;
+  else if (a < 3.5f) c = 5;
+  else if (a <= 5.0f) c = 6;
+  else c = 7;
+  return (uint8_t)((signbit(q) ? 8 : 0) | c);
+}
+
+static void mxfp4_ocp_block_encode(const float v[32], uint8_t* blk) {
+  float am = 0.0f;
+  int bad = 0;
+  for (int i = 0; i < 32; i++) {
+    if (isnan(v[i]) || isinf(v[i])) bad = 1;
+    float a = fabsf(v[i]);
+    if (a > am) am = a;
+  }
+  if (bad) {
+    memset(blk, 0, 16);
+    blk[16] = 0xFF;
+    return;
+  }
+  int X = 0;
+  if (am > 0.0f) {
+    int e;
+    frexpf(am, &e); /* am = f * 2^e, f in [0.5, 1): floor(log2 am) = e - 1 */
+    X = (e - 1) - 2;
+    if (X < -127) X = -127;
+    if (X > 127) X = 127;
+  }
+  const float r = ldexpf(1.0f, -X);
+  for (int i = 0; i < 16; i++) {
+    uint8_t hi = e2m1_rne(v[2 * i] * r), lo = e2m1_rne(v[2 * i + 1] * r);
+    blk[i] = (uint8_t)((hi << 4) | lo);
+  }
+  blk[16] = (uint8_t)(X + 127);
+}
+
+static void mxfp4_ocp_block_decode(const uint8_t* blk, float v[32]) {
+  static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  if (blk[16] == 0xFF) {
+    for (int i = 0; i < 32; i++) v[i] = NAN;
+    return;
+  }
+  const float s = ldexpf(1.0f, (int)blk[16] - 127);
+  for (int i = 0; i < 32; i++) {
+    uint8_t c = (i & 1) ? (blk[i / 2] & 15) : (blk[i / 2] >> 4);
+    float m = mag[c & 7] * s;
+    v[i] = (c & 8) ? -m : m;
+  }
 }
 
 float ora_quantize(int kind, const float* x, int64_t n, uint8_t* out) {
@@ -457,6 +526,19 @@ float ora_quantize(int kind, const float* x, int64_t n, uint8_t* out) {
           v[i] = k < n ? x[k] : 0.0f; /* tensor_dtype_conv.mojo:306-307 */
         }
         ora_mxfp4_block_encode(v, out + b * 17);
+      }
+      break;
+    }
+    case ORA_Q_MXFP4_OCP: {
+      int64_t nb = (n + 31) / 32;
+#pragma omp parallel for num_threads(ORA_NT) schedule(static)
+      for (int64_t b = 0; b < nb; b++) {
+        float v[32];
+        for (int i = 0; i < 32; i++) {
+          int64_t k = b * 32 + i;
+          v[i] = k < n ? x[k] : 0.0f;
+        }
+        mxfp4_ocp_block_encode(v, out + b * 17);
       }
       break;
     }
@@ -517,6 +599,16 @@ void ora_dequantize(int kind, const uint8_t* q, int64_t n, float ts, float* out)
       for (int64_t b = 0; b < nb; b++) {
         float v[32];
         ora_mxfp4_block_decode(q + b * 17, v);
+        for (int i = 0; i < 32 && b * 32 + i < n; i++) out[b * 32 + i] = v[i];
+      }
+      break;
+    }
+    case ORA_Q_MXFP4_OCP: {
+      int64_t nb = (n + 31) / 32;
+#pragma omp parallel for num_threads(ORA_NT) schedule(static)
+      for (int64_t b = 0; b < nb; b++) {
+        float v[32];
+        mxfp4_ocp_block_decode(q + b * 17, v);
         for (int i = 0; i < 32 && b * 32 + i < n; i++) out[b * 32 + i] = v[i];
       }
       break;

@@ -45,7 +45,8 @@ enum {
   ORA_Q_FP8_E4M3_TENSOR = 5, /* e4m3(w / s), s = amax/448             */
   ORA_Q_MXFP4 = 6,           /* AnyTensor.to_mxfp4()                  */
   ORA_Q_NVFP4 = 7,           /* AnyTensor.to_nvfp4()                  */
-  ORA_Q_NVFP4_TENSOR = 8     /* to_nvfp4(w / s_t), s_t = amax/2688    */
+  ORA_Q_NVFP4_TENSOR = 8,    /* to_nvfp4(w / s_t), s_t = amax/2688    */
+  ORA_Q_MXFP4_OCP = 9        /* OCP MX rule: X = floor(log2 amax) - 2, RNE */
 };
 
 /* ---- scalar casts ------------------------------------------------------ */

@@ -17,7 +17,8 @@ _lib = None
 
 F32, F16, BF16 = 0, 1, 2
 SGD, ADAM, ADAMW, LION, RMSPROP, ADAGRAD = 0, 1, 2, 3, 4, 5
-Q_NONE, Q_FP16, Q_BF16, Q_FP8_E4M3, Q_FP8_E5M2, Q_FP8_E4M3_TENSOR, Q_MXFP4, Q_NVFP4, Q_NVFP4_TENSOR = range(9)
+(Q_NONE, Q_FP16, Q_BF16, Q_FP8_E4M3, Q_FP8_E5M2, Q_FP8_E4M3_TENSOR, Q_MXFP4, Q_NVFP4, Q_NVFP4_TENSOR,
+ Q_MXFP4_OCP) = range(10)
 
 _p = C.c_void_p
 _i64 = C.c_int64

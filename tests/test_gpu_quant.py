@@ -8,7 +8,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-KINDS = [1, 2, 3, 4, 5, 6, 7, 8]  # FP16 .. NVFP4_TENSOR
+KINDS = [1, 2, 3, 4, 5, 6, 7, 8, 9]  # FP16 .. NVFP4_TENSOR, MXFP4 by the OCP MX rule
 
 
 @pytest.fixture(scope="module")
@@ -170,6 +170,32 @@ def test_fp4_encode_break_points_every_scale(ody, oracle, kind):
         want, wts = oracle.quantize(kind, x)
         np.testing.assert_array_equal(got, want, err_msg=f"mult {mult} tiny {tiny}")
         assert np.float32(ts) == np.float32(wts)
+
+
+def test_mxfp4_ocp_rounding_every_scale(ody, oracle):
+    """MXFP4 by the OCP MX rule (hardware E2M1 conversion, round to nearest
+    even, saturating) against the oracle at every rounding midpoint of the
+    E2M1 grid +-4 ulps, shared exponents 2^-130..2^125, both signs, signed
+    zeros, and blocks whose amax sits exactly on a power of two."""
+    rng = np.random.default_rng(5)
+    mids = np.float32([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 0.5, 1.0, 4.0])
+    blocks = []
+    for X in range(-130, 126, 3):
+        sc = np.float32(2.0 ** X)
+        pts = _ulp_sweep(mids * sc, 4) if sc * 0.25 > 1e-37 else np.float32(mids * sc)
+        pts = pts * np.where(rng.random(pts.size) < 0.5, np.float32(-1), np.float32(1))
+        for i in range(0, pts.size, 31):
+            blk = np.zeros(32, np.float32)
+            chunk = pts[i:i + 31]
+            blk[1:1 + chunk.size] = chunk
+            blk[0] = np.float32(4.0) * sc  # amax exactly 2^(X+2): shared exponent X
+            if i % 2:
+                blk[31] = np.float32(-0.0)
+            blocks.append(blk)
+    x = np.concatenate(blocks)
+    got, _ = _gpu_quant(ody, 9, x)
+    want, _ = oracle.quantize(9, x)
+    np.testing.assert_array_equal(got, want)
 
 
 @pytest.mark.parametrize("kind", KINDS)

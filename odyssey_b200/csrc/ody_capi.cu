@@ -1009,6 +1009,11 @@ extern "C" int ody_ctx_set_grad_double_buffer(ody_ctx* c, int32_t enable) {
   if (c->pending) return ctx_fail(c, ODY_ERR_STATE, "a step is in flight");
   if (c->dp_on) return ctx_fail(c, ODY_ERR_STATE, "double-buffered gradients do not combine with data-parallel gradients");
   ODY_CUDA(cudaSetDevice(c->cfg.device));
+  if (c->gexec && enable != (int32_t)c->dbuf) {
+    // a captured step names the old gradient arena: capture again later
+    ODY_CUDA(cudaStreamSynchronize(c->stream));
+    drop_graph(c);
+  }
   if (!enable) {
     if (!c->dbuf) return ODY_OK;
     ODY_CUDA(cudaStreamSynchronize(c->copy_stream));

@@ -444,13 +444,25 @@ def test_double_buffered_gradients(oracle, graph):
     for i, m in enumerate(wl.master(0)):
         ctx.set_master(i, m)
         model.master[i][:] = m
+    t = to = 1
+    if graph:
+        # two captured-graph steps first, so that a graph naming the single
+        # arena exists when double-buffering starts (it must not be replayed)
+        for s0 in (100, 101):
+            g0 = wl.grads(s0)
+            for i, g in enumerate(g0):
+                ctx.set_grad(i, g)
+            r = ctx.step(t)
+            ro = model.step(g0, to)
+            assert r["clip_coef"] == ro.coef
+            t += 1
+            to += 1
     ctx.set_grad_double_buffer(True)
     nsteps = 7
     grads = [wl.grads(s) for s in range(nsteps + 1)]
     kept = []  # the host arrays must outlive their async copies
     for i, g in enumerate(grads[0]):
         kept.append(ctx.set_grad(i, g, sync=False))
-    t = to = 1
     for s in range(nsteps):
         ctx.step_async(t)
         for i, g in enumerate(grads[s + 1]):
@@ -467,6 +479,19 @@ def test_double_buffered_gradients(oracle, graph):
     r = ctx.step(t)
     ro = model.step(grads[nsteps], to)
     assert r["skipped"] == ro.skipped and r["clip_coef"] == ro.coef
+    if not r["skipped"]:
+        t += 1
+        to += 1
+    # and single-arena steps afterwards (in graph mode: a fresh capture)
+    for s0 in (200, 201):
+        g0 = wl.grads(s0)
+        for i, g in enumerate(g0):
+            ctx.set_grad(i, g)
+        r = ctx.step(t)
+        ro = model.step(g0, to)
+        assert r["skipped"] == ro.skipped and r["clip_coef"] == ro.coef
+        t += 1
+        to += 1
     compare_state(ctx, model, wl.numels, [wl.quant] * len(wl.numels), wl.optimizer)
     ctx.close()
 

@@ -211,7 +211,8 @@ int ody_ctx_pass_times(ody_ctx* ctx, double* ms_out, int64_t* steps_out);
  * replay it with one graph launch, updating only the optimizer constants of
  * step t.  Host launch overhead per step drops to one graph launch, which is
  * what bounds small models (LeNet: 61,706 params).  Ignored while per-pass
- * timing is on, and with world_size > 1 (the NCCL exchange stays eager).
+ * timing is on, while gradients are double-buffered, and with world_size > 1
+ * (the NCCL exchange stays eager).
  * The reference has no equivalent (its step is a CPU call); results are
  * identical to the eager path. */
 int ody_ctx_set_graph(ody_ctx* ctx, int32_t enable);

@@ -71,7 +71,7 @@ FALLBACK_HBM_GBS = 6650.0
 # (dram__bytes_read.sum + dram__bytes_write.sum of the 8-tensor case
 # `--tensors 8`, divided by its 134,217,728 params; traffic grows with the
 # params a launch processes)
-TRAFFIC_BYTES_PER_PARAM_APPLY = 30.51
+TRAFFIC_BYTES_PER_PARAM_APPLY = 30.48
 
 
 def env_int(k, d):

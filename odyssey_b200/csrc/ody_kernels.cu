@@ -652,30 +652,56 @@ __device__ __forceinline__ uint32_t fp4_encode_plain(float x, const float* t) {
   return ((uint32_t)((x < 0.0f) && (a >= t[0])) << 3) | mag;
 }
 
+// One lane's 8 elements of a warp's slice (lane pairs form an NVFP4 block,
+// lane quads an MXFP4 block): the block scale from the shuffled amax, then
+// the codes by the exact-quotient table lookup of ody_fp4fast.cuh (MXFP4:
+// x * 2^-k with the sign in the table; NVFP4: the Markstein quotient and the
+// t0 sign rule), or by the threshold compares where that range does not
+// hold, or by the reference's special cases for non-finite elements and a
+// zero scale.
 template <bool MX>
-__device__ __forceinline__ void stage_fp4(const float v[8], uint8_t* ws, const Fp4Thr* thr) {
+__device__ __forceinline__ void stage_fp4(const float v[8], uint8_t* ws, const Fp4Thr* thr, const uint8_t* lut) {
   float am = 0.0f;
 #pragma unroll
   for (int k = 0; k < 8; k++) am = amax_acc(am, v[k]);
   am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
   if (MX) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
   const uint8_t e = MX ? e8m0_from_f32(block_scale_value_fast(am)) : e4m3_scale_from_f32(block_scale_value_fast(am));
-  float t[8];
-  thr_load(&thr[e], t);
   const bool z = !MX && e == 0;
   const bool special = z || (MX && e == 255) || any_nonfinite8(v);
   const int lane = threadIdx.x & 31;
   const int blk = MX ? (lane >> 2) : (lane >> 1), j = MX ? (lane & 3) : (lane & 1);
   const int bb = MX ? 17 : 9;
   uint8_t* dst = ws + blk * bb + 4 * j;
-  if (!special) {
+  if (!special && (MX ? e >= 1 : am <= 0x1p120f)) {
+    float q[8];
+    uint32_t w;
+    if (MX) {
+      // 1 / 2^(e-127) exactly (2^-127 is subnormal)
+      const float r = e <= 253 ? __uint_as_float((254u - e) << 23) : __uint_as_float(0x00400000u);
 #pragma unroll
-    for (int i = 0; i < 4; i++)
-      dst[i] = (uint8_t)((fp4_encode_plain(v[2 * i], t) << 4) | fp4_encode_plain(v[2 * i + 1], t));
+      for (int k = 0; k < 8; k++) q[k] = __fadd_rn(__fmul_rn(v[k], r), 0.0f);
+      w = fp4_word_signed(q, lut);
+    } else {
+      const NvScaleConst cst = g_nv_const[e];
+#pragma unroll
+      for (int k = 0; k < 8; k++) q[k] = div_mk(fabsf(v[k]), cst.scale, cst.rcp);
+      w = fp4_word(q, v, -cst.t0, lut);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) dst[i] = (uint8_t)(w >> (8 * i));
   } else {
+    float t[8];
+    thr_load(&thr[e], t);
+    if (!special) {
 #pragma unroll
-    for (int i = 0; i < 4; i++)
-      dst[i] = (uint8_t)((fp4_encode(v[2 * i], t, z) << 4) | fp4_encode(v[2 * i + 1], t, z));
+      for (int i = 0; i < 4; i++)
+        dst[i] = (uint8_t)((fp4_encode_plain(v[2 * i], t) << 4) | fp4_encode_plain(v[2 * i + 1], t));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        dst[i] = (uint8_t)((fp4_encode(v[2 * i], t, z) << 4) | fp4_encode(v[2 * i + 1], t, z));
+    }
   }
   if (j == (MX ? 3 : 1)) ws[blk * bb + bb - 1] = e;
 }
@@ -816,7 +842,8 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
 
 template <int GDT, int OPT>
 __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch, const Divisor& dv, bool clipped,
-                                             float coef, const Fp4Thr* s_mx, const Fp4Thr* s_nv, uint8_t* stage) {
+                                             float coef, const Fp4Thr* s_mx, const Fp4Thr* s_nv, const uint8_t* s_lut,
+                                             uint8_t* stage) {
   const OptConsts& oc = a.oc;
   const TensorDesc td = a.tensors[ch.tensor];
   const int kind = td.quant;
@@ -890,11 +917,11 @@ __device__ __forceinline__ void update_chunk(const ApplyArgs& a, const Chunk& ch
         const int w = threadIdx.x >> 5;
         uint8_t* ws = stage + w * kWarpStage;
         if (kind == Q_MXFP4) {
-          stage_fp4<true>(p, ws, s_mx);
+          stage_fp4<true>(p, ws, s_mx, s_lut);
           __syncwarp();
           flush_warp<true>(ws, a.qout + td.qoff + tile_in_tensor * kMxTileBytes + w * kMxWarpBytes, kMxWarpBytes);
         } else {
-          stage_fp4<false>(p, ws, s_nv);
+          stage_fp4<false>(p, ws, s_nv, s_lut);
           __syncwarp();
           flush_warp<false>(ws, a.qout + td.qoff + tile_in_tensor * kNvTileBytes + w * kNvWarpBytes, kNvWarpBytes);
         }
@@ -1046,7 +1073,7 @@ __global__ void __launch_bounds__(kThreads, 4) apply_kernel(ApplyArgs a) {
     if (job & kRequantJob)
       requant_chunk(a, ch, s_nv, s_t0, &s_t0_tensor, s_lut, stage);
     else
-      update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, stage);
+      update_chunk<GDT, OPT>(a, ch, dv, clipped, coef, s_mx, s_nv, s_lut, stage);
     __syncthreads();
     if (threadIdx.x == 0) s_next = nxt;
     __syncthreads();

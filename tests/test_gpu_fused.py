@@ -261,12 +261,14 @@ def _wide_master(rng, n, lo_exp, hi_exp, zeros=0.02, specials=()):
     return x
 
 
-def test_nvfp4_tensor_scale_sweep(oracle):
-    """NVFP4 with a per-tensor scale over tensors whose scales span the float
-    range (subnormal to huge amax, wide in-tensor spread, signed zeros, NaN
-    and Inf elements): the raw-master encode with composite thresholds
-    against the oracle's element-by-element division, bit for bit.  SGD with
-    lr 0 keeps the masters as written."""
+@pytest.mark.parametrize("quant", ["nvfp4_tensor", "nvfp4", "mxfp4"])
+def test_nvfp4_tensor_scale_sweep(oracle, quant):
+    """FP4 requant of tensors whose scales span the float range (subnormal to
+    huge amax, wide in-tensor spread, signed zeros, NaN and Inf elements)
+    against the oracle's element-by-element division, bit for bit: NVFP4
+    with a per-tensor scale (the requant jobs), and plain NVFP4 / MXFP4
+    (encoded inside the update jobs).  SGD with lr 0 keeps the masters as
+    written."""
     from odyssey_b200 import MixedPrecisionStep
     rng = np.random.Generator(np.random.PCG64(77))
     ranges = [(-149, -126), (-140, -100), (-60, -20), (-30, 0), (-8, -2), (-2, 2), (0, 30), (20, 60),
@@ -279,9 +281,9 @@ def test_nvfp4_tensor_scale_sweep(oracle):
     masters.append(_wide_master(rng, 3000, -10, 0, specials=[np.float32(3.4e38), -0.0]))
     masters.append(np.zeros(100, np.float32))
     numels = [m.size for m in masters]
-    ctx = MixedPrecisionStep(numels, grad_dtype="float32", quant="nvfp4_tensor", optimizer="sgd",
+    ctx = MixedPrecisionStep(numels, grad_dtype="float32", quant=quant, optimizer="sgd",
                              learning_rate=0.0, momentum=0.0, weight_decay=0.0, use_gradient_scaler=False)
-    specs = [{"numel": n, "grad_dtype": 0, "quant": QK["nvfp4_tensor"]} for n in numels]
+    specs = [{"numel": n, "grad_dtype": 0, "quant": QK[quant]} for n in numels]
     model = oracle.Model(specs, OPT["sgd"], 0.0, use_scaler=False, scaler_kwargs={"initial_scale": 1.0})
     for i, m in enumerate(masters):
         ctx.set_master(i, m)
@@ -294,8 +296,9 @@ def test_nvfp4_tensor_scale_sweep(oracle):
     for i in range(len(numels)):
         q = ctx.get_quant(i)
         np.testing.assert_array_equal(q.data, model.qout[i][:q.data.size], err_msg=f"tensor {i} {ranges[i:i+1]}")
-        assert np.float32(q.tensor_scale) == model.qscale[i][0] or (
-            np.isnan(q.tensor_scale) and np.isnan(model.qscale[i][0])), i
+        if quant == "nvfp4_tensor":
+            assert np.float32(q.tensor_scale) == model.qscale[i][0] or (
+                np.isnan(q.tensor_scale) and np.isnan(model.qscale[i][0])), i
     ctx.close()
 
 

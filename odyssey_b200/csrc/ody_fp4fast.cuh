@@ -93,6 +93,30 @@ __device__ __forceinline__ float div_mk(float x, float s, float r) {
   return __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
 }
 
+// Two quotients at once on the paired FP32 pipe (sm_100 FFMA2 / FMUL2,
+// round to nearest, no flush to zero): the same operations as div_mk
+// element by element, with -q0 * s written q0 * (-s), which rounds the same.
+__device__ __forceinline__ float2 div_mk2(float2 x, float2 ns, float2 r) {
+  const float2 q0 = __fmul2_rn(x, r);
+  return __ffma2_rn(__ffma2_rn(q0, ns, x), r, q0);
+}
+
+// q[k] = div_mk(div_mk(x[k], st, rst), bs, rbs) for N (even) elements,
+// |x[k]| when ABS
+template <int N, bool TWO, bool ABS>
+__device__ __forceinline__ void div_mk_n(const float* x, float st, float rst, float bs, float rbs, float* q) {
+  const float2 nst = make_float2(-st, -st), rst2 = make_float2(rst, rst);
+  const float2 nbs = make_float2(-bs, -bs), rbs2 = make_float2(rbs, rbs);
+#pragma unroll
+  for (int k = 0; k < N; k += 2) {
+    float2 v = ABS ? make_float2(fabsf(x[k]), fabsf(x[k + 1])) : make_float2(x[k], x[k + 1]);
+    if (TWO) v = div_mk2(v, nst, rst2);
+    v = div_mk2(v, nbs, rbs2);
+    q[k] = v.x;
+    q[k + 1] = v.y;
+  }
+}
+
 // Ladder index of a quotient q >= 0 (NaN and +Inf included): the ladder is
 // constant on each bucket bits(q) >> 21 (its break points are the buckets
 // 0x1F8, 0x1FD, 0x1FF, 0x201, 0x203, 0x205), so clamping the bucket to
@@ -242,16 +266,14 @@ __device__ __forceinline__ uint32_t nv_encode_block(const float* x, float st, fl
     const float bs = c.scale;
     if (TS && sign_fast) {
       float q[16];
-#pragma unroll
-      for (int k = 0; k < 16; k++) q[k] = div_mk(div_mk(x[k], st, rst), bs, c.rcp);  // +-0 give +0
+      div_mk_n<16, true, false>(x, st, rst, bs, c.rcp, q);  // +-0 give +0
       w[0] = fp4_word_signed(q, lut);
       w[1] = fp4_word_signed(q + 8, lut);
       return e;
     }
     const float neg_t0 = -(TS ? t0_ts[e] : c.t0);
     float q[16];
-#pragma unroll
-    for (int k = 0; k < 16; k++) q[k] = div_mk(TS ? div_mk(fabsf(x[k]), st, rst) : fabsf(x[k]), bs, c.rcp);
+    div_mk_n<16, TS, true>(x, st, rst, bs, c.rcp, q);
     w[0] = fp4_word(q, x, neg_t0, lut);
     w[1] = fp4_word(q + 8, x + 8, neg_t0, lut);
     return e;
@@ -337,8 +359,15 @@ __device__ __forceinline__ uint32_t mx_encode_block(const float* x, const Fp4Thr
     // 1 / 2^(e-127) exactly (2^-127 is subnormal)
     const float r = e <= 253 ? __uint_as_float((254u - e) << 23) : __uint_as_float(0x00400000u);
     float q[32];
+    // the products paired; "+ 0" (-0 to +0) stays scalar, as the paired
+    // add of a constant zero may be folded away
+    const float2 r2 = make_float2(r, r);
 #pragma unroll
-    for (int k = 0; k < 32; k++) q[k] = __fadd_rn(__fmul_rn(x[k], r), 0.0f);
+    for (int k = 0; k < 32; k += 2) {
+      const float2 v = __fmul2_rn(make_float2(x[k], x[k + 1]), r2);
+      q[k] = __fadd_rn(v.x, 0.0f);
+      q[k + 1] = __fadd_rn(v.y, 0.0f);
+    }
 #pragma unroll
     for (int i = 0; i < 4; i++) w[i] = fp4_word_signed(q + 8 * i, lut_s);
     return e;

@@ -679,13 +679,18 @@ __device__ __forceinline__ void stage_fp4(const float v[8], uint8_t* ws, const F
     if (MX) {
       // 1 / 2^(e-127) exactly (2^-127 is subnormal)
       const float r = e <= 253 ? __uint_as_float((254u - e) << 23) : __uint_as_float(0x00400000u);
+      // products paired, "+ 0" scalar (see mx_encode_block)
+      const float2 r2 = make_float2(r, r);
 #pragma unroll
-      for (int k = 0; k < 8; k++) q[k] = __fadd_rn(__fmul_rn(v[k], r), 0.0f);
+      for (int k = 0; k < 8; k += 2) {
+        const float2 y = __fmul2_rn(make_float2(v[k], v[k + 1]), r2);
+        q[k] = __fadd_rn(y.x, 0.0f);
+        q[k + 1] = __fadd_rn(y.y, 0.0f);
+      }
       w = fp4_word_signed(q, lut);
     } else {
       const NvScaleConst cst = g_nv_const[e];
-#pragma unroll
-      for (int k = 0; k < 8; k++) q[k] = div_mk(fabsf(v[k]), cst.scale, cst.rcp);
+      div_mk_n<8, false, true>(v, 0.0f, 0.0f, cst.scale, cst.rcp, q);
       w = fp4_word(q, v, -cst.t0, lut);
     }
 #pragma unroll
